@@ -1,0 +1,531 @@
+// SPDX-License-Identifier: MIT
+//
+// The C ABI of libdbs_cuda (include/dbs_cuda.h): argument checks, workspace
+// layout, launches. Every entry point is asynchronous on the caller's stream
+// except where the header says it synchronizes.
+#include <atomic>
+#include <cmath>
+#include <cstdlib>
+#include <cstring>
+#include <limits>
+#include <mutex>
+
+#include "dbs_cuda.h"
+#include "dbs_cuda_b200.h"
+#include "engine.cuh"
+
+namespace dbsb {
+
+// decode.cu / backward.cu
+cudaError_t launch_decode(const DecodeParams& p, int dtype, bool logits, cudaStream_t stream, int sm_count);
+cudaError_t launch_init(const DecodeParams& p, cudaStream_t stream);
+cudaError_t launch_validate(const DecodeParams& p, int* status, cudaStream_t stream);
+int decode_list_len(int K);
+size_t decode_select_smem(int K);
+
+
+cudaError_t launch_backward(const BackwardParams& p, cudaStream_t stream);
+cudaError_t launch_logit_correction(const BackwardParams& p, int dtype, const void* logits, const float* row_lse,
+                                    cudaStream_t stream);
+cudaError_t launch_length_penalty(const int32_t* lengths, int64_t count, float alpha, float* out, cudaStream_t stream);
+cudaError_t launch_backtrack(int B, int T, int K, const int32_t* tokens, const int32_t* parents,
+                             const int32_t* steps_pe, int64_t* out, cudaStream_t stream);
+
+namespace {
+
+constexpr int64_t kAlign = 256;
+constexpr unsigned long long kTimeoutNs = 20ull * 1000ull * 1000ull * 1000ull;  // bounded inter-CTA waits
+constexpr int kMaxRowSmem = 160 * 1024;  // largest row staged in shared memory
+
+std::atomic<int> g_sync{0};
+
+int64_t align_up(int64_t n) { return (n + kAlign - 1) / kAlign * kAlign; }
+
+bool sync_requested() {
+    if (g_sync.load(std::memory_order_relaxed)) return true;
+    const char* a = std::getenv("DBS_CUDA_SYNC_CHECK");
+    const char* b = std::getenv("DBS_CUDA_DEBUG_SYNC");
+    return (a && a[0] == '1') || (b && b[0] == '1');
+}
+
+int elem_bytes(int dtype) { return dtype == DBS_CUDA_DTYPE_F32 ? 4 : 2; }
+bool valid_dtype(int d) { return d == DBS_CUDA_DTYPE_F32 || d == DBS_CUDA_DTYPE_F16 || d == DBS_CUDA_DTYPE_BF16; }
+
+bool has_per_example(const DBSCudaDecodeArgs& a) {
+    return a.steps_per_example || a.beam_sizes_per_example || a.eos_tokens_per_example || a.min_lengths_per_example;
+}
+bool constrained(const DBSCudaDecodeArgs& a) { return a.no_repeat_ngram_size > 0 || a.repetition_penalty > 1.0f; }
+
+bool valid_args(const DBSCudaDecodeArgs* a) {
+    if (!a) return false;
+    if (a->batch_size <= 0 || a->steps <= 0 || a->beam_size <= 0 || a->vocab_size <= 0) return false;
+    if (a->beam_size > DBS_CUDA_MAX_BEAM) return false;
+    if (a->eos_token < -1 || a->eos_token >= a->vocab_size) return false;
+    if (a->min_length < 0 || a->reserved0 != 0) return false;
+    if (!std::isfinite(a->length_penalty_alpha) || a->length_penalty_alpha < 0.0f) return false;
+    if (!std::isfinite(a->repetition_penalty) || a->repetition_penalty < 0.0f) return false;
+    // Candidate indices parent * V + token fit in 32 bits (keys), tickets B*K*T fit in 31 bits.
+    const int64_t cand = static_cast<int64_t>(a->beam_size) * a->vocab_size;
+    if (cand > std::numeric_limits<int32_t>::max()) return false;
+    const int64_t tickets = static_cast<int64_t>(a->batch_size) * a->beam_size * a->steps;
+    if (tickets > (int64_t{1} << 31)) return false;
+    const double elems = static_cast<double>(a->batch_size) * a->steps * a->beam_size * a->vocab_size;
+    return elems < 9.0e18;
+}
+
+bool valid_options(const DBSCudaSearchOptions* o, const DBSCudaDecodeArgs& a) {
+    if (!o) return true;
+    if (o->reserved0 != 0 || o->reserved[0] || o->reserved[1] || o->reserved[2] || o->reserved[3]) return false;
+    if (o->extra_eos_count < 0 || o->extra_eos_count > DBS_CUDA_MAX_EXTRA_EOS) return false;
+    for (int i = 0; i < o->extra_eos_count; ++i)
+        if (o->extra_eos_tokens[i] < 0 || o->extra_eos_tokens[i] >= a.vocab_size) return false;
+    return o->extra_eos_count == 0 || a.eos_token >= 0 || a.eos_tokens_per_example;
+}
+
+// Workspace layout of a decode (step_stride < 0) or of one step.
+struct DecodeLayout {
+    int64_t raw, len, ended, last, keys, arrive, flag, ticket, error, status;
+    int64_t prefix[2], prefix_len[2];
+    int64_t total;
+    int list_len;
+};
+
+DecodeLayout make_layout(const DBSCudaDecodeArgs& a, bool step_api) {
+    DecodeLayout L{};
+    const int64_t B = a.batch_size, K = a.beam_size, T = a.steps;
+    int64_t off = 0;
+    auto take = [&off](int64_t bytes) {
+        const int64_t at = off;
+        off = align_up(off + (bytes > 0 ? bytes : 1));
+        return at;
+    };
+    L.list_len = decode_list_len(a.beam_size);
+    if (!step_api) {
+        L.raw = take(B * K * 4);
+        L.len = take(B * K * 4);
+        L.ended = take(B * K);
+        L.last = take(B * K * 4);
+    }
+    L.keys = take(B * K * L.list_len * 8);
+    L.arrive = take(B * 4);
+    L.flag = take(B * 4);
+    L.ticket = take(4);
+    L.error = take(4);
+    L.status = take(4);
+    if (!step_api && constrained(a)) {
+        for (int i = 0; i < 2; ++i) {
+            L.prefix[i] = take(B * K * T * 4);
+            L.prefix_len[i] = take(B * K * 4);
+        }
+    } else {
+        L.prefix[0] = L.prefix[1] = L.prefix_len[0] = L.prefix_len[1] = -1;
+    }
+    L.total = off;
+    return L;
+}
+
+// Scratch owned for the duration of one call when the caller passed none.
+class Scratch {
+public:
+    Scratch(void* user, int64_t user_bytes, int64_t need, cudaStream_t s) : stream_(s) {
+        if (user) {
+            ptr_ = static_cast<char*>(user);
+            status_ = user_bytes >= need ? DBS_CUDA_STATUS_OK : DBS_CUDA_STATUS_INVALID_ARGUMENT;
+            return;
+        }
+        void* p = nullptr;
+        if (cudaMallocAsync(&p, static_cast<size_t>(need > 0 ? need : 1), s) != cudaSuccess) {
+            cudaGetLastError();
+            status_ = DBS_CUDA_STATUS_OUT_OF_MEMORY;
+            return;
+        }
+        ptr_ = static_cast<char*>(p);
+        owned_ = true;
+    }
+    ~Scratch() {
+        if (owned_) cudaFreeAsync(ptr_, stream_);
+    }
+    Scratch(const Scratch&) = delete;
+    Scratch& operator=(const Scratch&) = delete;
+    int status() const { return status_; }
+    template <class T>
+    T* at(int64_t off) const {
+        return off < 0 ? nullptr : reinterpret_cast<T*>(ptr_ + off);
+    }
+
+private:
+    cudaStream_t stream_;
+    char* ptr_ = nullptr;
+    bool owned_ = false;
+    int status_ = DBS_CUDA_STATUS_OK;
+};
+
+int sm_count_of_current_device() {
+    static std::mutex mu;
+    static int cache[64] = {0};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+    std::lock_guard<std::mutex> lock(mu);
+    if (dev >= 0 && dev < 64 && cache[dev] > 0) return cache[dev];
+    int n = 0;
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    if (n <= 0) n = 148;
+    if (dev >= 0 && dev < 64) cache[dev] = n;
+    return n;
+}
+
+// End of a call: launch errors, then (debug) a synchronizing check of the
+// stream and of the engine's error word.
+int finish(cudaStream_t stream, const int32_t* error_word) {
+    if (cudaGetLastError() != cudaSuccess) return DBS_CUDA_STATUS_LAUNCH_FAILED;
+    if (sync_requested()) {
+        if (cudaStreamSynchronize(stream) != cudaSuccess) return DBS_CUDA_STATUS_LAUNCH_FAILED;
+        if (error_word) {
+            int32_t e = 0;
+            if (cudaMemcpy(&e, error_word, sizeof e, cudaMemcpyDeviceToHost) != cudaSuccess) return DBS_CUDA_STATUS_LAUNCH_FAILED;
+            if (e != 0) return DBS_CUDA_STATUS_LAUNCH_FAILED;
+        }
+        if (cudaGetLastError() != cudaSuccess) return DBS_CUDA_STATUS_LAUNCH_FAILED;
+    }
+    return DBS_CUDA_STATUS_OK;
+}
+
+void fill_params(DecodeParams& p, const DBSCudaDecodeArgs& a, const DBSCudaSearchOptions* o) {
+    std::memset(&p, 0, sizeof p);
+    p.B = a.batch_size;
+    p.T = a.steps;
+    p.K = a.beam_size;
+    p.V = a.vocab_size;
+    p.eos = a.eos_token;
+    p.min_length = a.min_length;
+    p.alpha = a.length_penalty_alpha;
+    p.ngram = a.no_repeat_ngram_size > 0 ? a.no_repeat_ngram_size : 0;
+    p.penalise = a.repetition_penalty > 1.0f ? 1 : 0;
+    // logf of the float penalty on the host, exactly as the CPU decoder computes it.
+    p.log_penalty = p.penalise ? std::log(a.repetition_penalty) : 0.0f;
+    p.n_extra = o ? o->extra_eos_count : 0;
+    for (int i = 0; i < p.n_extra; ++i) p.extra[i] = o->extra_eos_tokens[i];
+    p.steps_pe = a.steps_per_example;
+    p.beams_pe = a.beam_sizes_per_example;
+    p.eos_pe = a.eos_tokens_per_example;
+    p.minlen_pe = a.min_lengths_per_example;
+    p.banned = a.banned_tokens;
+    p.timeout_ns = kTimeoutNs;
+}
+
+// Range check of per-example arrays on the device (one synchronization).
+int validate_per_example(const DecodeParams& p, const DBSCudaDecodeArgs& a, int32_t* status, cudaStream_t stream) {
+    if (!has_per_example(a)) return DBS_CUDA_STATUS_OK;
+    if (cudaMemsetAsync(status, 0, sizeof(int32_t), stream) != cudaSuccess) return DBS_CUDA_STATUS_LAUNCH_FAILED;
+    if (launch_validate(p, status, stream) != cudaSuccess) return DBS_CUDA_STATUS_LAUNCH_FAILED;
+    int32_t h = 1;
+    if (cudaMemcpyAsync(&h, status, sizeof h, cudaMemcpyDeviceToHost, stream) != cudaSuccess) return DBS_CUDA_STATUS_LAUNCH_FAILED;
+    if (cudaStreamSynchronize(stream) != cudaSuccess) return DBS_CUDA_STATUS_LAUNCH_FAILED;
+    return h == 0 ? DBS_CUDA_STATUS_OK : DBS_CUDA_STATUS_INVALID_ARGUMENT;
+}
+
+void stage_choice(DecodeParams& p, int dtype, bool from_logits) {
+    const int64_t row_bytes = static_cast<int64_t>(p.V) * elem_bytes(dtype) + 16;
+    const int64_t row_smem = (row_bytes + 127) / 128 * 128;
+    const int64_t sel = static_cast<int64_t>(decode_select_smem(p.K));
+    p.staged = from_logits && row_smem + sel <= kMaxRowSmem ? 1 : 0;
+    p.row_smem = p.staged ? static_cast<int>(row_smem) : 0;
+}
+
+int run_decode(const void* inputs, int dtype, int from_logits, const DBSCudaDecodeArgs* args,
+               const DBSCudaSearchOptions* options, const DBSCudaDecodeOutputs* outputs, float* row_lse,
+               void* workspace, int64_t workspace_bytes, cudaStream_t stream) {
+    if (!inputs || !valid_dtype(dtype) || !valid_args(args) || !outputs || !outputs->final_scores) {
+        return DBS_CUDA_STATUS_INVALID_ARGUMENT;
+    }
+    if (!valid_options(options, *args)) return DBS_CUDA_STATUS_INVALID_ARGUMENT;
+    const DBSCudaDecodeArgs& a = *args;
+    const DecodeLayout L = make_layout(a, false);
+    Scratch ws(workspace, workspace_bytes, L.total, stream);
+    if (ws.status() != DBS_CUDA_STATUS_OK) return ws.status();
+    DecodeParams p;
+    fill_params(p, a, options);
+    p.inputs = inputs;
+    p.step_api = 0;
+    p.raw = ws.at<float>(L.raw);
+    p.len = ws.at<int32_t>(L.len);
+    p.ended = ws.at<uint8_t>(L.ended);
+    p.last = ws.at<int32_t>(L.last);
+    for (int i = 0; i < 2; ++i) {
+        p.prefix[i] = ws.at<int32_t>(L.prefix[i]);
+        p.prefix_len[i] = ws.at<int32_t>(L.prefix_len[i]);
+    }
+    p.out = *outputs;
+    p.row_lse = row_lse;
+    p.keys = ws.at<uint64_t>(L.keys);
+    p.list_len = L.list_len;
+    p.arrive = ws.at<uint32_t>(L.arrive);
+    p.flag = ws.at<int32_t>(L.flag);
+    p.ticket = ws.at<uint32_t>(L.ticket);
+    p.error = ws.at<int32_t>(L.error);
+    stage_choice(p, dtype, from_logits != 0);
+    const int rc = validate_per_example(p, a, ws.at<int32_t>(L.status), stream);
+    if (rc != DBS_CUDA_STATUS_OK) return rc;
+    if (launch_init(p, stream) != cudaSuccess) return DBS_CUDA_STATUS_LAUNCH_FAILED;
+    if (launch_decode(p, dtype, from_logits != 0, stream, sm_count_of_current_device()) != cudaSuccess) {
+        return DBS_CUDA_STATUS_LAUNCH_FAILED;
+    }
+    return finish(stream, p.error);
+}
+
+int run_step(const void* inputs, int dtype, int from_logits, const DBSCudaDecodeArgs* args,
+             const DBSCudaSearchOptions* options, const DBSCudaBeamState* state, const DBSCudaDecodeOutputs* outputs,
+             float* row_lse, void* workspace, int64_t workspace_bytes, cudaStream_t stream) {
+    if (!inputs || !valid_dtype(dtype) || !valid_args(args) || !state || !outputs) return DBS_CUDA_STATUS_INVALID_ARGUMENT;
+    if (!valid_options(options, *args)) return DBS_CUDA_STATUS_INVALID_ARGUMENT;
+    const DBSCudaDecodeArgs& a = *args;
+    if (a.steps != 1 || a.steps_per_example) return DBS_CUDA_STATUS_INVALID_ARGUMENT;
+    if (!state->raw_scores || !state->lengths || !state->finished || state->prefix_stride < 0 || state->reserved0 != 0) {
+        return DBS_CUDA_STATUS_INVALID_ARGUMENT;
+    }
+    if (constrained(a) && state->prefix_stride > 0 && !state->prefixes) return DBS_CUDA_STATUS_INVALID_ARGUMENT;
+    const DecodeLayout L = make_layout(a, true);
+    Scratch ws(workspace, workspace_bytes, L.total, stream);
+    if (ws.status() != DBS_CUDA_STATUS_OK) return ws.status();
+    DecodeParams p;
+    fill_params(p, a, options);
+    p.inputs = inputs;
+    p.step_api = 1;
+    p.raw = state->raw_scores;
+    p.len = state->lengths;
+    p.ended = state->finished;
+    p.last = nullptr;
+    p.caller_prefix = state->prefixes;
+    p.prefix_stride = state->prefix_stride;
+    p.out = *outputs;
+    p.row_lse = row_lse;
+    p.keys = ws.at<uint64_t>(L.keys);
+    p.list_len = L.list_len;
+    p.arrive = ws.at<uint32_t>(L.arrive);
+    p.flag = ws.at<int32_t>(L.flag);
+    p.ticket = ws.at<uint32_t>(L.ticket);
+    p.error = ws.at<int32_t>(L.error);
+    stage_choice(p, dtype, from_logits != 0);
+    const int rc = validate_per_example(p, a, ws.at<int32_t>(L.status), stream);
+    if (rc != DBS_CUDA_STATUS_OK) return rc;
+    if (launch_init(p, stream) != cudaSuccess) return DBS_CUDA_STATUS_LAUNCH_FAILED;
+    if (launch_decode(p, dtype, from_logits != 0, stream, sm_count_of_current_device()) != cudaSuccess) {
+        return DBS_CUDA_STATUS_LAUNCH_FAILED;
+    }
+    return finish(stream, p.error);
+}
+
+int64_t backward_ws_bytes(const DBSCudaDecodeArgs& a) {
+    return align_up(static_cast<int64_t>(a.batch_size) * a.steps * a.beam_size * 4);
+}
+
+BackwardParams backward_params(const DBSCudaDecodeArgs& a) {
+    BackwardParams p;
+    std::memset(&p, 0, sizeof p);
+    p.B = a.batch_size;
+    p.T = a.steps;
+    p.K = a.beam_size;
+    p.V = a.vocab_size;
+    p.alpha = a.length_penalty_alpha;
+    p.steps_pe = a.steps_per_example;
+    p.beams_pe = a.beam_sizes_per_example;
+    return p;
+}
+
+}  // namespace
+}  // namespace dbsb
+
+using namespace dbsb;
+
+extern "C" {
+
+DBS_CUDA_EXPORT int dbs_cuda_available(void) {
+    int n = 0;
+    const bool ok = cudaGetDeviceCount(&n) == cudaSuccess && n > 0;
+    if (!ok) cudaGetLastError();
+    return ok ? 1 : 0;
+}
+
+DBS_CUDA_EXPORT const char* dbs_cuda_status_string(int status) {
+    switch (status) {
+        case DBS_CUDA_STATUS_OK: return "ok";
+        case DBS_CUDA_STATUS_UNAVAILABLE: return "CUDA backend unavailable";
+        case DBS_CUDA_STATUS_INVALID_ARGUMENT: return "invalid argument";
+        case DBS_CUDA_STATUS_LAUNCH_FAILED: return "CUDA launch failed";
+        case DBS_CUDA_STATUS_OUT_OF_MEMORY: return "CUDA out of memory";
+        default: return "unknown CUDA status";
+    }
+}
+
+DBS_CUDA_EXPORT int dbs_cuda_set_synchronization(int synchronize) {
+    if (synchronize != 0 && synchronize != 1) return DBS_CUDA_STATUS_INVALID_ARGUMENT;
+    g_sync.store(synchronize, std::memory_order_relaxed);
+    return DBS_CUDA_STATUS_OK;
+}
+
+DBS_CUDA_EXPORT int dbs_cuda_get_synchronization(void) { return g_sync.load(std::memory_order_relaxed); }
+
+DBS_CUDA_EXPORT int64_t dbs_cuda_decode_workspace_size(const DBSCudaDecodeArgs* args) {
+    if (!valid_args(args)) return -1;
+    return make_layout(*args, false).total;
+}
+
+DBS_CUDA_EXPORT int64_t dbs_cuda_backward_workspace_size(const DBSCudaDecodeArgs* args) {
+    if (!valid_args(args)) return -1;
+    return backward_ws_bytes(*args);
+}
+
+DBS_CUDA_EXPORT int64_t dbs_cuda_decode_step_workspace_size(const DBSCudaDecodeArgs* args, int prefix_stride) {
+    if (!valid_args(args) || args->steps != 1 || args->steps_per_example || prefix_stride < 0) return -1;
+    return make_layout(*args, true).total;
+}
+
+DBS_CUDA_EXPORT int dbs_cuda_decode_ex2(const void* inputs, int data_type, int from_logits, const DBSCudaDecodeArgs* args,
+                                        const DBSCudaSearchOptions* options, const DBSCudaDecodeOutputs* outputs,
+                                        float* row_lse, void* workspace, int64_t workspace_bytes, void* stream) {
+    return run_decode(inputs, data_type, from_logits, args, options, outputs, row_lse, workspace, workspace_bytes,
+                      static_cast<cudaStream_t>(stream));
+}
+
+DBS_CUDA_EXPORT int dbs_cuda_decode_ex(const void* inputs, int data_type, int from_logits, const DBSCudaDecodeArgs* args,
+                                       const DBSCudaDecodeOutputs* outputs, float* row_lse, void* workspace,
+                                       int64_t workspace_bytes, void* stream) {
+    return dbs_cuda_decode_ex2(inputs, data_type, from_logits, args, nullptr, outputs, row_lse, workspace,
+                               workspace_bytes, stream);
+}
+
+DBS_CUDA_EXPORT int dbs_cuda_decode(const float* log_probs, const DBSCudaDecodeArgs* args,
+                                    const DBSCudaDecodeOutputs* outputs, void* workspace, int64_t workspace_bytes,
+                                    void* stream) {
+    return dbs_cuda_decode_ex(log_probs, DBS_CUDA_DTYPE_F32, 0, args, outputs, nullptr, workspace, workspace_bytes,
+                              stream);
+}
+
+DBS_CUDA_EXPORT int dbs_cuda_decode_step_ex2(const void* inputs, int data_type, int from_logits,
+                                             const DBSCudaDecodeArgs* args, const DBSCudaSearchOptions* options,
+                                             const DBSCudaBeamState* state, const DBSCudaDecodeOutputs* outputs,
+                                             float* row_lse, void* workspace, int64_t workspace_bytes, void* stream) {
+    return run_step(inputs, data_type, from_logits, args, options, state, outputs, row_lse, workspace, workspace_bytes,
+                    static_cast<cudaStream_t>(stream));
+}
+
+DBS_CUDA_EXPORT int dbs_cuda_decode_step_ex(const void* inputs, int data_type, int from_logits,
+                                            const DBSCudaDecodeArgs* args, const DBSCudaBeamState* state,
+                                            const DBSCudaDecodeOutputs* outputs, float* row_lse, void* workspace,
+                                            int64_t workspace_bytes, void* stream) {
+    return dbs_cuda_decode_step_ex2(inputs, data_type, from_logits, args, nullptr, state, outputs, row_lse, workspace,
+                                    workspace_bytes, stream);
+}
+
+DBS_CUDA_EXPORT int dbs_cuda_decode_step(const float* log_probs, const DBSCudaDecodeArgs* args,
+                                         const DBSCudaBeamState* state, const DBSCudaDecodeOutputs* outputs,
+                                         void* workspace, int64_t workspace_bytes, void* stream) {
+    return dbs_cuda_decode_step_ex(log_probs, DBS_CUDA_DTYPE_F32, 0, args, state, outputs, nullptr, workspace,
+                                   workspace_bytes, stream);
+}
+
+DBS_CUDA_EXPORT int dbs_cuda_backward_ex(const DBSCudaDecodeArgs* args, const DBSCudaBackwardInputs* in,
+                                         float* grad_inputs, void* workspace, int64_t workspace_bytes, void* stream_ptr) {
+    if (!valid_args(args) || !in || !grad_inputs) return DBS_CUDA_STATUS_INVALID_ARGUMENT;
+    if (!in->parents || !in->tokens || !in->lengths || !in->from_logprob) return DBS_CUDA_STATUS_INVALID_ARGUMENT;
+    if (in->reserved0 != 0 || in->reserved[0] || in->reserved[1] || in->reserved[2] || in->reserved[3]) {
+        return DBS_CUDA_STATUS_INVALID_ARGUMENT;
+    }
+    if (in->logits && (!in->row_lse || !valid_dtype(in->logits_type))) return DBS_CUDA_STATUS_INVALID_ARGUMENT;
+    cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+    const DBSCudaDecodeArgs& a = *args;
+    BackwardParams p = backward_params(a);
+    p.parents = in->parents;
+    p.tokens = in->tokens;
+    p.lengths = in->lengths;
+    p.from_logprob = in->from_logprob;
+    p.g_final = in->grad_final_scores;
+    p.g_final_raw = in->grad_final_raw_scores;
+    p.g_scores = in->grad_scores;
+    p.g_raw = in->grad_raw_scores;
+    if (!in->logits) {
+        p.grad = grad_inputs;
+        if (launch_backward(p, stream) != cudaSuccess) return DBS_CUDA_STATUS_LAUNCH_FAILED;
+        return finish(stream, nullptr);
+    }
+    Scratch ws(workspace, workspace_bytes, backward_ws_bytes(a), stream);
+    if (ws.status() != DBS_CUDA_STATUS_OK) return ws.status();
+    p.draws = ws.at<float>(0);
+    const size_t slots = static_cast<size_t>(a.batch_size) * a.steps * a.beam_size;
+    if (cudaMemsetAsync(p.draws, 0, slots * sizeof(float), stream) != cudaSuccess) return DBS_CUDA_STATUS_LAUNCH_FAILED;
+    if (launch_backward(p, stream) != cudaSuccess) return DBS_CUDA_STATUS_LAUNCH_FAILED;
+    p.grad = grad_inputs;
+    if (launch_logit_correction(p, in->logits_type, in->logits, in->row_lse, stream) != cudaSuccess) {
+        return DBS_CUDA_STATUS_LAUNCH_FAILED;
+    }
+    return finish(stream, nullptr);
+}
+
+DBS_CUDA_EXPORT int dbs_cuda_backward(const DBSCudaDecodeArgs* args, const int32_t* parents, const int32_t* tokens,
+                                      const int32_t* lengths, const uint8_t* from_logprob,
+                                      const float* grad_final_scores, float* grad_log_probs, void* workspace,
+                                      int64_t workspace_bytes, void* stream) {
+    if (!valid_args(args) || !parents || !tokens || !lengths || !from_logprob || !grad_final_scores || !grad_log_probs) {
+        return DBS_CUDA_STATUS_INVALID_ARGUMENT;
+    }
+    DBSCudaBackwardInputs in;
+    std::memset(&in, 0, sizeof in);
+    in.parents = parents;
+    in.tokens = tokens;
+    in.lengths = lengths;
+    in.from_logprob = from_logprob;
+    in.grad_final_scores = grad_final_scores;
+    return dbs_cuda_backward_ex(args, &in, grad_log_probs, workspace, workspace_bytes, stream);
+}
+
+DBS_CUDA_EXPORT int dbs_cuda_length_penalty(const int32_t* lengths, int64_t count, float alpha, float* out,
+                                            void* stream_ptr) {
+    if (count < 0 || (count > 0 && (!lengths || !out)) || !std::isfinite(alpha) || alpha < 0.0f) {
+        return DBS_CUDA_STATUS_INVALID_ARGUMENT;
+    }
+    if (count == 0) return DBS_CUDA_STATUS_OK;
+    cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+    if (launch_length_penalty(lengths, count, alpha, out, stream) != cudaSuccess) return DBS_CUDA_STATUS_LAUNCH_FAILED;
+    return finish(stream, nullptr);
+}
+
+DBS_CUDA_EXPORT int dbs_cuda_path_gradient(const DBSCudaDecodeArgs* args, const int32_t* parents,
+                                           const int32_t* tokens, const int32_t* lengths, const uint8_t* from_logprob,
+                                           const float* grad_final_scores, float* draws, void* stream_ptr) {
+    if (!valid_args(args) || !parents || !tokens || !lengths || !from_logprob || !grad_final_scores || !draws) {
+        return DBS_CUDA_STATUS_INVALID_ARGUMENT;
+    }
+    cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+    const DBSCudaDecodeArgs& a = *args;
+    const size_t slots = static_cast<size_t>(a.batch_size) * a.steps * a.beam_size;
+    if (cudaMemsetAsync(draws, 0, slots * sizeof(float), stream) != cudaSuccess) return DBS_CUDA_STATUS_LAUNCH_FAILED;
+    BackwardParams p = backward_params(a);
+    p.parents = parents;
+    p.tokens = tokens;
+    p.lengths = lengths;
+    p.from_logprob = from_logprob;
+    p.g_final = grad_final_scores;
+    p.draws = draws;
+    if (launch_backward(p, stream) != cudaSuccess) return DBS_CUDA_STATUS_LAUNCH_FAILED;
+    return finish(stream, nullptr);
+}
+
+// ---------------------------------------------------------------------------
+// Additions of this engine (include/dbs_cuda_b200.h)
+// ---------------------------------------------------------------------------
+
+DBS_CUDA_EXPORT int dbs_cuda_backtrack(const DBSCudaDecodeArgs* args, const int32_t* tokens, const int32_t* parents,
+                                       int64_t* sequences, void* stream_ptr) {
+    if (!valid_args(args) || !tokens || !parents || !sequences) return DBS_CUDA_STATUS_INVALID_ARGUMENT;
+    cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+    const DBSCudaDecodeArgs& a = *args;
+    if (launch_backtrack(a.batch_size, a.steps, a.beam_size, tokens, parents, a.steps_per_example, sequences, stream) !=
+        cudaSuccess) {
+        return DBS_CUDA_STATUS_LAUNCH_FAILED;
+    }
+    return finish(stream, nullptr);
+}
+
+DBS_CUDA_EXPORT int dbs_cuda_b200_abi_version(void) { return DBS_CUDA_B200_ABI_VERSION; }
+
+}  // extern "C"

@@ -1,0 +1,223 @@
+// SPDX-License-Identifier: MIT
+//
+// Companion kernels of the decode: the surrogate-gradient backward (per-slot
+// path gradients, optionally scattered into a dense [B, T, K, V] gradient),
+// the log-softmax correction of rows decoded from logits, the GNMT length
+// penalty, and backtracking of the final beams' token sequences.
+//
+// Backward semantics (beamgrad 2.3.0 src/decoder.cpp:186-304, run_backward
+// without a relaxed pool): walking an example's steps from the last to the
+// first, slot k of step t with parent q >= 0 gets
+//     drank = g_scores[t, k] (+ g_final[k] at the last step)
+//     draw  = next[k] + drank * (1 / penalty(max(len, 1))) + g_raw[t, k]
+//             (+ g_final_raw[k] at the last step)
+// and, when draw != 0, adds draw to prev[q] (children summed in slot order,
+// starting from 0) and, when the slot consumed an input entry, to entry
+// (t, q, token). Every slot of a step has a distinct entry, so the dense
+// update needs no atomics and the result is deterministic.
+#include "engine.cuh"
+
+namespace dbsb {
+
+
+
+// One CTA per example; its beams' running gradients live in shared memory.
+__global__ void __launch_bounds__(kThreads) backward_kernel(const __grid_constant__ BackwardParams p) {
+    __shared__ float next_g[DBS_CUDA_MAX_BEAM];
+    __shared__ float prev_g[DBS_CUDA_MAX_BEAM];
+    __shared__ float draw_s[DBS_CUDA_MAX_BEAM];
+    __shared__ int32_t par_s[DBS_CUDA_MAX_BEAM];
+    const int b = blockIdx.x;
+    const int tid = threadIdx.x;
+    const int K = p.K;
+    int steps = p.steps_pe ? p.steps_pe[b] : p.T;
+    int Kb = p.beams_pe ? p.beams_pe[b] : K;
+    steps = steps < 0 ? 0 : (steps > p.T ? p.T : steps);
+    Kb = Kb < 0 ? 0 : (Kb > K ? K : Kb);
+    for (int k = tid; k < Kb; k += kThreads) next_g[k] = 0.0f;
+    __syncthreads();
+    for (int t = steps - 1; t >= 0; --t) {
+        const bool last = t == steps - 1;
+        const int64_t base = (static_cast<int64_t>(b) * p.T + t) * K;
+        for (int k = tid; k < Kb; k += kThreads) {
+            const int64_t slot = base + k;
+            const int q = p.parents[slot];
+            float d = 0.0f;
+            int pq = -1;
+            if (q >= 0 && q < Kb) {
+                float drank = 0.0f;
+                if (p.g_scores) drank = __fadd_rn(drank, p.g_scores[slot]);
+                if (last && p.g_final) drank = __fadd_rn(drank, p.g_final[static_cast<int64_t>(b) * K + k]);
+                const float inv = __fdiv_rn(1.0f, gnmt_penalty(p.lengths[slot], p.alpha));
+                d = __fadd_rn(next_g[k], __fmul_rn(drank, inv));
+                if (p.g_raw) d = __fadd_rn(d, p.g_raw[slot]);
+                if (last && p.g_final_raw) d = __fadd_rn(d, p.g_final_raw[static_cast<int64_t>(b) * K + k]);
+                if (d != 0.0f) {
+                    pq = q;
+                    const int tok = p.tokens[slot];
+                    if (p.from_logprob[slot] && tok >= 0 && tok < p.V) {
+                        if (p.draws) p.draws[slot] = d;
+                        if (p.grad) {
+                            const int64_t g = (base + q) * static_cast<int64_t>(p.V) + tok;
+                            p.grad[g] = __fadd_rn(p.grad[g], d);
+                        }
+                    }
+                }
+            }
+            draw_s[k] = d;
+            par_s[k] = pq;
+        }
+        __syncthreads();
+        // prev[q] = sum of its children's draws in slot order, from 0.
+        for (int q = tid; q < Kb; q += kThreads) {
+            float sum = 0.0f;
+            for (int k = 0; k < Kb; ++k)
+                if (par_s[k] == q) sum = __fadd_rn(sum, draw_s[k]);
+            prev_g[q] = sum;
+        }
+        __syncthreads();
+        for (int k = tid; k < Kb; k += kThreads) next_g[k] = prev_g[k];
+        __syncthreads();
+    }
+}
+
+// Log-softmax correction, one CTA per input row (b, t, q). A row receives
+// g_v - softmax(x)_v * S over every v, where g_v are the path gradients of the
+// slots of step t that extend parent q (their draws, at their tokens) and S
+// their sum in token order (src/decoder.hpp:212-242 apply_path_gradient).
+// Rows without a path gradient are left untouched.
+template <int DT>
+__global__ void __launch_bounds__(kThreads) logit_correction_kernel(const __grid_constant__ BackwardParams p,
+                                                                    const void* logits, const float* row_lse) {
+    __shared__ int32_t tok_s[DBS_CUDA_MAX_BEAM];
+    __shared__ float val_s[DBS_CUDA_MAX_BEAM];
+    __shared__ int n_s;
+    __shared__ float sum_s;
+    const int64_t r = blockIdx.x;  // row index in [B*T*K)
+    const int K = p.K;
+    const int q = static_cast<int>(r % K);
+    const int64_t bt = r / K;
+    const int b = static_cast<int>(bt / p.T);
+    const int t = static_cast<int>(bt - static_cast<int64_t>(b) * p.T);
+    int steps = p.steps_pe ? p.steps_pe[b] : p.T;
+    int Kb = p.beams_pe ? p.beams_pe[b] : K;
+    Kb = Kb < 0 ? 0 : (Kb > K ? K : Kb);
+    if (t >= steps || q >= Kb) return;
+    const int64_t base = bt * K;
+    const int tid = threadIdx.x;
+    if (tid == 0) n_s = 0;
+    __syncthreads();
+    for (int k = tid; k < Kb; k += kThreads) {
+        const float d = p.draws[base + k];
+        if (d != 0.0f && p.parents[base + k] == q) {
+            const int i = atomicAdd(&n_s, 1);
+            tok_s[i] = p.tokens[base + k];
+            val_s[i] = d;
+        }
+    }
+    __syncthreads();
+    const int n = n_s;
+    if (n == 0) return;
+    if (tid == 0) {
+        // Sort by token (distinct within a row) and sum in token order.
+        for (int i = 1; i < n; ++i) {
+            const int32_t tk = tok_s[i];
+            const float vv = val_s[i];
+            int j = i;
+            while (j > 0 && tok_s[j - 1] > tk) {
+                tok_s[j] = tok_s[j - 1];
+                val_s[j] = val_s[j - 1];
+                --j;
+            }
+            tok_s[j] = tk;
+            val_s[j] = vv;
+        }
+        float s = 0.0f;
+        for (int i = 0; i < n; ++i) s = __fadd_rn(s, val_s[i]);
+        sum_s = s;
+    }
+    __syncthreads();
+    const float S = sum_s;
+    const float lse = row_lse[r];
+    const int64_t V = p.V;
+    const int64_t off = r * V;
+    float* g = p.grad + off;
+    for (int64_t v = tid; v < V; v += kThreads) {
+        const float x = load_elem<DT>(logits, off + v);
+        float gv = 0.0f;
+        int lo = 0, hi = n;
+        while (lo < hi) {
+            const int mid = (lo + hi) >> 1;
+            if (tok_s[mid] < v) lo = mid + 1;
+            else hi = mid;
+        }
+        if (lo < n && tok_s[lo] == v) gv = val_s[lo];
+        const float d = __fsub_rn(gv, __fmul_rn(softmax_probability(x, lse), S));
+        g[v] = __fadd_rn(g[v], d);
+    }
+}
+
+__global__ void length_penalty_kernel(const int32_t* __restrict__ lengths, int64_t count, float alpha,
+                                      float* __restrict__ out) {
+    const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i < count) out[i] = gnmt_penalty(lengths[i], alpha);
+}
+
+// Token sequences of the final beams, [B, K, T] int64: entry (b, k, t) is the
+// token final beam k holds at step t, following parents back from the last
+// step; -1 for dead beams and for steps past the example's length
+// (python/beamgrad/_torch.py:582-606 of beamgrad 2.3.0). One thread per (b, k).
+__global__ void backtrack_kernel(int B, int T, int K, const int32_t* __restrict__ tokens,
+                                 const int32_t* __restrict__ parents, const int32_t* __restrict__ steps_pe,
+                                 int64_t* __restrict__ out) {
+    const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= static_cast<int64_t>(B) * K) return;
+    const int b = static_cast<int>(i / K);
+    const int k = static_cast<int>(i - static_cast<int64_t>(b) * K);
+    int steps = steps_pe ? steps_pe[b] : T;
+    int beam = k;
+    int64_t* o = out + i * T;
+    for (int t = T - 1; t >= 0; --t) {
+        const bool decoded = t < steps;
+        const bool alive = beam >= 0 && decoded;
+        const int64_t slot = (static_cast<int64_t>(b) * T + t) * K + (beam >= 0 ? beam : 0);
+        o[t] = alive ? static_cast<int64_t>(tokens[slot]) : -1;
+        if (decoded) beam = beam >= 0 ? parents[slot] : -1;
+        if (beam >= K) beam = -1;
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Launchers
+// ---------------------------------------------------------------------------
+cudaError_t launch_backward(const BackwardParams& p, cudaStream_t stream) {
+    backward_kernel<<<static_cast<unsigned>(p.B), kThreads, 0, stream>>>(p);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_logit_correction(const BackwardParams& p, int dtype, const void* logits, const float* row_lse,
+                                    cudaStream_t stream) {
+    const int64_t rows = static_cast<int64_t>(p.B) * p.T * p.K;
+    const unsigned grid = static_cast<unsigned>(rows);
+    switch (dtype) {
+        case DBS_CUDA_DTYPE_F16: logit_correction_kernel<1><<<grid, kThreads, 0, stream>>>(p, logits, row_lse); break;
+        case DBS_CUDA_DTYPE_BF16: logit_correction_kernel<2><<<grid, kThreads, 0, stream>>>(p, logits, row_lse); break;
+        default: logit_correction_kernel<0><<<grid, kThreads, 0, stream>>>(p, logits, row_lse); break;
+    }
+    return cudaGetLastError();
+}
+
+cudaError_t launch_length_penalty(const int32_t* lengths, int64_t count, float alpha, float* out, cudaStream_t stream) {
+    const int64_t blocks = (count + 255) / 256;
+    length_penalty_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(lengths, count, alpha, out);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_backtrack(int B, int T, int K, const int32_t* tokens, const int32_t* parents,
+                             const int32_t* steps_pe, int64_t* out, cudaStream_t stream) {
+    const int64_t n = static_cast<int64_t>(B) * K;
+    backtrack_kernel<<<static_cast<unsigned>((n + 127) / 128), 128, 0, stream>>>(B, T, K, tokens, parents, steps_pe, out);
+    return cudaGetLastError();
+}
+
+}  // namespace dbsb

@@ -1,0 +1,119 @@
+// SPDX-License-Identifier: MIT
+//
+// The fused decode step of the B200 engine: one persistent kernel runs every
+// step of every example.
+//
+// Work items are beam rows (t, b, k), handed out by an atomic ticket in
+// t-major order. A CTA that takes row (t, b, k) waits (bounded) until example
+// b's step t-1 is published, reads the parent's state, and, when the row is
+// read by the search (live, unfinished parent of an active step), streams it
+// from HBM once:
+//   - from logits: the row is staged in shared memory by a 1-D TMA bulk copy
+//     (cp.async.bulk + mbarrier); pass 1 takes the maximum and the NaN/+inf
+//     flag, pass 2 sums exp(x - max) with thread j owning logsumexp lane j
+//     (v = j mod 256, increasing v, the reference's fixed order), then the
+//     pairwise lane tree gives lse; pass 3 turns entries into candidate keys;
+//   - from log-probs: a single streaming pass of 128-bit loads;
+// and keeps the row's best candidates (register top-k per thread for beams up
+// to 16, a block radix select above). The CTA that completes the last row of
+// (t, b) merges the K row lists with the carried-forward finished beams, writes
+// the step's trace and the new state, and publishes step t of example b.
+//
+// Tickets of step t are all handed out before any of step t+1, and a CTA only
+// waits for a step whose tickets are lower than its own (held by running CTAs),
+// so the hand-off cannot deadlock; every wait is also bounded by a timeout that
+// sets the workspace error word.
+//
+// Candidate order: within one step every scanned candidate of an example
+// extends a beam of the same length, so ranking by (raw desc, parent*V+token
+// asc) -- a 64-bit key -- equals the CPU decoder's ranking by (score, raw,
+// parent, token) (src/common.hpp:269-276 of beamgrad 2.3.0). Carried-forward
+// candidates are merged with the full comparator.
+#include "decode_impl.cuh"
+
+namespace dbsb {
+
+cudaError_t launch_decode_f32(const DecodeParams& p, bool logits, cudaStream_t stream, int sm_count);
+cudaError_t launch_decode_f16(const DecodeParams& p, bool logits, cudaStream_t stream, int sm_count);
+cudaError_t launch_decode_bf16(const DecodeParams& p, bool logits, cudaStream_t stream, int sm_count);
+
+// ---------------------------------------------------------------------------
+// Set-up kernels
+// ---------------------------------------------------------------------------
+__global__ void init_decode_kernel(DecodeParams p) {
+    const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    const int64_t beams = static_cast<int64_t>(p.B) * p.K;
+    if (i < beams) {
+        const int b = static_cast<int>(i / p.K);
+        const int k = static_cast<int>(i - static_cast<int64_t>(b) * p.K);
+        if (!p.step_api) {
+            const Meta m = load_meta(p, b);
+            p.raw[i] = (k == 0 && k < m.beam) ? 0.0f : f_ninf();
+            p.len[i] = 0;
+            p.ended[i] = 0;
+            p.last[i] = -1;
+            if (p.prefix_len[0]) p.prefix_len[0][i] = 0;
+        }
+        if (k == 0) {
+            p.flag[b] = 0;
+            p.arrive[b] = 0;
+            if (p.out.invalid_input) p.out.invalid_input[b] = 0;
+        }
+    }
+    if (i == 0) {
+        *p.ticket = 0;
+        *p.error = kErrNone;
+    }
+}
+
+// Per-example arguments in range? (status stays 0 when they all are.)
+__global__ void validate_meta_kernel(DecodeParams p, int* status) {
+    const int b = blockIdx.x * blockDim.x + threadIdx.x;
+    if (b >= p.B) return;
+    const int steps = p.steps_pe ? p.steps_pe[b] : p.T;
+    const int beam = p.beams_pe ? p.beams_pe[b] : p.K;
+    const int eos = p.eos_pe ? p.eos_pe[b] : p.eos;
+    const int ml = p.minlen_pe ? p.minlen_pe[b] : p.min_length;
+    const bool ok = steps >= 1 && steps <= p.T && beam >= 1 && beam <= p.K && eos >= -1 && eos < p.V && ml >= 0;
+    if (!ok) atomicExch(status, 1);
+}
+
+// ---------------------------------------------------------------------------
+// Host-side launch
+// ---------------------------------------------------------------------------
+
+// Keys kept per row list.
+int decode_list_len(int K) {
+    if (K <= 1) return 1;
+    if (K <= 2) return 2;
+    if (K <= 4) return 4;
+    if (K <= 8) return 8;
+    if (K <= 16) return 16;
+    return K;
+}
+
+size_t decode_select_smem(int K) {
+    return K <= kFastBeam ? sizeof(SelectShared<kFastBeam>) : sizeof(SelectShared<kSelectCap>);
+}
+
+cudaError_t launch_decode(const DecodeParams& p, int dtype, bool logits, cudaStream_t stream, int sm_count) {
+    switch (dtype) {
+        case DBS_CUDA_DTYPE_F16: return launch_decode_f16(p, logits, stream, sm_count);
+        case DBS_CUDA_DTYPE_BF16: return launch_decode_bf16(p, logits, stream, sm_count);
+        default: return launch_decode_f32(p, logits, stream, sm_count);
+    }
+}
+
+cudaError_t launch_init(const DecodeParams& p, cudaStream_t stream) {
+    const int64_t n = static_cast<int64_t>(p.B) * p.K;
+    const int64_t blocks = (n + 255) / 256;
+    init_decode_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(p);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_validate(const DecodeParams& p, int* status, cudaStream_t stream) {
+    validate_meta_kernel<<<static_cast<unsigned>((p.B + 255) / 256), 256, 0, stream>>>(p, status);
+    return cudaGetLastError();
+}
+
+}  // namespace dbsb

@@ -1,0 +1,1023 @@
+// SPDX-License-Identifier: MIT
+//
+// The fused decode step of the B200 engine: one persistent kernel runs every
+// step of every example.
+//
+// Work items are beam rows (t, b, k), handed out by an atomic ticket in
+// t-major order. A CTA that takes row (t, b, k) waits (bounded) until example
+// b's step t-1 is published, reads the parent's state, and, when the row is
+// read by the search (live, unfinished parent of an active step), streams it
+// from HBM once:
+//   - from logits: the row is staged in shared memory by a 1-D TMA bulk copy
+//     (cp.async.bulk + mbarrier); pass 1 takes the maximum and the NaN/+inf
+//     flag, pass 2 sums exp(x - max) with thread j owning logsumexp lane j
+//     (v = j mod 256, increasing v, the reference's fixed order), then the
+//     pairwise lane tree gives lse; pass 3 turns entries into candidate keys;
+//   - from log-probs: a single streaming pass of 128-bit loads;
+// and keeps the row's best candidates (register top-k per thread for beams up
+// to 16, a block radix select above). The CTA that completes the last row of
+// (t, b) merges the K row lists with the carried-forward finished beams, writes
+// the step's trace and the new state, and publishes step t of example b.
+//
+// Tickets of step t are all handed out before any of step t+1, and a CTA only
+// waits for a step whose tickets are lower than its own (held by running CTAs),
+// so the hand-off cannot deadlock; every wait is also bounded by a timeout that
+// sets the workspace error word.
+//
+// Candidate order: within one step every scanned candidate of an example
+// extends a beam of the same length, so ranking by (raw desc, parent*V+token
+// asc) -- a 64-bit key -- equals the CPU decoder's ranking by (score, raw,
+// parent, token) (src/common.hpp:269-276 of beamgrad 2.3.0). Carried-forward
+// candidates are merged with the full comparator.
+#pragma once
+#include "engine.cuh"
+
+namespace dbsb {
+namespace {  // internal to each translation unit that includes this file
+
+// ---------------------------------------------------------------------------
+// Shared memory
+// ---------------------------------------------------------------------------
+
+struct RowShared {
+    unsigned long long mbar;
+    int ticket;
+    int is_last;
+    int invalid;
+    int n_blocked;
+    int n_penal;
+    int count;
+    int done;
+    int remaining;
+    unsigned long long sel_prefix;
+    unsigned long long sel_mask;
+    float wred[kWarps];
+    int ired[kWarps];
+    float lanes[kLanes];
+    int hist[256];
+    uint64_t wkeys[kWarps * kFastBeam];
+    int32_t blocked[kConsCap];
+    int32_t penal[kConsCap];
+    // select bookkeeping
+    int n_scanned;
+    int n_carry;
+};
+
+// Per-example select arrays of capacity KCAP, in dynamic shared memory.
+template <int KCAP>
+struct SelectShared {
+    uint64_t keys[KCAP];
+    float s_raw[KCAP];
+    int32_t s_len[KCAP];
+    int32_t s_last[KCAP];
+    uint8_t s_ended[KCAP];
+    float c_score[KCAP];
+    float c_raw[KCAP];
+    int32_t c_parent[KCAP];
+    int32_t c_len[KCAP];
+    int32_t c_token[KCAP];
+    float sc_score[KCAP];
+    // final assignment of slots
+    int32_t o_parent[KCAP];
+    int32_t o_token[KCAP];
+    int32_t o_len[KCAP];
+    float o_score[KCAP];
+    float o_raw[KCAP];
+    uint8_t o_from[KCAP];
+};
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// ---------------------------------------------------------------------------
+// TMA bulk staging of one row
+// ---------------------------------------------------------------------------
+
+__device__ __forceinline__ void mbar_init(unsigned long long* mbar) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_u32(mbar)) : "memory");
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(unsigned long long* mbar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(mbar)), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ void bulk_g2s(void* sdst, const void* gsrc, uint32_t bytes, unsigned long long* mbar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(smem_u32(sdst)),
+        "l"(gsrc), "r"(bytes), "r"(smem_u32(mbar))
+        : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(unsigned long long* mbar, uint32_t phase) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred P;\n mbarrier.try_wait.parity.shared::cta.b64 P, [%1], %2;\n selp.u32 %0, 1, 0, P;\n}\n"
+        : "=r"(ok)
+        : "r"(smem_u32(mbar)), "r"(phase)
+        : "memory");
+    return ok != 0;
+}
+
+// Bounded wait for the row's bulk copy. On timeout: records the error and keeps
+// waiting (bounded again) so no copy is left writing into shared memory.
+__device__ __forceinline__ bool mbar_wait(const DecodeParams& p, unsigned long long* mbar, uint32_t phase) {
+    if (mbar_try_wait(mbar, phase)) return true;
+    const unsigned long long start = global_ns();
+    for (;;) {
+        if (mbar_try_wait(mbar, phase)) return true;
+        if (global_ns() - start > p.timeout_ns) {
+            atomicCAS(p.error, kErrNone, kErrTimeout);
+            const unsigned long long again = global_ns();
+            while (!mbar_try_wait(mbar, phase) && global_ns() - again < p.timeout_ns) {
+            }
+            return false;
+        }
+    }
+}
+
+// Row layout in shared memory: the row keeps its global address modulo 16,
+// so the 16-byte-aligned body moves with one bulk copy and the ragged head
+// and tail (under 16 bytes each) with plain loads. Returns the offset of
+// element 0 in the buffer.
+template <int EB>
+__device__ __forceinline__ int stage_row(const DecodeParams& p, RowShared& sh, char* sbuf, const char* g,
+                                         int V, uint32_t& phase, bool& ok) {
+    const uintptr_t g0 = reinterpret_cast<uintptr_t>(g);
+    const uintptr_t g1 = g0 + static_cast<uintptr_t>(V) * EB;
+    const uintptr_t a0 = (g0 + 15) & ~static_cast<uintptr_t>(15);
+    const uintptr_t a1 = g1 & ~static_cast<uintptr_t>(15);
+    const int off = static_cast<int>(g0 & 15);
+    const int tid = threadIdx.x;
+    const bool bulk = a1 > a0;
+    if (tid == 0 && bulk) {
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        const uint32_t bytes = static_cast<uint32_t>(a1 - a0);
+        mbar_expect_tx(&sh.mbar, bytes);
+        constexpr uint32_t kChunk = 1u << 16;
+        for (uint32_t c = 0; c < bytes; c += kChunk) {
+            const uint32_t n = bytes - c < kChunk ? bytes - c : kChunk;
+            bulk_g2s(sbuf + (a0 - (g0 & ~static_cast<uintptr_t>(15))) + c, reinterpret_cast<const char*>(a0) + c, n,
+                     &sh.mbar);
+        }
+    }
+    // Ragged head / tail bytes (element granularity), or the whole row when tiny.
+    const uintptr_t head_end = bulk ? a0 : g1;
+    const int n_head = static_cast<int>((head_end - g0) / EB);
+    const int n_tail = bulk ? static_cast<int>((g1 - a1) / EB) : 0;
+    for (int i = tid; i < n_head + n_tail; i += kThreads) {
+        const uintptr_t src = i < n_head ? g0 + static_cast<uintptr_t>(i) * EB : a1 + static_cast<uintptr_t>(i - n_head) * EB;
+        char* dst = sbuf + (src - (g0 & ~static_cast<uintptr_t>(15)));
+        if (EB == 4) *reinterpret_cast<uint32_t*>(dst) = *reinterpret_cast<const uint32_t*>(src);
+        else *reinterpret_cast<uint16_t*>(dst) = *reinterpret_cast<const uint16_t*>(src);
+    }
+    ok = true;
+    if (bulk) {
+        ok = mbar_wait(p, &sh.mbar, phase);
+        phase ^= 1u;
+    }
+    ok = __syncthreads_and(ok) != 0;
+    return off;
+}
+
+// ---------------------------------------------------------------------------
+// Element iteration: 128-bit vectors for the aligned body, scalars for the
+// ragged ends. f(x, v) is called for every element exactly once; each thread
+// sees its elements in increasing v.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint4 ld_stream_v4(const void* p) {
+    uint4 r;
+    asm volatile("ld.global.nc.L1::no_allocate.L2::256B.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+                 : "l"(p));
+    return r;
+}
+
+template <int DT, bool kGlobal, class F>
+__device__ __forceinline__ void for_row(const char* row, int V, F&& f) {
+    using E = Elem<DT>;
+    constexpr int EB = E::kBytes;
+    constexpr int PER = 16 / EB;
+    const int tid = threadIdx.x;
+    const uintptr_t a = reinterpret_cast<uintptr_t>(row);
+    int head = static_cast<int>(((16 - (a & 15)) & 15) / EB);
+    if (head > V) head = V;
+    const auto* rp = reinterpret_cast<const typename E::T*>(row);
+    if (tid < head) f(E::to_f32(rp[tid]), tid);
+    const int nvec = (V - head) / PER;
+    const uint4* vp = reinterpret_cast<const uint4*>(row + static_cast<size_t>(head) * EB);
+    auto unpack = [&](const uint4& q, int v0) {
+        const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+        if constexpr (EB == 4) {
+#pragma unroll
+            for (int j = 0; j < 4; ++j) f(__uint_as_float(w[j]), v0 + j);
+        } else {
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                f(E::to_f32(static_cast<uint16_t>(w[j] & 0xffffu)), v0 + 2 * j);
+                f(E::to_f32(static_cast<uint16_t>(w[j] >> 16)), v0 + 2 * j + 1);
+            }
+        }
+    };
+    int c = tid;
+    if constexpr (kGlobal) {
+        for (; c + 3 * kThreads < nvec; c += 4 * kThreads) {
+            const uint4 q0 = ld_stream_v4(vp + c);
+            const uint4 q1 = ld_stream_v4(vp + c + kThreads);
+            const uint4 q2 = ld_stream_v4(vp + c + 2 * kThreads);
+            const uint4 q3 = ld_stream_v4(vp + c + 3 * kThreads);
+            unpack(q0, head + c * PER);
+            unpack(q1, head + (c + kThreads) * PER);
+            unpack(q2, head + (c + 2 * kThreads) * PER);
+            unpack(q3, head + (c + 3 * kThreads) * PER);
+        }
+        for (; c < nvec; c += kThreads) unpack(ld_stream_v4(vp + c), head + c * PER);
+    } else {
+        for (; c < nvec; c += kThreads) unpack(vp[c], head + c * PER);
+    }
+    const int tail0 = head + nvec * PER;
+    if (tail0 + tid < V) f(E::to_f32(rp[tail0 + tid]), tail0 + tid);
+}
+
+// ---------------------------------------------------------------------------
+// Block reductions
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ float block_max(RowShared& sh, float v) {
+    v = warp_max_f32(v);
+    if ((threadIdx.x & 31) == 0) sh.wred[threadIdx.x >> 5] = v;
+    __syncthreads();
+    float r = sh.wred[0];
+#pragma unroll
+    for (int w = 1; w < kWarps; ++w) r = fmaxf(r, sh.wred[w]);
+    __syncthreads();
+    return r;
+}
+__device__ __forceinline__ int block_sum(RowShared& sh, int v) {
+    v = warp_sum_i32(v);
+    if ((threadIdx.x & 31) == 0) sh.ired[threadIdx.x >> 5] = v;
+    __syncthreads();
+    int r = 0;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) r += sh.ired[w];
+    __syncthreads();
+    return r;
+}
+
+// ---------------------------------------------------------------------------
+// Block radix select: writes the `want` largest non-zero keys among gen(0..n)
+// (keys are unique) to out[0..count) in no particular order; returns count =
+// min(want, number of non-zero keys). 8-bit digits, most significant first,
+// stopping as soon as the boundary bucket is taken whole.
+// ---------------------------------------------------------------------------
+template <class Gen, class Out>
+__device__ int block_select(RowShared& sh, Gen&& gen, int n, int want, Out&& out) {
+    const int tid = threadIdx.x;
+    const int lane = tid & 31;
+    int c = 0;
+    for (int i = tid; i < n; i += kThreads) c += gen(i) != 0 ? 1 : 0;
+    const int total = block_sum(sh, c);
+    uint64_t prefix = 0, mask = 0;
+    const bool take_all = total <= want;
+    if (!take_all) {
+        if (tid == 0) {
+            sh.sel_prefix = 0;
+            sh.sel_mask = 0;
+            sh.remaining = want;
+            sh.done = 0;
+        }
+        for (int shift = 56; shift >= 0; shift -= 8) {
+            sh.hist[tid] = 0;
+            __syncthreads();
+            prefix = sh.sel_prefix;
+            mask = sh.sel_mask;
+            for (int base = 0; base < n; base += kThreads) {
+                const int i = base + tid;
+                const uint64_t key = i < n ? gen(i) : 0;
+                const bool in = key != 0 && (key & mask) == prefix;
+                const int digit = in ? static_cast<int>((key >> shift) & 255u) : 256;
+                const unsigned peers = __match_any_sync(0xffffffffu, digit);
+                if (in && lane == __ffs(peers) - 1) atomicAdd(&sh.hist[digit], __popc(peers));
+            }
+            __syncthreads();
+            if (tid == 0) {
+                int rem = sh.remaining;
+                int d = 255;
+                while (d > 0 && sh.hist[d] < rem) rem -= sh.hist[d--];
+                sh.sel_prefix |= static_cast<unsigned long long>(d) << shift;
+                sh.sel_mask |= 255ull << shift;
+                sh.remaining = rem;
+                sh.done = sh.hist[d] == rem;
+            }
+            __syncthreads();
+            if (sh.done) break;
+        }
+        prefix = sh.sel_prefix;
+        mask = sh.sel_mask;
+    }
+    if (tid == 0) sh.count = 0;
+    __syncthreads();
+    for (int base = 0; base < n; base += kThreads) {
+        const int i = base + tid;
+        const uint64_t key = i < n ? gen(i) : 0;
+        const bool take = key != 0 && (take_all || (key & mask) >= prefix);
+        const unsigned ballot = __ballot_sync(0xffffffffu, take);
+        int pos0 = 0;
+        if (lane == 0 && ballot) pos0 = atomicAdd(&sh.count, __popc(ballot));
+        pos0 = __shfl_sync(0xffffffffu, pos0, 0);
+        if (take) {
+            const int pos = pos0 + __popc(ballot & ((1u << lane) - 1u));
+            if (pos < want) out(pos, key);
+        }
+    }
+    __syncthreads();
+    const int count = sh.count < want ? sh.count : want;
+    __syncthreads();
+    return count;
+}
+
+// Bitonic sort (descending) of n = power of two keys in shared memory.
+__device__ __forceinline__ void bitonic_desc(uint64_t* keys, int n) {
+    for (int k = 2; k <= n; k <<= 1) {
+        for (int j = k >> 1; j > 0; j >>= 1) {
+            for (int i = threadIdx.x; i < n; i += kThreads) {
+                const int partner = i ^ j;
+                if (partner > i) {
+                    const uint64_t a = keys[i], b = keys[partner];
+                    const bool up = (i & k) == 0;
+                    if (up ? (a < b) : (a > b)) {
+                        keys[i] = b;
+                        keys[partner] = a;
+                    }
+                }
+            }
+            __syncthreads();
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Constraint sets of one parent row (n-gram blocking, repetition penalty),
+// src/decoder.cpp:196-258 of beamgrad 2.3.0: sorted token lists in shared
+// memory. Prefixes longer than kConsCap fall back to scanning the prefix.
+// ---------------------------------------------------------------------------
+struct ConsView {
+    const int32_t* prefix;  // the parent's prefix
+    int L;
+    bool in_smem;
+};
+
+__device__ __forceinline__ void sort_small(int32_t* a, int n) {
+    // odd-even transposition sort, n <= kConsCap, all threads
+    for (int phase = 0; phase < n; ++phase) {
+        for (int i = 2 * threadIdx.x + (phase & 1); i + 1 < n; i += 2 * kThreads) {
+            if (a[i] > a[i + 1]) {
+                const int32_t t = a[i];
+                a[i] = a[i + 1];
+                a[i + 1] = t;
+            }
+        }
+        __syncthreads();
+    }
+}
+
+__device__ __forceinline__ bool ngram_match_at(const int32_t* pre, int L, int n, int i) {
+    const int suffix = L - (n - 1);
+    for (int j = 0; j < n - 1; ++j)
+        if (pre[i + j] != pre[suffix + j]) return false;
+    return true;
+}
+
+__device__ ConsView build_constraints(const DecodeParams& p, RowShared& sh, const int32_t* pre, int L) {
+    ConsView cv{pre, L, L <= kConsCap};
+    if (threadIdx.x == 0) {
+        sh.n_blocked = 0;
+        sh.n_penal = 0;
+    }
+    __syncthreads();
+    if (!cv.in_smem) return cv;
+    const int n = p.ngram;
+    if (n == 1) {
+        for (int i = threadIdx.x; i < L; i += kThreads) {
+            const int tok = ld_cg(pre + i);
+            if (tok >= 0 && tok < p.V) sh.blocked[atomicAdd(&sh.n_blocked, 1)] = tok;
+        }
+    } else if (n > 1 && L >= n - 1) {
+        for (int i = threadIdx.x; i + n <= L; i += kThreads) {
+            if (ngram_match_at(pre, L, n, i)) {
+                const int tok = ld_cg(pre + i + n - 1);
+                if (tok >= 0 && tok < p.V) sh.blocked[atomicAdd(&sh.n_blocked, 1)] = tok;
+            }
+        }
+    }
+    if (p.penalise) {
+        for (int i = threadIdx.x; i < L; i += kThreads) {
+            const int tok = ld_cg(pre + i);
+            if (tok >= 0 && tok < p.V) sh.penal[atomicAdd(&sh.n_penal, 1)] = tok;
+        }
+    }
+    __syncthreads();
+    sort_small(sh.blocked, sh.n_blocked);
+    sort_small(sh.penal, sh.n_penal);
+    return cv;
+}
+
+__device__ __forceinline__ bool sorted_has(const int32_t* a, int n, int v) {
+    int lo = 0, hi = n;
+    while (lo < hi) {
+        const int mid = (lo + hi) >> 1;
+        if (a[mid] < v) lo = mid + 1;
+        else hi = mid;
+    }
+    return lo < n && a[lo] == v;
+}
+
+__device__ __forceinline__ bool cons_blocked(const DecodeParams& p, const RowShared& sh, const ConsView& cv, int v) {
+    if (cv.in_smem) return sorted_has(sh.blocked, sh.n_blocked, v);
+    const int n = p.ngram;
+    if (n == 1) {
+        for (int i = 0; i < cv.L; ++i)
+            if (ld_cg(cv.prefix + i) == v) return true;
+        return false;
+    }
+    if (n > 1 && cv.L >= n - 1) {
+        for (int i = 0; i + n <= cv.L; ++i)
+            if (ld_cg(cv.prefix + i + n - 1) == v && ngram_match_at(cv.prefix, cv.L, n, i)) return true;
+    }
+    return false;
+}
+
+__device__ __forceinline__ bool cons_penalised(const DecodeParams& p, const RowShared& sh, const ConsView& cv, int v) {
+    if (!p.penalise) return false;
+    if (cv.in_smem) return sorted_has(sh.penal, sh.n_penal, v);
+    for (int i = 0; i < cv.L; ++i)
+        if (ld_cg(cv.prefix + i) == v) return true;
+    return false;
+}
+
+// ---------------------------------------------------------------------------
+// Candidate evaluation of one entry of a parent row.
+// ---------------------------------------------------------------------------
+struct RowCtx {
+    float pr;        // parent raw score
+    int new_len;     // parent length + 1
+    int k;           // parent slot
+    bool mask_eos;   // EOS tokens are masked (new_len < min_length)
+    bool constrained;
+    ConsView cv;
+    Meta m;
+};
+
+// The full key of entry v with log-probability lp (finite), or 0 when the entry
+// is not a candidate. The caller has already rejected NaN / +inf / -inf.
+__device__ __forceinline__ uint64_t full_key(const DecodeParams& p, const RowShared& sh, const RowCtx& c, float lp,
+                                             int v) {
+    if (p.banned && p.banned[v]) return 0;
+    if (c.mask_eos && is_eos(p, c.m, v)) return 0;
+    float value = lp;
+    if (c.constrained) {
+        if (cons_blocked(p, sh, c.cv, v)) return 0;
+        if (cons_penalised(p, sh, c.cv, v)) value = __fsub_rn(lp, p.log_penalty);
+    }
+    const float raw = __fadd_rn(c.pr, value);
+    if (raw == f_ninf()) return 0;
+    return make_key(raw, static_cast<uint32_t>(c.k) * static_cast<uint32_t>(p.V) + static_cast<uint32_t>(v));
+}
+
+// ---------------------------------------------------------------------------
+// Selection of example b at step t (run by the CTA that finished its last row).
+// ---------------------------------------------------------------------------
+template <int KMAX, int KCAP>
+__device__ void select_step(const DecodeParams& p, RowShared& sh, SelectShared<KCAP>& ss, int t, int b, const Meta& m) {
+    const int tid = threadIdx.x;
+    const int K = p.K;
+    const int V = p.V;
+    const int64_t sbase = static_cast<int64_t>(b) * K;
+    const int64_t obase = (static_cast<int64_t>(b) * p.T + t) * K;
+    const bool active = t < m.steps;
+    const bool last_step = p.step_api ? true : (t == p.T - 1);
+
+    // Snapshot of the state before this step.
+    for (int k = tid; k < m.beam; k += kThreads) {
+        ss.s_raw[k] = ld_cg(p.raw + sbase + k);
+        ss.s_len[k] = ld_cg(p.len + sbase + k);
+        ss.s_ended[k] = ld_cg(p.ended + sbase + k);
+        int last = -1;
+        if (p.step_api) {
+            const int L = ss.s_len[k];
+            if (p.caller_prefix && L >= 1 && L <= p.prefix_stride)
+                last = ld_cg(p.caller_prefix + (sbase + k) * p.prefix_stride + L - 1);
+        } else {
+            last = ld_cg(p.last + sbase + k);
+        }
+        ss.s_last[k] = last;
+    }
+    __syncthreads();
+
+    int filled = 0;
+    if (active) {
+        // 1. The step's best m.beam scanned keys, sorted descending.
+        int ns = 0;
+        const uint64_t* lists = p.keys + sbase * p.list_len;
+        if constexpr (KMAX > 0) {
+            if (tid < 32) {
+                constexpr int kPer = (kFastBeam * kFastBeam) / 32;
+                const int n = K * KMAX;
+                uint64_t mine[kPer];
+#pragma unroll
+                for (int j = 0; j < kPer; ++j) {
+                    const int i = tid + 32 * j;
+                    mine[j] = i < n ? ld_cg(lists + i) : 0;
+                }
+                int r = 0;
+                for (; r < m.beam; ++r) {
+                    uint64_t best = 0;
+#pragma unroll
+                    for (int j = 0; j < kPer; ++j) best = mine[j] > best ? mine[j] : best;
+                    const uint64_t w = warp_max_u64(best);
+                    if (w == 0) break;
+#pragma unroll
+                    for (int j = 0; j < kPer; ++j)
+                        if (mine[j] == w) mine[j] = 0;
+                    if (tid == 0) ss.keys[r] = w;
+                }
+                if (tid == 0) sh.n_scanned = r;
+            }
+            __syncthreads();
+            ns = sh.n_scanned;
+        } else {
+            const int n = K * p.list_len;
+            ns = block_select(
+                sh, [&](int i) { return ld_cg(lists + i); }, n, m.beam, [&](int pos, uint64_t key) { ss.keys[pos] = key; });
+            int n2 = 1;
+            while (n2 < ns) n2 <<= 1;
+            for (int i = ns + tid; i < n2; i += kThreads) ss.keys[i] = 0;
+            __syncthreads();
+            bitonic_desc(ss.keys, n2);
+        }
+        // 2. Scanned candidates' scores; carried-forward finished beams.
+        for (int i = tid; i < ns; i += kThreads) {
+            const uint32_t index = key_index(ss.keys[i]);
+            const int parent = static_cast<int>(index / static_cast<uint32_t>(V));
+            const float inv = __fdiv_rn(1.0f, gnmt_penalty(ss.s_len[parent] + 1, p.alpha));
+            ss.sc_score[i] = __fmul_rn(key_raw(ss.keys[i]), inv);
+        }
+        if (tid == 0) sh.n_carry = 0;
+        __syncthreads();
+        if (m.eos >= 0) {
+            for (int q = tid; q < m.beam; q += kThreads) {
+                const float raw = ss.s_raw[q];
+                if (ss.s_ended[q] && f_finite(raw)) {
+                    const int l = ss.s_len[q] > 1 ? ss.s_len[q] : 1;
+                    const int j = atomicAdd(&sh.n_carry, 1);
+                    ss.c_score[j] = __fdiv_rn(raw, gnmt_penalty(l, p.alpha));
+                    ss.c_raw[j] = raw;
+                    ss.c_parent[j] = q;
+                    ss.c_len[j] = l;
+                    const int last = ss.s_last[q];
+                    ss.c_token[j] = (last >= 0 && last < V && is_eos(p, m, last)) ? last : m.eos;
+                }
+            }
+        }
+        __syncthreads();
+        const int nc = sh.n_carry;
+        // 3. Merge by counting (every candidate is unique under the full order,
+        //    src/common.hpp:269-276).
+        auto better = [](float as, float ar, int ap, int at, int al, int af, float bs, float br, int bp, int bt, int bl,
+                         int bf) {
+            if (as != bs) return as > bs;
+            if (ar != br) return ar > br;
+            if (ap != bp) return ap < bp;
+            if (at != bt) return at < bt;
+            if (al != bl) return al < bl;
+            return af > bf;
+        };
+        for (int i = tid; i < ns + nc; i += kThreads) {
+            float cs, cr;
+            int cp, ct, cl, cf;
+            int pos;
+            if (i < ns) {
+                const uint32_t index = key_index(ss.keys[i]);
+                cp = static_cast<int>(index / static_cast<uint32_t>(V));
+                ct = static_cast<int>(index - static_cast<uint32_t>(cp) * static_cast<uint32_t>(V));
+                cs = ss.sc_score[i];
+                cr = key_raw(ss.keys[i]);
+                cl = ss.s_len[cp] + 1;
+                cf = 1;
+                pos = i;
+                for (int j = 0; j < nc; ++j)
+                    pos += better(ss.c_score[j], ss.c_raw[j], ss.c_parent[j], ss.c_token[j], ss.c_len[j], 0, cs, cr, cp,
+                                  ct, cl, cf);
+            } else {
+                const int j0 = i - ns;
+                cs = ss.c_score[j0];
+                cr = ss.c_raw[j0];
+                cp = ss.c_parent[j0];
+                ct = ss.c_token[j0];
+                cl = ss.c_len[j0];
+                cf = 0;
+                pos = 0;
+                for (int j = 0; j < nc; ++j)
+                    pos += (j != j0) && better(ss.c_score[j], ss.c_raw[j], ss.c_parent[j], ss.c_token[j], ss.c_len[j], 0,
+                                               cs, cr, cp, ct, cl, cf);
+                for (int j = 0; j < ns; ++j) {
+                    const uint32_t index = key_index(ss.keys[j]);
+                    const int sp = static_cast<int>(index / static_cast<uint32_t>(V));
+                    const int st = static_cast<int>(index - static_cast<uint32_t>(sp) * static_cast<uint32_t>(V));
+                    pos += better(ss.sc_score[j], key_raw(ss.keys[j]), sp, st, ss.s_len[sp] + 1, 1, cs, cr, cp, ct, cl, cf);
+                }
+            }
+            if (pos < m.beam) {
+                ss.o_parent[pos] = cp;
+                ss.o_token[pos] = ct;
+                ss.o_len[pos] = cl;
+                ss.o_score[pos] = cs;
+                ss.o_raw[pos] = cr;
+                ss.o_from[pos] = static_cast<uint8_t>(cf);
+            }
+        }
+        filled = ns + nc < m.beam ? ns + nc : m.beam;
+        __syncthreads();
+    }
+
+    // 4. Emit the step's slots and the new state.
+    const int cur = t & 1, nxt = (t + 1) & 1;
+    for (int k = tid; k < K; k += kThreads) {
+        const int64_t o = obase + k;
+        const int64_t s = sbase + k;
+        if (k < filled) {
+            const int par = ss.o_parent[k];
+            const int tok = ss.o_token[k];
+            if (p.out.tokens) p.out.tokens[o] = tok;
+            if (p.out.parents) p.out.parents[o] = par;
+            if (p.out.lengths) p.out.lengths[o] = ss.o_len[k];
+            if (p.out.scores) p.out.scores[o] = ss.o_score[k];
+            if (p.out.raw_scores) p.out.raw_scores[o] = ss.o_raw[k];
+            if (p.out.from_logprob) p.out.from_logprob[o] = ss.o_from[k];
+            p.raw[s] = ss.o_raw[k];
+            p.len[s] = ss.o_len[k];
+            p.ended[s] = static_cast<uint8_t>(ss.o_from[k] ? (ss.s_ended[par] != 0 || is_eos(p, m, tok)) : 1);
+            if (!p.step_api) p.last[s] = tok;
+        } else {
+            if (p.out.tokens) p.out.tokens[o] = -1;
+            if (p.out.parents) p.out.parents[o] = -1;
+            if (p.out.lengths) p.out.lengths[o] = 0;
+            if (p.out.scores) p.out.scores[o] = f_ninf();
+            if (p.out.raw_scores) p.out.raw_scores[o] = f_ninf();
+            if (p.out.from_logprob) p.out.from_logprob[o] = 0;
+            if (active) {
+                p.raw[s] = f_ninf();
+                p.len[s] = 0;
+                p.ended[s] = 0;
+                if (!p.step_api) p.last[s] = -1;
+            }
+        }
+    }
+    // Prefixes of the new hypotheses (decode with constraints): parent's, plus the emitted token.
+    if (active && p.prefix[0] && !p.step_api) {
+        const int T = p.T;
+        for (int k = 0; k < K; ++k) {
+            int32_t* dst = p.prefix[nxt] + (sbase + k) * T;
+            if (k < filled) {
+                const int par = ss.o_parent[k];
+                const int32_t* src = p.prefix[cur] + (sbase + par) * T;
+                const int L = ld_cg(p.prefix_len[cur] + sbase + par);
+                for (int i = tid; i < L; i += kThreads) dst[i] = ld_cg(src + i);
+                const bool append = ss.o_from[k] && ss.o_token[k] >= 0 && L < T;
+                if (tid == 0) {
+                    if (append) dst[L] = ss.o_token[k];
+                    p.prefix_len[nxt][sbase + k] = L + (append ? 1 : 0);
+                }
+            } else if (tid == 0) {
+                p.prefix_len[nxt][sbase + k] = 0;
+            }
+        }
+    } else if (!active && p.prefix[0] && !p.step_api) {
+        // Inactive step: carry the prefixes over unchanged.
+        const int T = p.T;
+        for (int k = 0; k < K; ++k) {
+            const int L = ld_cg(p.prefix_len[cur] + sbase + k);
+            for (int i = tid; i < L; i += kThreads)
+                p.prefix[nxt][(sbase + k) * T + i] = ld_cg(p.prefix[cur] + (sbase + k) * T + i);
+            if (tid == 0) p.prefix_len[nxt][sbase + k] = L;
+        }
+    }
+    __syncthreads();
+    // 5. Final scores after the last step.
+    if (last_step && p.out.final_scores) {
+        for (int k = tid; k < K; k += kThreads) {
+            const int64_t s = sbase + k;
+            float raw = f_ninf(), score = f_ninf();
+            int len = 0;
+            if (k < m.beam) {
+                raw = p.raw[s];
+                len = p.len[s];
+                score = __fdiv_rn(raw, gnmt_penalty(len, p.alpha));
+            }
+            p.out.final_scores[s] = score;
+            if (p.out.final_raw_scores) p.out.final_raw_scores[s] = raw;
+            if (p.out.final_lengths) p.out.final_lengths[s] = len;
+        }
+    }
+    __syncthreads();
+}
+
+// ---------------------------------------------------------------------------
+// The persistent decode kernel.
+// ---------------------------------------------------------------------------
+template <int DT, bool LOGITS, int KMAX>
+__global__ void __launch_bounds__(kThreads) decode_kernel(const __grid_constant__ DecodeParams p) {
+    constexpr int KCAP = KMAX > 0 ? kFastBeam : kSelectCap;
+    using E = Elem<DT>;
+    constexpr int EB = E::kBytes;
+    __shared__ RowShared sh;
+    extern __shared__ __align__(128) unsigned char dyn[];
+    auto& ss = *reinterpret_cast<SelectShared<KCAP>*>(dyn);
+    char* srow = reinterpret_cast<char*>(dyn) + ((sizeof(SelectShared<KCAP>) + 127) & ~static_cast<size_t>(127));
+
+    const int tid = threadIdx.x;
+    const int lane = tid & 31;
+    const int warp = tid >> 5;
+    if (tid == 0) mbar_init(&sh.mbar);
+    __syncthreads();
+    uint32_t phase = 0;
+
+    const int K = p.K, V = p.V;
+    const uint32_t rows_per_step = static_cast<uint32_t>(p.B) * static_cast<uint32_t>(K);
+    const uint32_t total = rows_per_step * static_cast<uint32_t>(p.T);
+
+    for (;;) {
+        if (tid == 0) sh.ticket = static_cast<int>(atomicAdd(p.ticket, 1u));
+        __syncthreads();
+        const uint32_t tk = static_cast<uint32_t>(sh.ticket);
+        if (tk >= total) break;
+        const int t = static_cast<int>(tk / rows_per_step);
+        const uint32_t rem = tk - static_cast<uint32_t>(t) * rows_per_step;
+        const int b = static_cast<int>(rem / static_cast<uint32_t>(K));
+        const int k = static_cast<int>(rem - static_cast<uint32_t>(b) * static_cast<uint32_t>(K));
+        const Meta m = load_meta(p, b);
+
+        if (tid == 0) sh.is_last = wait_flag(p, p.flag + b, t) ? 0 : -1;
+        __syncthreads();
+        if (sh.is_last < 0) break;  // timed out or aborted
+
+        const int64_t s = static_cast<int64_t>(b) * K + k;
+        const int64_t rowi = (static_cast<int64_t>(b) * p.T + t) * K + k;
+        bool read = false;
+        float pr = 0.0f;
+        int plen = 0;
+        if (t < m.steps && k < m.beam) {
+            pr = ld_cg(p.raw + s);
+            plen = ld_cg(p.len + s);
+            const uint8_t ended = ld_cg(p.ended + s);
+            read = f_finite(pr) && !(m.eos >= 0 && ended != 0);
+        }
+        uint64_t* list = p.keys + s * p.list_len;
+        if (!read) {
+            for (int i = tid; i < p.list_len; i += kThreads) list[i] = 0;
+            if (tid == 0 && p.row_lse) p.row_lse[rowi] = 0.0f;
+        } else {
+            RowCtx c;
+            c.pr = pr;
+            c.new_len = plen + 1;
+            c.k = k;
+            c.m = m;
+            c.mask_eos = m.eos >= 0 && c.new_len < m.min_length;
+            c.constrained = p.ngram > 0 || p.penalise;
+            c.cv = ConsView{nullptr, 0, true};
+            if (c.constrained) {
+                const int32_t* pre;
+                int L;
+                if (p.step_api) {
+                    pre = p.caller_prefix ? p.caller_prefix + s * p.prefix_stride : nullptr;
+                    L = plen < 0 ? 0 : (plen > p.prefix_stride ? p.prefix_stride : plen);
+                    if (!pre) L = 0;
+                } else {
+                    pre = p.prefix[t & 1] + s * p.T;
+                    L = ld_cg(p.prefix_len[t & 1] + s);
+                }
+                c.cv = build_constraints(p, sh, pre, L);
+            }
+            const char* grow = static_cast<const char*>(p.inputs) + rowi * static_cast<int64_t>(V) * EB;
+            float lse = 0.0f;
+            bool invalid = false;
+            const char* src = grow;  // where passes read the row
+            bool has_cands = true;
+            if constexpr (LOGITS) {
+                bool ok = true;
+                if (p.staged) src = srow + stage_row<EB>(p, sh, srow, grow, V, phase, ok);
+                if (!ok) break;
+                // Pass 1: maximum over entries below +inf, and the NaN/+inf flag.
+                float mx = f_ninf();
+                auto pass1 = [&](float x, int) {
+                    if (x < f_inf()) mx = fmaxf(mx, x);
+                    else invalid = true;
+                };
+                if (p.staged) for_row<DT, false>(src, V, pass1);
+                else for_row<DT, true>(src, V, pass1);
+                mx = block_max(sh, mx);
+                const int any_invalid = block_sum(sh, invalid ? 1 : 0);
+                invalid = any_invalid != 0;
+                lse = f_ninf();
+                if (mx != f_ninf()) {
+                    // Pass 2: lane tid sums exp(x - max) over v = tid (mod 256) in increasing v.
+                    const auto* er = reinterpret_cast<const typename E::T*>(src);
+                    float acc = 0.0f;
+                    if (!invalid) {
+                        int v = tid;
+                        for (; v + 3 * kLanes < V; v += 4 * kLanes) {
+                            const float d0 = __fsub_rn(E::to_f32(er[v]), mx);
+                            const float d1 = __fsub_rn(E::to_f32(er[v + kLanes]), mx);
+                            const float d2 = __fsub_rn(E::to_f32(er[v + 2 * kLanes]), mx);
+                            const float d3 = __fsub_rn(E::to_f32(er[v + 3 * kLanes]), mx);
+                            const float e0 = d0 >= cephes::kMin ? exp_nonpositive_fast(d0) : 0.0f;
+                            const float e1 = d1 >= cephes::kMin ? exp_nonpositive_fast(d1) : 0.0f;
+                            const float e2 = d2 >= cephes::kMin ? exp_nonpositive_fast(d2) : 0.0f;
+                            const float e3 = d3 >= cephes::kMin ? exp_nonpositive_fast(d3) : 0.0f;
+                            acc = __fadd_rn(acc, e0);
+                            acc = __fadd_rn(acc, e1);
+                            acc = __fadd_rn(acc, e2);
+                            acc = __fadd_rn(acc, e3);
+                        }
+                        for (; v < V; v += kLanes) {
+                            const float d = __fsub_rn(E::to_f32(er[v]), mx);
+                            acc = __fadd_rn(acc, d >= cephes::kMin ? exp_nonpositive_fast(d) : 0.0f);
+                        }
+                    } else {
+                        for (int v = tid; v < V; v += kLanes) {
+                            const float x = E::to_f32(er[v]);
+                            if (x < f_inf() && x != f_ninf()) acc = __fadd_rn(acc, exp_nonpositive(__fsub_rn(x, mx)));
+                        }
+                    }
+                    sh.lanes[tid] = acc;
+                    __syncthreads();
+#pragma unroll
+                    for (int st = kLanes / 2; st >= 32; st >>= 1) {
+                        if (tid < st) sh.lanes[tid] = __fadd_rn(sh.lanes[tid], sh.lanes[tid + st]);
+                        __syncthreads();
+                    }
+                    if (tid < 32) {
+                        float x = sh.lanes[tid];
+#pragma unroll
+                        for (int st = 16; st >= 1; st >>= 1) {
+                            const float o = __shfl_down_sync(0xffffffffu, x, st);
+                            if (tid < st) x = __fadd_rn(x, o);
+                        }
+                        if (tid == 0) sh.lanes[0] = x;
+                    }
+                    __syncthreads();
+                    lse = logsumexp_from(mx, sh.lanes[0]);
+                    __syncthreads();
+                }
+                if (tid == 0 && p.row_lse) p.row_lse[rowi] = lse;
+                has_cands = lse != f_ninf();
+            } else {
+                if (tid == 0 && p.row_lse) p.row_lse[rowi] = 0.0f;
+            }
+
+            // Pass 3: candidate keys.
+            if constexpr (KMAX > 0) {
+                uint64_t best[KMAX];
+#pragma unroll
+                for (int j = 0; j < KMAX; ++j) best[j] = 0;
+                float thr = f_ninf();
+                auto consider = [&](float x, int v) {
+                    const float lp = LOGITS ? __fsub_rn(x, lse) : x;
+                    if (!(lp < f_inf())) {
+                        invalid = true;
+                        return;
+                    }
+                    const float raw = __fadd_rn(pr, lp);
+                    if (raw >= thr && lp != f_ninf()) {
+                        const uint64_t key = full_key(p, sh, c, lp, v);
+                        if (key > best[KMAX - 1]) {
+                            best[KMAX - 1] = key;
+#pragma unroll
+                            for (int j = KMAX - 1; j > 0; --j) {
+                                if (best[j] > best[j - 1]) {
+                                    const uint64_t tmp = best[j];
+                                    best[j] = best[j - 1];
+                                    best[j - 1] = tmp;
+                                }
+                            }
+                            if (best[KMAX - 1] != 0) thr = key_raw(best[KMAX - 1]);
+                        }
+                    }
+                };
+                if (has_cands) {
+                    if (LOGITS && p.staged) for_row<DT, false>(src, V, consider);
+                    else for_row<DT, true>(src, V, consider);
+                }
+                // Warp lists, then the CTA's list (the row's best KMAX keys).
+                const int R = m.beam < KMAX ? m.beam : KMAX;
+                for (int r = 0; r < R; ++r) {
+                    const uint64_t w = warp_max_u64(best[0]);
+                    if (best[0] == w && w != 0) {
+#pragma unroll
+                        for (int j = 0; j < KMAX - 1; ++j) best[j] = best[j + 1];
+                        best[KMAX - 1] = 0;
+                    }
+                    if (lane == 0) sh.wkeys[warp * KMAX + r] = w;
+                }
+                __syncthreads();
+                if (warp == 0) {
+                    constexpr int kPer = (kWarps * KMAX + 31) / 32;
+                    uint64_t mine[kPer];
+#pragma unroll
+                    for (int j = 0; j < kPer; ++j) {
+                        const int i = lane + 32 * j;
+                        const int w = i / KMAX, r = i - (i / KMAX) * KMAX;
+                        mine[j] = (i < kWarps * KMAX && r < R) ? sh.wkeys[i] : 0;
+                        (void)w;
+                    }
+                    for (int r = 0; r < KMAX; ++r) {
+                        uint64_t bst = 0;
+#pragma unroll
+                        for (int j = 0; j < kPer; ++j) bst = mine[j] > bst ? mine[j] : bst;
+                        const uint64_t w = r < R ? warp_max_u64(bst) : 0;
+#pragma unroll
+                        for (int j = 0; j < kPer; ++j)
+                            if (w != 0 && mine[j] == w) mine[j] = 0;
+                        if (lane == 0) list[r] = w;
+                    }
+                }
+                const int inv_any = block_sum(sh, invalid ? 1 : 0);
+                if (tid == 0 && inv_any && p.out.invalid_input) p.out.invalid_input[b] = 1;
+            } else {
+                // Generic beams: block radix select of the row's best min(beam, V) keys.
+                auto gen = [&](int v) -> uint64_t {
+                    const float x = load_elem<DT>(src, v);
+                    const float lp = LOGITS ? __fsub_rn(x, lse) : x;
+                    if (!(lp < f_inf()) || lp == f_ninf()) return 0;
+                    return full_key(p, sh, c, lp, v);
+                };
+                if (!LOGITS) {
+                    // NaN / +inf anywhere in the row.
+                    bool inv = false;
+                    for_row<DT, true>(src, V, [&](float x, int) { inv |= !(x < f_inf()); });
+                    invalid = inv;
+                }
+                int cnt = 0;
+                if (has_cands) cnt = block_select(sh, gen, V, m.beam, [&](int pos, uint64_t key) { list[pos] = key; });
+                for (int i = cnt + tid; i < p.list_len; i += kThreads) list[i] = 0;
+                const int inv_any = block_sum(sh, invalid ? 1 : 0);
+                if (tid == 0 && inv_any && p.out.invalid_input) p.out.invalid_input[b] = 1;
+            }
+        }
+
+        // Arrive; the last row of (t, b) selects.
+        __syncthreads();
+        if (tid == 0) {
+            __threadfence();
+            sh.is_last = atomicAdd(p.arrive + b, 1u) == static_cast<uint32_t>(K) - 1u ? 1 : 0;
+        }
+        __syncthreads();
+        if (sh.is_last) {
+            __threadfence();
+            select_step<KMAX, KCAP>(p, sh, ss, t, b, m);
+            if (tid == 0) {
+                p.arrive[b] = 0;
+                __threadfence();
+                st_release(p.flag + b, t + 1);
+            }
+        }
+        __syncthreads();
+    }
+}
+
+
+// Launch of one (dtype, logits) family: the beam size picks the register
+// top-k width (1..16) or the generic radix-select path.
+template <int DT, bool LOGITS, int KMAX>
+static cudaError_t launch_decode_as(const DecodeParams& p, cudaStream_t stream, int sm_count) {
+    constexpr int KCAP = KMAX > 0 ? kFastBeam : kSelectCap;
+    const size_t sel = (sizeof(SelectShared<KCAP>) + 127) & ~static_cast<size_t>(127);
+    const size_t dyn = sel + (p.staged ? static_cast<size_t>(p.row_smem) : 0);
+    auto kernel = decode_kernel<DT, LOGITS, KMAX>;
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(dyn));
+    if (e != cudaSuccess) return e;
+    int per_sm = 0;
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kThreads, dyn);
+    if (e != cudaSuccess) return e;
+    if (per_sm < 1) per_sm = 1;
+    const int64_t tickets = static_cast<int64_t>(p.B) * p.K * p.T;
+    int64_t grid = static_cast<int64_t>(sm_count) * per_sm;
+    if (grid > tickets) grid = tickets;
+    kernel<<<static_cast<unsigned>(grid), kThreads, dyn, stream>>>(p);
+    return cudaGetLastError();
+}
+
+template <int DT, bool LOGITS>
+static cudaError_t launch_decode_k(const DecodeParams& p, cudaStream_t stream, int sm_count) {
+    const int K = p.K;
+    if (K <= 1) return launch_decode_as<DT, LOGITS, 1>(p, stream, sm_count);
+    if (K <= 2) return launch_decode_as<DT, LOGITS, 2>(p, stream, sm_count);
+    if (K <= 4) return launch_decode_as<DT, LOGITS, 4>(p, stream, sm_count);
+    if (K <= 8) return launch_decode_as<DT, LOGITS, 8>(p, stream, sm_count);
+    if (K <= 16) return launch_decode_as<DT, LOGITS, 16>(p, stream, sm_count);
+    return launch_decode_as<DT, LOGITS, 0>(p, stream, sm_count);
+}
+
+}  // namespace
+}  // namespace dbsb

@@ -1,0 +1,183 @@
+// SPDX-License-Identifier: MIT
+//
+// Shared pieces of the B200 beam-search engine: launch parameters, bounded
+// inter-CTA waits, and block-level reductions.
+#pragma once
+
+#include <cstdint>
+#include <cuda_runtime.h>
+
+#include "dbs_cuda.h"
+#include "detmath.cuh"
+
+namespace dbsb {
+
+constexpr int kThreads = 256;          // threads per CTA of every row kernel (one per logsumexp lane)
+constexpr int kWarps = kThreads / 32;
+constexpr int kFastBeam = 16;          // largest beam of the register top-k path
+constexpr int kConsCap = 512;          // constraint tokens kept in shared memory per row
+constexpr int kSelectCap = 1024;       // largest beam of the generic select (DBS_CUDA_MAX_BEAM)
+
+// Error codes written to the workspace error word (never a GPU trap).
+constexpr int kErrNone = 0;
+constexpr int kErrTimeout = 1;         // a bounded wait gave up
+
+// Per-example settings (clamped into range; the host validates them first).
+struct Meta {
+    int steps;
+    int beam;
+    int eos;
+    int min_length;
+};
+
+// Everything the decode kernels need. Passed by value (kernel parameter space).
+struct DecodeParams {
+    // problem
+    int B, T, K, V;
+    int eos, min_length;
+    float alpha;
+    int ngram;
+    int penalise;
+    float log_penalty;      // logf(repetition_penalty), computed on the host as the CPU decoder does
+    int n_extra;            // extra EOS tokens (active for examples with EOS handling)
+    int32_t extra[DBS_CUDA_MAX_EXTRA_EOS];
+    const int32_t* steps_pe;
+    const int32_t* beams_pe;
+    const int32_t* eos_pe;
+    const int32_t* minlen_pe;
+    const uint8_t* banned;  // [V] or null
+    // input rows
+    const void* inputs;
+    int step_api;           // 1: one step from a caller-owned state (T == 1)
+    // beam state [B, K]
+    float* raw;
+    int32_t* len;
+    uint8_t* ended;
+    int32_t* last;          // token of each slot after the previous step (decode only)
+    // prefixes for n-gram blocking / repetition penalty
+    const int32_t* caller_prefix;  // step API: [B, K, prefix_stride]
+    int prefix_stride;
+    int32_t* prefix[2];            // decode: double-buffered [B, K, T]
+    int32_t* prefix_len[2];        // decode: [B, K]
+    // outputs
+    DBSCudaDecodeOutputs out;
+    float* row_lse;
+    // scratch
+    uint64_t* keys;         // [B, K, list_len] per-row candidate lists
+    int list_len;
+    uint32_t* arrive;       // [B] rows of the current step that finished
+    int32_t* flag;          // [B] steps whose selection is published
+    uint32_t* ticket;       // work-item counter
+    int32_t* error;         // error word
+    int staged;             // rows are staged in shared memory (from logits)
+    int row_smem;           // bytes of the shared-memory row buffer
+    unsigned long long timeout_ns;
+};
+
+// Everything the backward kernels need.
+struct BackwardParams {
+    int B, T, K, V;
+    float alpha;
+    const int32_t* steps_pe;
+    const int32_t* beams_pe;
+    const int32_t* parents;
+    const int32_t* tokens;
+    const int32_t* lengths;
+    const uint8_t* from_logprob;
+    const float* g_final;
+    const float* g_final_raw;
+    const float* g_scores;
+    const float* g_raw;
+    float* grad;    // dense [B, T, K, V] (+=), or null
+    float* draws;   // per slot [B, T, K], or null
+};
+
+__device__ __forceinline__ Meta load_meta(const DecodeParams& p, int b) {
+    Meta m;
+    m.steps = p.steps_pe ? p.steps_pe[b] : p.T;
+    m.beam = p.beams_pe ? p.beams_pe[b] : p.K;
+    m.eos = p.eos_pe ? p.eos_pe[b] : p.eos;
+    m.min_length = p.minlen_pe ? p.minlen_pe[b] : p.min_length;
+    m.steps = m.steps < 0 ? 0 : (m.steps > p.T ? p.T : m.steps);
+    m.beam = m.beam < 0 ? 0 : (m.beam > p.K ? p.K : m.beam);
+    if (m.eos < -1 || m.eos >= p.V) m.eos = -1;
+    return m;
+}
+
+__device__ __forceinline__ bool is_eos(const DecodeParams& p, const Meta& m, int token) {
+    if (m.eos < 0) return false;
+    if (token == m.eos) return true;
+    for (int i = 0; i < p.n_extra; ++i)
+        if (p.extra[i] == token) return true;
+    return false;
+}
+
+// ---------------------------------------------------------------------------
+// Memory-model helpers for the per-example step hand-off between CTAs.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ int ld_acquire(const int32_t* p) {
+    int v;
+    asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_release(int32_t* p, int v) {
+    asm volatile("st.release.gpu.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long global_ns() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+    return t;
+}
+
+// Waits until flag >= target. Bounded: after timeout_ns it records kErrTimeout
+// and returns false. Called by one thread.
+__device__ __forceinline__ bool wait_flag(const DecodeParams& p, const int32_t* flag, int target) {
+    if (ld_acquire(flag) >= target) return true;
+    const unsigned long long start = global_ns();
+    unsigned sleep = 32;
+    for (;;) {
+        if (ld_acquire(flag) >= target) return true;
+        if (ld_acquire(p.error) != kErrNone) return false;
+        if (global_ns() - start > p.timeout_ns) {
+            atomicCAS(p.error, kErrNone, kErrTimeout);
+            return false;
+        }
+        __nanosleep(sleep);
+        if (sleep < 1024) sleep <<= 1;
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Block-level helpers (kThreads threads).
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint64_t shfl_xor_u64(uint64_t v, int m) {
+    const uint32_t lo = __shfl_xor_sync(0xffffffffu, static_cast<uint32_t>(v), m);
+    const uint32_t hi = __shfl_xor_sync(0xffffffffu, static_cast<uint32_t>(v >> 32), m);
+    return (static_cast<uint64_t>(hi) << 32) | lo;
+}
+__device__ __forceinline__ uint64_t warp_max_u64(uint64_t v) {
+#pragma unroll
+    for (int m = 16; m > 0; m >>= 1) {
+        const uint64_t o = shfl_xor_u64(v, m);
+        v = o > v ? o : v;
+    }
+    return v;
+}
+__device__ __forceinline__ float warp_max_f32(float v) {
+#pragma unroll
+    for (int m = 16; m > 0; m >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, m));
+    return v;
+}
+__device__ __forceinline__ int warp_sum_i32(int v) {
+#pragma unroll
+    for (int m = 16; m > 0; m >>= 1) v += __shfl_xor_sync(0xffffffffu, v, m);
+    return v;
+}
+
+// Global loads of data another CTA wrote during this launch: served by L2.
+template <class T>
+__device__ __forceinline__ T ld_cg(const T* p) {
+    return __ldcg(p);
+}
+
+}  // namespace dbsb

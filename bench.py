@@ -1,0 +1,341 @@
+# SPDX-License-Identifier: MIT
+"""Benchmark of the fused decode on BASELINE configs[1]:
+bf16 logits [B=64, T=128, K=8, V=32000] = N(0, 2) + Zipf(s=1.1) per-token bias, from_logits,
+eos=2, length-penalty alpha=1.0 -- decoded through the engine's C ABI (dbs_cuda_decode_ex2).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+One JSON line on rank 0. `value` is whole-job candidates/s (B*T*K*V per decode, all ranks)
+with inputs resident in HBM; `e2e` is the same metric through the same C-ABI call with the
+inputs in pinned host memory, copied in and the outputs copied out inside the timed region.
+Under torchrun each rank decodes its own batch of the config (weak scaling, no collective on
+the data path). `--impl reference` times the reference's own CPU implementation (libdbs,
+oracle/_ref/libdbs.so) with every host thread on the same config.
+"""
+
+from __future__ import annotations
+
+import argparse
+import ctypes as C
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+B, T, K, V = 64, 128, 8, 32000
+EOS, ALPHA = 2, 1.0
+METRIC = "beam candidates/s (B·T·K·V) and HBM GB/s vs roofline at 1/2/4/8 B200"
+WORKLOAD = "C2: bf16 logits [64,128,8,32000] N(0,2)+Zipf(1.1) bias, from_logits, eos=2, alpha=1.0"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    return ap.parse_args()
+
+
+def peaks() -> tuple[float, str]:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi samples of SM clocks and throttle reasons during the timed region."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.rows: list[list[str]] = []
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.rows.append([c.strip() for c in line.split(",")])
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        if not self.rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(r[1]) for r in self.rows if len(r) > 2 and r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in self.rows if len(r) > 2 and r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = set()
+        for r in self.rows:
+            for i, n in enumerate(names):
+                if len(r) > 5 + i and r[5 + i].lower().startswith("active"):
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(self.rows)}
+
+
+def make_inputs(torch, seed: int, device):
+    g = torch.Generator(device=device).manual_seed(seed)
+    bias = -1.1 * torch.log(torch.randperm(V, generator=g, device=device).float() + 1.0)
+    x = torch.empty((B, T, K, V), dtype=torch.bfloat16, device=device)
+    for b in range(B):  # chunked: keeps the float32 temporary small
+        x[b] = (torch.randn((T, K, V), generator=g, device=device) * 2.0 + bias).to(torch.bfloat16)
+    return x
+
+
+def rows_read(tokens, parents, from_logprob, raw) -> int:
+    """Rows the search read: 1 per example at t = 0, then the live, unfinished slots of step t-1."""
+    live = (parents[:, :-1] >= 0) & (from_logprob[:, :-1] == 1) & (tokens[:, :-1] != EOS) & np.isfinite(raw[:, :-1])
+    return int(tokens.shape[0] + live.sum())
+
+
+def cpu_reference(x_host_bits: np.ndarray, threads: int, min_seconds: float = 10.0, max_reps: int = 5):
+    """The reference CPU decoder (libdbs, every host thread) on the whole workload; seconds per decode."""
+    from oracle import oracle
+    from beamgrad_b200 import _abi as A
+
+    pb = oracle.Problem(x_host_bits, dtype=A.DTYPE_BF16, from_logits=True, eos=EOS, alpha=ALPHA)
+    times = []
+    with oracle.RefDecoder(pb) as d:
+        start = time.perf_counter()
+        while len(times) < max_reps and (time.perf_counter() - start < min_seconds or len(times) < 1):
+            t0 = time.perf_counter()
+            d.decode(threads=threads)
+            times.append(time.perf_counter() - t0)
+    return statistics.median(times), len(times)
+
+
+def run_reference_arm(args, rank: int, world: int):
+    if rank != 0:
+        return
+    import torch
+    from oracle import oracle
+
+    if not oracle.ref_available():
+        print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/libdbs.so was not built"}))
+        return
+    threads = oracle.cpu_count()
+    x = make_inputs(torch, 1000, "cuda" if torch.cuda.is_available() else "cpu")
+    bits = x.view(torch.int16).cpu().numpy().view(np.uint16)
+    del x
+    per_step = []
+    for i in range(args.warmup + args.steps):
+        sec, _ = cpu_reference(bits, threads, min_seconds=0.0, max_reps=1)
+        if i >= args.warmup:
+            per_step.append(sec)
+    sec = statistics.median(per_step)
+    cand = B * T * K * V
+    value = cand / sec
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "candidates/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": sec * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": WORKLOAD, "global_batch": B, "seq_len": T, "beam": K, "vocab": V,
+                   "parallelism": "host threads"},
+        "cpu_baseline": {"value": value, "unit": "candidates/s", "cores": threads, "kind": "reference",
+                         "sample": f"full workload ({B} examples) per step, libdbs dbs_decode_batch_into_ex"},
+        "e2e": {"value": value, "unit": "candidates/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+def main():
+    args = parse()
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        return run_reference_arm(args, rank, world)
+
+    import torch
+
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+    from beamgrad_b200 import _abi as A
+
+    lib = A.load()
+    dev = torch.device("cuda", local)
+    x = make_inputs(torch, 1000 + rank, dev)
+
+    # Outputs and workspace allocated once.
+    f32, i32, u8 = torch.float32, torch.int32, torch.uint8
+    out = {
+        "final_scores": torch.empty((B, K), dtype=f32, device=dev),
+        "final_raw_scores": torch.empty((B, K), dtype=f32, device=dev),
+        "final_lengths": torch.empty((B, K), dtype=i32, device=dev),
+        "tokens": torch.empty((B, T, K), dtype=i32, device=dev),
+        "parents": torch.empty((B, T, K), dtype=i32, device=dev),
+        "lengths": torch.empty((B, T, K), dtype=i32, device=dev),
+        "scores": torch.empty((B, T, K), dtype=f32, device=dev),
+        "raw_scores": torch.empty((B, T, K), dtype=f32, device=dev),
+        "from_logprob": torch.empty((B, T, K), dtype=u8, device=dev),
+        "invalid_input": torch.empty((B,), dtype=u8, device=dev),
+    }
+    row_lse = torch.empty((B, T, K), dtype=f32, device=dev)
+    o = A.DecodeOutputs()
+    for k, v in out.items():
+        setattr(o, k, v.data_ptr())
+    a = A.DecodeArgs()
+    a.batch_size, a.steps, a.beam_size, a.vocab_size = B, T, K, V
+    a.eos_token, a.length_penalty_alpha, a.repetition_penalty = EOS, ALPHA, 1.0
+    ws_bytes = lib.dbs_cuda_decode_workspace_size(C.byref(a))
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def decode(inp) -> None:
+        rc = lib.dbs_cuda_decode_ex2(C.c_void_p(inp.data_ptr()), A.DTYPE_BF16, 1, C.byref(a), None, C.byref(o),
+                                     C.c_void_p(row_lse.data_ptr()), C.c_void_p(ws.data_ptr()), ws_bytes,
+                                     C.c_void_p(stream.cuda_stream))
+        A.check(rc, "decode")
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+
+    for _ in range(args.warmup):
+        decode(x)
+    barrier()
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    launch_ms = []
+    with ClockSampler(local) as clocks:
+        barrier()
+        start.record(stream)
+        for _ in range(args.steps):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            decode(x)
+            e1.record(stream)
+            launch_ms.append((e0, e1))
+        stop.record(stream)
+        barrier()
+    elapsed = start.elapsed_time(stop) / 1e3
+    per_launch = statistics.mean(e0.elapsed_time(e1) for e0, e1 in launch_ms) / 1e3
+    t_all = torch.tensor([elapsed], device=dev, dtype=torch.float64)
+    if dist is not None:
+        dist.all_reduce(t_all, op=dist.ReduceOp.MAX)
+    elapsed = float(t_all.item())
+
+    # Algorithmic bytes of one decode: every row the search read (V bf16 entries) + trace/state writes.
+    host = {k: v.cpu().numpy() for k, v in out.items()}
+    n_rows = rows_read(host["tokens"], host["parents"], host["from_logprob"], host["raw_scores"])
+    trace_bytes = B * T * K * (4 * 5 + 1) + B * T * K * 4 + B * K * 12
+    alg_bytes = n_rows * V * 2 + trace_bytes
+    peak, peak_kind = peaks()
+    achieved = alg_bytes / per_launch / 1e9
+
+    # End to end through the same C-ABI call: pinned host input -> device, decode, outputs -> host.
+    e2e = None
+    if not args.no_e2e:
+        xh = torch.empty(x.shape, dtype=x.dtype, pin_memory=True)
+        xh.copy_(x)
+        xd = torch.empty_like(x)
+        outs_h = {k: torch.empty(v.shape, dtype=v.dtype, pin_memory=True) for k, v in out.items()}
+        h2d = xh.numel() * xh.element_size()
+        d2h = sum(v.numel() * v.element_size() for v in outs_h.values())
+        e2e_steps = max(2, min(args.steps, 5))
+
+        def e2e_step():
+            xd.copy_(xh, non_blocking=True)
+            decode(xd)
+            for k, v in out.items():
+                outs_h[k].copy_(v, non_blocking=True)
+
+        e2e_step()
+        barrier()
+        s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s0.record(stream)
+        for _ in range(e2e_steps):
+            e2e_step()
+        s1.record(stream)
+        barrier()
+        e2e_t = torch.tensor([s0.elapsed_time(s1) / 1e3 / e2e_steps], device=dev, dtype=torch.float64)
+        if dist is not None:
+            dist.all_reduce(e2e_t, op=dist.ReduceOp.MAX)
+        e2e = {"value": world * B * T * K * V / float(e2e_t.item()), "unit": "candidates/s",
+               "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h}
+        del xh, xd
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        from oracle import oracle
+
+        if oracle.ref_available():
+            bits = x.view(torch.int16).cpu().numpy().view(np.uint16)
+            threads = oracle.cpu_count()
+            sec, reps = cpu_reference(bits, threads)
+            cpu = {"value": B * T * K * V / sec, "unit": "candidates/s", "cores": threads, "kind": "reference",
+                   "sample": f"the full workload ({B} examples), {reps} run(s) of libdbs dbs_decode_batch_into_ex"}
+
+    if dist is not None:
+        dist.barrier()
+    if rank == 0:
+        cand = world * B * T * K * V
+        line = {
+            "metric": METRIC,
+            "value": cand / elapsed * args.steps,
+            "unit": "candidates/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": elapsed / args.steps * 1e3,
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "bf16",
+            "data": "synthetic",
+            "config": {"workload": WORKLOAD, "global_batch": world * B, "seq_len": T, "beam": K, "vocab": V,
+                       "parallelism": f"batch x{world}" if world > 1 else "single GPU",
+                       "l2": "inputs (4.19 GB per GPU) larger than L2"},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "traffic": None, "peak_kind": peak_kind,
+                         "alg_bytes_per_launch": alg_bytes, "rows_read": n_rows},
+            "cpu_baseline": cpu,
+            "e2e": e2e,
+            "gpu_launches": 2 * args.steps,
+            "clocks": clocks.summary(),
+        }
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()
