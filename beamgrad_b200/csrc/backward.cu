@@ -35,7 +35,7 @@ __global__ void __launch_bounds__(kThreads) backward_kernel(const __grid_constan
     steps = steps < 0 ? 0 : (steps > p.T ? p.T : steps);
     Kb = Kb < 0 ? 0 : (Kb > K ? K : Kb);
     for (int k = tid; k < Kb; k += kThreads) next_g[k] = 0.0f;
-    __syncthreads();
+    block_sync();
     for (int t = steps - 1; t >= 0; --t) {
         const bool last = t == steps - 1;
         const int64_t base = (static_cast<int64_t>(b) * p.T + t) * K;
@@ -67,7 +67,7 @@ __global__ void __launch_bounds__(kThreads) backward_kernel(const __grid_constan
             draw_s[k] = d;
             par_s[k] = pq;
         }
-        __syncthreads();
+        block_sync();
         // prev[q] = sum of its children's draws in slot order, from 0.
         for (int q = tid; q < Kb; q += kThreads) {
             float sum = 0.0f;
@@ -75,9 +75,9 @@ __global__ void __launch_bounds__(kThreads) backward_kernel(const __grid_constan
                 if (par_s[k] == q) sum = __fadd_rn(sum, draw_s[k]);
             prev_g[q] = sum;
         }
-        __syncthreads();
+        block_sync();
         for (int k = tid; k < Kb; k += kThreads) next_g[k] = prev_g[k];
-        __syncthreads();
+        block_sync();
     }
 }
 
@@ -106,7 +106,7 @@ __global__ void __launch_bounds__(kThreads) logit_correction_kernel(const __grid
     const int64_t base = bt * K;
     const int tid = threadIdx.x;
     if (tid == 0) n_s = 0;
-    __syncthreads();
+    block_sync();
     for (int k = tid; k < Kb; k += kThreads) {
         const float d = p.draws[base + k];
         if (d != 0.0f && p.parents[base + k] == q) {
@@ -115,7 +115,7 @@ __global__ void __launch_bounds__(kThreads) logit_correction_kernel(const __grid
             val_s[i] = d;
         }
     }
-    __syncthreads();
+    block_sync();
     const int n = n_s;
     if (n == 0) return;
     if (tid == 0) {
@@ -136,7 +136,7 @@ __global__ void __launch_bounds__(kThreads) logit_correction_kernel(const __grid
         for (int i = 0; i < n; ++i) s = __fadd_rn(s, val_s[i]);
         sum_s = s;
     }
-    __syncthreads();
+    block_sync();
     const float S = sum_s;
     const float lse = row_lse[r];
     const int64_t V = p.V;

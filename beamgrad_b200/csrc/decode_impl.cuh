@@ -178,7 +178,7 @@ __device__ __forceinline__ int stage_row(const DecodeParams& p, RowShared& sh, c
         ok = mbar_wait(p, &sh.mbar, phase);
         phase ^= 1u;
     }
-    ok = __syncthreads_and(ok) != 0;
+    ok = block_and(ok);
     return off;
 }
 
@@ -247,21 +247,21 @@ __device__ __forceinline__ void for_row(const char* row, int V, F&& f) {
 __device__ __forceinline__ float block_max(RowShared& sh, float v) {
     v = warp_max_f32(v);
     if ((threadIdx.x & 31) == 0) sh.wred[threadIdx.x >> 5] = v;
-    __syncthreads();
+    block_sync();
     float r = sh.wred[0];
 #pragma unroll
     for (int w = 1; w < kWarps; ++w) r = fmaxf(r, sh.wred[w]);
-    __syncthreads();
+    block_sync();
     return r;
 }
 __device__ __forceinline__ int block_sum(RowShared& sh, int v) {
     v = warp_sum_i32(v);
     if ((threadIdx.x & 31) == 0) sh.ired[threadIdx.x >> 5] = v;
-    __syncthreads();
+    block_sync();
     int r = 0;
 #pragma unroll
     for (int w = 0; w < kWarps; ++w) r += sh.ired[w];
-    __syncthreads();
+    block_sync();
     return r;
 }
 
@@ -289,7 +289,7 @@ __device__ int block_select(RowShared& sh, Gen&& gen, int n, int want, Out&& out
         }
         for (int shift = 56; shift >= 0; shift -= 8) {
             sh.hist[tid] = 0;
-            __syncthreads();
+            block_sync();
             prefix = sh.sel_prefix;
             mask = sh.sel_mask;
             for (int base = 0; base < n; base += kThreads) {
@@ -300,7 +300,7 @@ __device__ int block_select(RowShared& sh, Gen&& gen, int n, int want, Out&& out
                 const unsigned peers = __match_any_sync(0xffffffffu, digit);
                 if (in && lane == __ffs(peers) - 1) atomicAdd(&sh.hist[digit], __popc(peers));
             }
-            __syncthreads();
+            block_sync();
             if (tid == 0) {
                 int rem = sh.remaining;
                 int d = 255;
@@ -310,14 +310,14 @@ __device__ int block_select(RowShared& sh, Gen&& gen, int n, int want, Out&& out
                 sh.remaining = rem;
                 sh.done = sh.hist[d] == rem;
             }
-            __syncthreads();
+            block_sync();
             if (sh.done) break;
         }
         prefix = sh.sel_prefix;
         mask = sh.sel_mask;
     }
     if (tid == 0) sh.count = 0;
-    __syncthreads();
+    block_sync();
     for (int base = 0; base < n; base += kThreads) {
         const int i = base + tid;
         const uint64_t key = i < n ? gen(i) : 0;
@@ -331,9 +331,9 @@ __device__ int block_select(RowShared& sh, Gen&& gen, int n, int want, Out&& out
             if (pos < want) out(pos, key);
         }
     }
-    __syncthreads();
+    block_sync();
     const int count = sh.count < want ? sh.count : want;
-    __syncthreads();
+    block_sync();
     return count;
 }
 
@@ -352,7 +352,7 @@ __device__ __forceinline__ void bitonic_desc(uint64_t* keys, int n) {
                     }
                 }
             }
-            __syncthreads();
+            block_sync();
         }
     }
 }
@@ -378,7 +378,7 @@ __device__ __forceinline__ void sort_small(int32_t* a, int n) {
                 a[i + 1] = t;
             }
         }
-        __syncthreads();
+        block_sync();
     }
 }
 
@@ -395,7 +395,7 @@ __device__ ConsView build_constraints(const DecodeParams& p, RowShared& sh, cons
         sh.n_blocked = 0;
         sh.n_penal = 0;
     }
-    __syncthreads();
+    block_sync();
     if (!cv.in_smem) return cv;
     const int n = p.ngram;
     if (n == 1) {
@@ -417,7 +417,7 @@ __device__ ConsView build_constraints(const DecodeParams& p, RowShared& sh, cons
             if (tok >= 0 && tok < p.V) sh.penal[atomicAdd(&sh.n_penal, 1)] = tok;
         }
     }
-    __syncthreads();
+    block_sync();
     sort_small(sh.blocked, sh.n_blocked);
     sort_small(sh.penal, sh.n_penal);
     return cv;
@@ -513,7 +513,7 @@ __device__ void select_step(const DecodeParams& p, RowShared& sh, SelectShared<K
         }
         ss.s_last[k] = last;
     }
-    __syncthreads();
+    block_sync();
 
     int filled = 0;
     if (active) {
@@ -544,7 +544,7 @@ __device__ void select_step(const DecodeParams& p, RowShared& sh, SelectShared<K
                 }
                 if (tid == 0) sh.n_scanned = r;
             }
-            __syncthreads();
+            block_sync();
             ns = sh.n_scanned;
         } else {
             const int n = K * p.list_len;
@@ -553,7 +553,7 @@ __device__ void select_step(const DecodeParams& p, RowShared& sh, SelectShared<K
             int n2 = 1;
             while (n2 < ns) n2 <<= 1;
             for (int i = ns + tid; i < n2; i += kThreads) ss.keys[i] = 0;
-            __syncthreads();
+            block_sync();
             bitonic_desc(ss.keys, n2);
         }
         // 2. Scanned candidates' scores; carried-forward finished beams.
@@ -564,7 +564,7 @@ __device__ void select_step(const DecodeParams& p, RowShared& sh, SelectShared<K
             ss.sc_score[i] = __fmul_rn(key_raw(ss.keys[i]), inv);
         }
         if (tid == 0) sh.n_carry = 0;
-        __syncthreads();
+        block_sync();
         if (m.eos >= 0) {
             for (int q = tid; q < m.beam; q += kThreads) {
                 const float raw = ss.s_raw[q];
@@ -580,7 +580,7 @@ __device__ void select_step(const DecodeParams& p, RowShared& sh, SelectShared<K
                 }
             }
         }
-        __syncthreads();
+        block_sync();
         const int nc = sh.n_carry;
         // 3. Merge by counting (every candidate is unique under the full order,
         //    src/common.hpp:269-276).
@@ -638,7 +638,7 @@ __device__ void select_step(const DecodeParams& p, RowShared& sh, SelectShared<K
             }
         }
         filled = ns + nc < m.beam ? ns + nc : m.beam;
-        __syncthreads();
+        block_sync();
     }
 
     // 4. Emit the step's slots and the new state.
@@ -703,7 +703,7 @@ __device__ void select_step(const DecodeParams& p, RowShared& sh, SelectShared<K
             if (tid == 0) p.prefix_len[nxt][sbase + k] = L;
         }
     }
-    __syncthreads();
+    block_sync();
     // 5. Final scores after the last step.
     if (last_step && p.out.final_scores) {
         for (int k = tid; k < K; k += kThreads) {
@@ -720,7 +720,8 @@ __device__ void select_step(const DecodeParams& p, RowShared& sh, SelectShared<K
             if (p.out.final_lengths) p.out.final_lengths[s] = len;
         }
     }
-    __syncthreads();
+    __threadfence();  // the new state, prefixes and trace, before the caller publishes the step
+    block_sync();
 }
 
 // ---------------------------------------------------------------------------
@@ -740,7 +741,7 @@ __global__ void __launch_bounds__(kThreads) decode_kernel(const __grid_constant_
     const int lane = tid & 31;
     const int warp = tid >> 5;
     if (tid == 0) mbar_init(&sh.mbar);
-    __syncthreads();
+    block_sync();
     uint32_t phase = 0;
 
     const int K = p.K, V = p.V;
@@ -749,7 +750,7 @@ __global__ void __launch_bounds__(kThreads) decode_kernel(const __grid_constant_
 
     for (;;) {
         if (tid == 0) sh.ticket = static_cast<int>(atomicAdd(p.ticket, 1u));
-        __syncthreads();
+        block_sync();
         const uint32_t tk = static_cast<uint32_t>(sh.ticket);
         if (tk >= total) break;
         const int t = static_cast<int>(tk / rows_per_step);
@@ -758,8 +759,11 @@ __global__ void __launch_bounds__(kThreads) decode_kernel(const __grid_constant_
         const int k = static_cast<int>(rem - static_cast<uint32_t>(b) * static_cast<uint32_t>(K));
         const Meta m = load_meta(p, b);
 
-        if (tid == 0) sh.is_last = wait_flag(p, p.flag + b, t) ? 0 : -1;
-        __syncthreads();
+        if (warp == 0) {
+            const bool ok = wait_flag_warp(p, p.flag + b, t);
+            if (lane == 0) sh.is_last = ok ? 0 : -1;
+        }
+        block_sync();
         if (sh.is_last < 0) break;  // timed out or aborted
 
         const int64_t s = static_cast<int64_t>(b) * K + k;
@@ -851,11 +855,11 @@ __global__ void __launch_bounds__(kThreads) decode_kernel(const __grid_constant_
                         }
                     }
                     sh.lanes[tid] = acc;
-                    __syncthreads();
+                    block_sync();
 #pragma unroll
                     for (int st = kLanes / 2; st >= 32; st >>= 1) {
                         if (tid < st) sh.lanes[tid] = __fadd_rn(sh.lanes[tid], sh.lanes[tid + st]);
-                        __syncthreads();
+                        block_sync();
                     }
                     if (tid < 32) {
                         float x = sh.lanes[tid];
@@ -866,9 +870,9 @@ __global__ void __launch_bounds__(kThreads) decode_kernel(const __grid_constant_
                         }
                         if (tid == 0) sh.lanes[0] = x;
                     }
-                    __syncthreads();
+                    block_sync();
                     lse = logsumexp_from(mx, sh.lanes[0]);
-                    __syncthreads();
+                    block_sync();
                 }
                 if (tid == 0 && p.row_lse) p.row_lse[rowi] = lse;
                 has_cands = lse != f_ninf();
@@ -920,7 +924,7 @@ __global__ void __launch_bounds__(kThreads) decode_kernel(const __grid_constant_
                     }
                     if (lane == 0) sh.wkeys[warp * KMAX + r] = w;
                 }
-                __syncthreads();
+                block_sync();
                 if (warp == 0) {
                     constexpr int kPer = (kWarps * KMAX + 31) / 32;
                     uint64_t mine[kPer];
@@ -966,23 +970,25 @@ __global__ void __launch_bounds__(kThreads) decode_kernel(const __grid_constant_
             }
         }
 
-        // Arrive; the last row of (t, b) selects.
-        __syncthreads();
+        // Arrive; the last row of (t, b) selects. Every thread that wrote the row's
+        // list fences its own writes before the arrival is counted.
+        __threadfence();
+        block_sync();
         if (tid == 0) {
-            __threadfence();
             sh.is_last = atomicAdd(p.arrive + b, 1u) == static_cast<uint32_t>(K) - 1u ? 1 : 0;
         }
-        __syncthreads();
+        block_sync();
         if (sh.is_last) {
             __threadfence();
             select_step<KMAX, KCAP>(p, sh, ss, t, b, m);
+            // select_step ends with every writer's fence and a barrier; then one release.
             if (tid == 0) {
                 p.arrive[b] = 0;
                 __threadfence();
                 st_release(p.flag + b, t + 1);
             }
         }
-        __syncthreads();
+        block_sync();
     }
 }
 

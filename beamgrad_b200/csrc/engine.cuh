@@ -74,6 +74,7 @@ struct DecodeParams {
     unsigned long long timeout_ns;
 };
 
+
 // Everything the backward kernels need.
 struct BackwardParams {
     int B, T, K, V;
@@ -129,19 +130,33 @@ __device__ __forceinline__ unsigned long long global_ns() {
     return t;
 }
 
-// Waits until flag >= target. Bounded: after timeout_ns it records kErrTimeout
-// and returns false. Called by one thread.
-__device__ __forceinline__ bool wait_flag(const DecodeParams& p, const int32_t* flag, int target) {
-    if (ld_acquire(flag) >= target) return true;
-    const unsigned long long start = global_ns();
+// Waits until flag >= target; executed by all 32 lanes of one warp together
+// (lane 0 reads, the warp follows its decision), so the warp never diverges
+// around the spin. Bounded: after timeout_ns it records kErrTimeout and returns
+// false; it also returns false as soon as another CTA recorded an error.
+__device__ __forceinline__ bool wait_flag_warp(const DecodeParams& p, const int32_t* flag, int target) {
+    const int lane = threadIdx.x & 31;
+    unsigned long long start = 0;
     unsigned sleep = 32;
-    for (;;) {
-        if (ld_acquire(flag) >= target) return true;
-        if (ld_acquire(p.error) != kErrNone) return false;
-        if (global_ns() - start > p.timeout_ns) {
-            atomicCAS(p.error, kErrNone, kErrTimeout);
-            return false;
+    for (int iter = 0;; ++iter) {
+        int state = 0;  // 1 ready, 2 give up
+        if (lane == 0) {
+            if (ld_acquire(flag) >= target) {
+                state = 1;
+            } else if (ld_acquire(p.error) != kErrNone) {
+                state = 2;
+            } else {
+                const unsigned long long now = global_ns();
+                if (iter == 0) start = now;
+                if (now - start > p.timeout_ns) {
+                    atomicCAS(p.error, kErrNone, kErrTimeout);
+                    state = 2;
+                }
+            }
         }
+        state = __shfl_sync(0xffffffffu, state, 0);
+        if (state == 1) return true;
+        if (state == 2) return false;
         __nanosleep(sleep);
         if (sleep < 1024) sleep <<= 1;
     }
@@ -172,6 +187,24 @@ __device__ __forceinline__ int warp_sum_i32(int v) {
 #pragma unroll
     for (int m = 16; m > 0; m >>= 1) v += __shfl_xor_sync(0xffffffffu, v, m);
     return v;
+}
+
+// Block-wide barriers with per-thread arrival (the non-.aligned PTX forms).
+// __syncthreads() is an aligned barrier, which assumes every warp arrives
+// converged; a warp whose lanes diverged (one lane in a bounded spin on another
+// CTA's flag, or in an atomic) can then be counted as arrived by its other
+// lanes, and the block's barriers pair up across different program points.
+// barrier.sync / barrier.red count threads, so every barrier of the engine
+// goes through these.
+__device__ __forceinline__ void block_sync() { asm volatile("barrier.sync 0;" ::: "memory"); }
+__device__ __forceinline__ bool block_and(bool v) {
+    int r;
+    asm volatile(
+        "{\n .reg .pred p, q;\n setp.ne.u32 p, %1, 0;\n barrier.red.and.pred q, 0, p;\n selp.s32 %0, 1, 0, q;\n}\n"
+        : "=r"(r)
+        : "r"(static_cast<unsigned>(v))
+        : "memory");
+    return r != 0;
 }
 
 // Global loads of data another CTA wrote during this launch: served by L2.
