@@ -228,7 +228,11 @@ void stage_choice(DecodeParams& p, int dtype, bool from_logits) {
     const int64_t row_bytes = static_cast<int64_t>(p.V) * elem_bytes(dtype) + 16;
     const int64_t row_smem = (row_bytes + 127) / 128 * 128;
     const int64_t sel = static_cast<int64_t>(decode_select_smem(p.K));
-    p.staged = from_logits && row_smem + sel <= kMaxRowSmem ? 1 : 0;
+    // Rows that fit are staged in shared memory: from logits the three passes read them
+    // there; from log-probs the staging lets the load start before the previous step's
+    // selection is known.
+    (void)from_logits;
+    p.staged = row_smem + sel <= kMaxRowSmem ? 1 : 0;
     p.row_smem = p.staged ? static_cast<int>(row_smem) : 0;
 }
 

@@ -42,6 +42,7 @@ namespace {  // internal to each translation unit that includes this file
 struct RowShared {
     unsigned long long mbar;
     int ticket;
+    int ready;
     int is_last;
     int invalid;
     int n_blocked;
@@ -727,6 +728,418 @@ __device__ void select_step(const DecodeParams& p, RowShared& sh, SelectShared<K
 // ---------------------------------------------------------------------------
 // The persistent decode kernel.
 // ---------------------------------------------------------------------------
+// ---------------------------------------------------------------------------
+// Warp-cooperative top-k for beams up to 16: lane j < KMAX of a warp holds the
+// warp's j-th best key so far (descending; 0 = empty). Each round every lane
+// offers one key; a ballot picks the offers that beat the warp's K-th key and
+// they are inserted one at a time by the whole warp, so the warp never diverges
+// and a rejected offer costs one compare.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint64_t shfl_u64(uint64_t v, int src) {
+    const uint32_t lo = __shfl_sync(0xffffffffu, static_cast<uint32_t>(v), src);
+    const uint32_t hi = __shfl_sync(0xffffffffu, static_cast<uint32_t>(v >> 32), src);
+    return (static_cast<uint64_t>(hi) << 32) | lo;
+}
+__device__ __forceinline__ uint64_t shfl_up_u64(uint64_t v, int d) {
+    const uint32_t lo = __shfl_up_sync(0xffffffffu, static_cast<uint32_t>(v), d);
+    const uint32_t hi = __shfl_up_sync(0xffffffffu, static_cast<uint32_t>(v >> 32), d);
+    return (static_cast<uint64_t>(hi) << 32) | lo;
+}
+
+template <int KMAX>
+struct WarpTopK {
+    uint64_t wl;   // this lane's entry (lanes < KMAX)
+    uint64_t tk;   // the KMAX-th best key of the warp (0 while the list is not full)
+    float thr;     // raw-score filter: no candidate with raw < thr can enter
+    float thr0;    // filter bound known before the scan (pass 1)
+
+    __device__ __forceinline__ void init(float bound) {
+        wl = 0;
+        tk = 0;
+        thr0 = bound;
+        thr = bound;
+    }
+    __device__ __forceinline__ void offer(uint64_t key, int lane) {
+        unsigned m = __ballot_sync(0xffffffffu, key > tk);
+        while (m) {
+            const int src = __ffs(m) - 1;
+            const uint64_t kk = shfl_u64(key, src);
+            const int pos = __popc(__ballot_sync(0xffffffffu, lane < KMAX && wl > kk));
+            const uint64_t up = shfl_up_u64(wl, 1);
+            if (lane < KMAX) {
+                if (lane == pos) wl = kk;
+                else if (lane > pos) wl = up;
+            }
+            tk = shfl_u64(wl, KMAX - 1);
+            if (tk != 0) thr = fmaxf(thr0, key_raw(tk));
+            m &= m - 1;
+            m &= __ballot_sync(0xffffffffu, key > tk);
+        }
+    }
+};
+
+// The r-th largest (r in [1, 32]) of one float per lane, by a bitonic sort of the warp.
+__device__ __forceinline__ float warp_rth_largest(float v, int r) {
+    const int lane = threadIdx.x & 31;
+#pragma unroll
+    for (int k = 2; k <= 32; k <<= 1) {
+#pragma unroll
+        for (int j = k >> 1; j > 0; j >>= 1) {
+            const float o = __shfl_xor_sync(0xffffffffu, v, j);
+            const bool lower = (lane & j) == 0;
+            const bool desc = (lane & k) == 0;
+            // descending blocks keep the larger value in the lower lane
+            const bool take_max = (lower == desc);
+            v = take_max ? fmaxf(v, o) : fminf(v, o);
+        }
+    }
+    return __shfl_sync(0xffffffffu, v, r - 1);
+}
+
+// ---------------------------------------------------------------------------
+// Row split into 16-byte chunks plus ragged ends. Chunk c (c < nvec) covers
+// entries [head + c*PER, head + (c+1)*PER) and belongs to thread c mod 256; the
+// ragged ends (under 16 bytes before the first and after the last chunk) belong
+// to threads 0..n_ends-1. Passes 1 and 3 both use this assignment, which is what
+// lets pass 1's per-thread maxima bound pass 3's warp lists.
+// ---------------------------------------------------------------------------
+struct RowSplit {
+    int V, head, nvec, tail0, per;
+
+    template <int EB>
+    __device__ __forceinline__ static RowSplit of(const char* row, int V) {
+        RowSplit r;
+        r.V = V;
+        r.per = 16 / EB;
+        const uintptr_t a = reinterpret_cast<uintptr_t>(row);
+        int head = static_cast<int>(((16 - (a & 15)) & 15) / EB);
+        if (head > V) head = V;
+        r.head = head;
+        r.nvec = (V - head) / r.per;
+        r.tail0 = head + r.nvec * r.per;
+        return r;
+    }
+    __device__ __forceinline__ int n_ends() const { return head + (V - tail0); }
+    __device__ __forceinline__ int end_entry(int i) const { return i < head ? i : tail0 + (i - head); }
+    // Whether the calling thread owns entry v.
+    __device__ __forceinline__ bool owns(int v) const {
+        if (v < 0 || v >= V) return false;
+        const int tid = threadIdx.x;
+        if (v < head) return tid == v;
+        if (v >= tail0) return tid == head + (v - tail0);
+        return ((v - head) / per) % kThreads == tid;
+    }
+};
+
+template <int DT>
+__device__ __forceinline__ void unpack16(const uint4& q, float (&x)[16 / Elem<DT>::kBytes]) {
+    using E = Elem<DT>;
+    const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+    if constexpr (E::kBytes == 4) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) x[j] = __uint_as_float(w[j]);
+    } else {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            x[2 * j] = E::to_f32(static_cast<uint16_t>(w[j] & 0xffffu));
+            x[2 * j + 1] = E::to_f32(static_cast<uint16_t>(w[j] >> 16));
+        }
+    }
+}
+
+__device__ __forceinline__ uint4 ld_v4(const void* p, bool smem) {
+    return smem ? *reinterpret_cast<const uint4*>(p) : ld_stream_v4(p);
+}
+
+// f(x, v) for every entry the calling thread owns (per-thread trip counts).
+template <int DT, class F>
+__device__ __forceinline__ void for_chunks(const char* row, const RowSplit& rs, bool smem, F&& f) {
+    using E = Elem<DT>;
+    constexpr int PER = 16 / E::kBytes;
+    const int tid = threadIdx.x;
+    const char* body = row + static_cast<size_t>(rs.head) * E::kBytes;
+    int c = tid;
+    for (; c + kThreads < rs.nvec; c += 2 * kThreads) {
+        const uint4 q0 = ld_v4(body + static_cast<size_t>(c) * 16, smem);
+        const uint4 q1 = ld_v4(body + static_cast<size_t>(c + kThreads) * 16, smem);
+        float x0[PER], x1[PER];
+        unpack16<DT>(q0, x0);
+        unpack16<DT>(q1, x1);
+#pragma unroll
+        for (int j = 0; j < PER; ++j) f(x0[j], rs.head + c * PER + j);
+#pragma unroll
+        for (int j = 0; j < PER; ++j) f(x1[j], rs.head + (c + kThreads) * PER + j);
+    }
+    for (; c < rs.nvec; c += kThreads) {
+        float x0[PER];
+        unpack16<DT>(ld_v4(body + static_cast<size_t>(c) * 16, smem), x0);
+#pragma unroll
+        for (int j = 0; j < PER; ++j) f(x0[j], rs.head + c * PER + j);
+    }
+    if (tid < rs.n_ends()) {
+        const int v = rs.end_entry(tid);
+        f(load_elem<DT>(row, v), v);
+    }
+}
+
+// Warp-uniform scan of the same assignment: test(x) on every owned entry; a chunk
+// round in which any lane of the warp has a hit calls hit(x, v, valid) for each of
+// its PER entries on every lane (valid = the lane owns the entry), so the callee
+// may use warp collectives.
+template <int DT, class Test, class Hit>
+__device__ __forceinline__ void scan_chunks_ballot(const char* row, const RowSplit& rs, bool smem, Test&& test,
+                                                   Hit&& hit) {
+    using E = Elem<DT>;
+    constexpr int PER = 16 / E::kBytes;
+    const int tid = threadIdx.x;
+    const char* body = row + static_cast<size_t>(rs.head) * E::kBytes;
+    const int rounds = (rs.nvec + kThreads - 1) / kThreads;
+    for (int r = 0; r < rounds; ++r) {
+        const int c = tid + r * kThreads;
+        const bool valid = c < rs.nvec;
+        float x[PER];
+        if (valid) {
+            unpack16<DT>(ld_v4(body + static_cast<size_t>(c) * 16, smem), x);
+        } else {
+#pragma unroll
+            for (int j = 0; j < PER; ++j) x[j] = f_ninf();
+        }
+        bool any = false;
+#pragma unroll
+        for (int j = 0; j < PER; ++j) any |= test(x[j]) && valid;
+        if (__ballot_sync(0xffffffffu, any)) {
+#pragma unroll 1
+            for (int j = 0; j < PER; ++j) hit(x[j], rs.head + c * PER + j, valid);
+        }
+    }
+    // Ragged ends: one round for every warp (only warp 0 can own them).
+    {
+        const bool valid = tid < rs.n_ends();
+        const int v = valid ? rs.end_entry(tid) : 0;
+        const float x = valid ? load_elem<DT>(row, v) : f_ninf();
+        const bool any = valid && test(x);
+        if (__ballot_sync(0xffffffffu, any)) hit(x, v, valid);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Selection of example b at step t for beams up to 16, by warp 0 alone: the
+// step's best keys, the carried-forward finished beams, their merge in the
+// full candidate order, and the new trace / state / prefixes / finals.
+// ---------------------------------------------------------------------------
+template <int KMAX>
+__device__ void select_fast(const DecodeParams& p, int t, int b, const Meta& m) {
+    const int lane = threadIdx.x & 31;
+    const int K = p.K;
+    const uint32_t V = static_cast<uint32_t>(p.V);
+    const int64_t sbase = static_cast<int64_t>(b) * K;
+    const int64_t obase = (static_cast<int64_t>(b) * p.T + t) * K;
+    const bool active = t < m.steps;
+    const bool last_step = p.step_api ? true : (t == p.T - 1);
+    const int beam = m.beam;
+
+    // State before the step (lane k holds slot k) and the step's candidate keys.
+    float s_raw = f_ninf();
+    int s_len = 0, s_last = -1;
+    int s_end = 0;
+    if (lane < beam) {
+        s_raw = ld_cg(p.raw + sbase + lane);
+        s_len = ld_cg(p.len + sbase + lane);
+        s_end = ld_cg(p.ended + sbase + lane);
+        if (p.step_api) {
+            if (p.caller_prefix && s_len >= 1 && s_len <= p.prefix_stride)
+                s_last = ld_cg(p.caller_prefix + (sbase + lane) * p.prefix_stride + s_len - 1);
+        } else {
+            s_last = ld_cg(p.last + sbase + lane);
+        }
+    }
+    constexpr int kPer = (kFastBeam * kFastBeam) / 32;
+    const uint64_t* lists = p.keys + sbase * KMAX;
+    const int n = K * KMAX;
+    uint64_t mine[kPer];
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) {
+        const int i = lane + 32 * j;
+        mine[j] = (active && i < n) ? ld_cg(lists + i) : 0;
+    }
+
+    int filled = 0;
+    // This lane's candidate (scanned: lanes [0, ns); carried: lanes [ns, ns + nc)).
+    uint64_t my_key = 0;
+    float c_score = 0.0f, c_raw = 0.0f;
+    int c_parent = -1, c_token = -1, c_len = 0, c_from = 0;
+    int pos = 1 << 30;
+    if (active) {
+        int ns = 0;
+        for (; ns < beam; ++ns) {
+            uint64_t bst = 0;
+#pragma unroll
+            for (int j = 0; j < kPer; ++j) bst = mine[j] > bst ? mine[j] : bst;
+            const uint64_t w = warp_max_u64(bst);
+            if (w == 0) break;
+#pragma unroll
+            for (int j = 0; j < kPer; ++j)
+                if (mine[j] == w) mine[j] = 0;
+            if (lane == ns) my_key = w;
+        }
+        // Carried-forward candidates: finished, live beams (EOS handling on).
+        const bool carry = m.eos >= 0 && lane < beam && s_end != 0 && f_finite(s_raw);
+        const unsigned cm = __ballot_sync(0xffffffffu, carry);
+        const int nc = __popc(cm);
+        // Scanned candidate of lane i < ns.
+        {
+            const uint32_t index = key_index(my_key);
+            const int par = lane < ns ? static_cast<int>(index / V) : 0;
+            const int plen = __shfl_sync(0xffffffffu, s_len, par);
+            if (lane < ns) {
+                c_parent = par;
+                c_token = static_cast<int>(index - static_cast<uint32_t>(par) * V);
+                c_len = plen + 1;
+                c_raw = key_raw(my_key);
+                c_score = __fmul_rn(c_raw, __fdiv_rn(1.0f, gnmt_penalty(c_len, p.alpha)));
+                c_from = 1;
+            }
+        }
+        // Carried candidate j (the j-th carrying slot in slot order) moves to lane ns + j.
+        {
+            const int j = __popc(cm & ((1u << lane) - 1u));
+            const int l = s_len > 1 ? s_len : 1;
+            const float sc = carry ? __fdiv_rn(s_raw, gnmt_penalty(l, p.alpha)) : 0.0f;
+            const int tok = (s_last >= 0 && s_last < p.V && is_eos(p, m, s_last)) ? s_last : m.eos;
+            // Source lane of carried candidate (lane - ns): the (lane - ns)-th set bit of cm.
+            int srcl = 0;
+            {
+                const int want = lane - ns;
+                unsigned mm = cm;
+                for (int q = 0; q < want && mm; ++q) mm &= mm - 1;
+                srcl = mm ? __ffs(mm) - 1 : 0;
+            }
+            const float g_sc = __shfl_sync(0xffffffffu, sc, srcl);
+            const float g_raw = __shfl_sync(0xffffffffu, s_raw, srcl);
+            const int g_tok = __shfl_sync(0xffffffffu, tok, srcl);
+            const int g_len = __shfl_sync(0xffffffffu, l, srcl);
+            (void)j;
+            if (lane >= ns && lane < ns + nc) {
+                c_score = g_sc;
+                c_raw = g_raw;
+                c_parent = srcl;
+                c_token = g_tok;
+                c_len = g_len;
+                c_from = 0;
+            }
+        }
+        // Positions by counting under the full order (src/common.hpp:269-276).
+        const int total = ns + nc;
+        pos = 0;
+        for (int o = 0; o < total; ++o) {
+            const float os = __shfl_sync(0xffffffffu, c_score, o);
+            const float orr = __shfl_sync(0xffffffffu, c_raw, o);
+            const int op = __shfl_sync(0xffffffffu, c_parent, o);
+            const int ot = __shfl_sync(0xffffffffu, c_token, o);
+            const int ol = __shfl_sync(0xffffffffu, c_len, o);
+            const int of = __shfl_sync(0xffffffffu, c_from, o);
+            bool better;
+            if (os != c_score) better = os > c_score;
+            else if (orr != c_raw) better = orr > c_raw;
+            else if (op != c_parent) better = op < c_parent;
+            else if (ot != c_token) better = ot < c_token;
+            else if (ol != c_len) better = ol < c_len;
+            else better = of > c_from;
+            if (o != lane && better) ++pos;
+        }
+        if (lane >= total) pos = 1 << 30;
+        filled = total < beam ? total : beam;
+        // Parent-derived fields needed at the new slot.
+        const int par_end = __shfl_sync(0xffffffffu, s_end, c_parent >= 0 ? c_parent : 0);
+        if (pos < beam) {
+            const int64_t o = obase + pos;
+            if (p.out.tokens) p.out.tokens[o] = c_token;
+            if (p.out.parents) p.out.parents[o] = c_parent;
+            if (p.out.lengths) p.out.lengths[o] = c_len;
+            if (p.out.scores) p.out.scores[o] = c_score;
+            if (p.out.raw_scores) p.out.raw_scores[o] = c_raw;
+            if (p.out.from_logprob) p.out.from_logprob[o] = static_cast<uint8_t>(c_from);
+        }
+        __syncwarp();
+        // New state (every lane has its snapshot already).
+        if (pos < beam) {
+            const int64_t sl = sbase + pos;
+            p.raw[sl] = c_raw;
+            p.len[sl] = c_len;
+            p.ended[sl] = static_cast<uint8_t>(c_from ? (par_end != 0 || is_eos(p, m, c_token)) : 1);
+            if (!p.step_api) p.last[sl] = c_token;
+        }
+    }
+    // Empty slots.
+    if (lane < K && lane >= filled) {
+        const int64_t o = obase + lane;
+        if (p.out.tokens) p.out.tokens[o] = -1;
+        if (p.out.parents) p.out.parents[o] = -1;
+        if (p.out.lengths) p.out.lengths[o] = 0;
+        if (p.out.scores) p.out.scores[o] = f_ninf();
+        if (p.out.raw_scores) p.out.raw_scores[o] = f_ninf();
+        if (p.out.from_logprob) p.out.from_logprob[o] = 0;
+        if (active) {
+            const int64_t sl = sbase + lane;
+            p.raw[sl] = f_ninf();
+            p.len[sl] = 0;
+            p.ended[sl] = 0;
+            if (!p.step_api) p.last[sl] = -1;
+        }
+    }
+    // Prefixes of the new hypotheses (decode with n-gram blocking / repetition penalty).
+    if (p.prefix[0] && !p.step_api) {
+        const int T = p.T;
+        const int cur = t & 1, nxt = (t + 1) & 1;
+        // slot -> (parent, token, from) for the filled slots: the lane whose pos == slot.
+        for (int k = 0; k < K; ++k) {
+            const unsigned owner = __ballot_sync(0xffffffffu, active && pos == k);
+            int32_t* dst = p.prefix[nxt] + (sbase + k) * T;
+            if (owner) {
+                const int ol = __ffs(owner) - 1;
+                const int par = __shfl_sync(0xffffffffu, c_parent, ol);
+                const int tok = __shfl_sync(0xffffffffu, c_token, ol);
+                const int frm = __shfl_sync(0xffffffffu, c_from, ol);
+                const int32_t* src = p.prefix[cur] + (sbase + par) * T;
+                const int L = ld_cg(p.prefix_len[cur] + sbase + par);
+                for (int i = lane; i < L; i += 32) dst[i] = ld_cg(src + i);
+                const bool append = frm && tok >= 0 && L < T;
+                if (lane == 0) {
+                    if (append) dst[L] = tok;
+                    p.prefix_len[nxt][sbase + k] = L + (append ? 1 : 0);
+                }
+            } else if (!active) {
+                const int32_t* src = p.prefix[cur] + (sbase + k) * T;
+                const int L = ld_cg(p.prefix_len[cur] + sbase + k);
+                for (int i = lane; i < L; i += 32) dst[i] = ld_cg(src + i);
+                if (lane == 0) p.prefix_len[nxt][sbase + k] = L;
+            } else if (lane == 0) {
+                p.prefix_len[nxt][sbase + k] = 0;
+            }
+        }
+    }
+    __syncwarp();
+    // Final scores after the last step.
+    if (last_step && p.out.final_scores && lane < K) {
+        const int64_t sl = sbase + lane;
+        float raw = f_ninf(), score = f_ninf();
+        int len = 0;
+        if (lane < beam) {
+            raw = p.raw[sl];
+            len = p.len[sl];
+            score = __fdiv_rn(raw, gnmt_penalty(len, p.alpha));
+        }
+        p.out.final_scores[sl] = score;
+        if (p.out.final_raw_scores) p.out.final_raw_scores[sl] = raw;
+        if (p.out.final_lengths) p.out.final_lengths[sl] = len;
+    }
+    __threadfence();
+    __syncwarp();
+}
+
+// ---------------------------------------------------------------------------
+// The persistent decode kernel.
+// ---------------------------------------------------------------------------
 template <int DT, bool LOGITS, int KMAX>
 __global__ void __launch_bounds__(kThreads) decode_kernel(const __grid_constant__ DecodeParams p) {
     constexpr int KCAP = KMAX > 0 ? kFastBeam : kSelectCap;
@@ -747,50 +1160,176 @@ __global__ void __launch_bounds__(kThreads) decode_kernel(const __grid_constant_
     const int K = p.K, V = p.V;
     const uint32_t rows_per_step = static_cast<uint32_t>(p.B) * static_cast<uint32_t>(K);
     const uint32_t total = rows_per_step * static_cast<uint32_t>(p.T);
+    const bool exclusions = p.banned != nullptr;
+    const bool constrained = p.ngram > 0 || p.penalise;
 
     for (;;) {
-        if (tid == 0) sh.ticket = static_cast<int>(atomicAdd(p.ticket, 1u));
+        if (tid == 0) {
+            const uint32_t tk0 = atomicAdd(p.ticket, 1u);
+            sh.ticket = static_cast<int>(tk0);
+            int ready = 0;
+            if (tk0 < total) ready = ld_acquire(p.flag + (tk0 - (tk0 / rows_per_step) * rows_per_step) / K) >=
+                                             static_cast<int>(tk0 / rows_per_step);
+            sh.ready = ready;
+        }
         block_sync();
         const uint32_t tk = static_cast<uint32_t>(sh.ticket);
         if (tk >= total) break;
+        const bool ready = sh.ready != 0;
         const int t = static_cast<int>(tk / rows_per_step);
         const uint32_t rem = tk - static_cast<uint32_t>(t) * rows_per_step;
         const int b = static_cast<int>(rem / static_cast<uint32_t>(K));
         const int k = static_cast<int>(rem - static_cast<uint32_t>(b) * static_cast<uint32_t>(K));
         const Meta m = load_meta(p, b);
+        const int64_t s = static_cast<int64_t>(b) * K + k;
+        const int64_t rowi = (static_cast<int64_t>(b) * p.T + t) * K + k;
+        const char* grow = static_cast<const char*>(p.inputs) + rowi * static_cast<int64_t>(V) * EB;
+        // Rows a step can read: an active step's beams (at t = 0 of a decode, only beam 0).
+        const bool maybe = t < m.steps && k < m.beam && (p.step_api || t > 0 || k == 0);
 
-        if (warp == 0) {
+        // Per-row results of passes 1-2.
+        const char* src = grow;
+        bool prepared = false;
+        float lse = 0.0f;
+        bool invalid = false;
+        bool inv_known = false;  // invalid computed over the whole row
+        float xthr = f_ninf();   // lower bound on this thread's warp's R-th best eligible entry
+        const int R = KMAX > 0 ? (m.beam < KMAX ? m.beam : KMAX) : 0;
+        bool aborted = false;
+        RowSplit rs;
+
+        // Stage the row and compute its max / logsumexp / filter bound. None of it
+        // depends on the selection of the previous step.
+        auto prepare = [&](bool use_smem) {
+            prepared = true;
+            src = grow;
+            if (use_smem) {
+                bool ok = true;
+                src = srow + stage_row<EB>(p, sh, srow, grow, V, phase, ok);
+                if (!ok) {
+                    aborted = true;
+                    return;
+                }
+            }
+            rs = RowSplit::of<EB>(src, V);
+            const bool want_bound = KMAX > 0 && !constrained && !exclusions;
+            if (!LOGITS && !(want_bound && use_smem)) return;
+            // Pass 1 (16-byte chunks): maximum and the NaN/+inf flag. Every thread's
+            // maximum is also a lower bound on its own best entry; the R-th largest of a
+            // warp's bounds bounds the warp's R-th best entry from below.
+            float mx = f_ninf();
+            bool bad = false;
+            for_chunks<DT>(src, rs, use_smem, [&](float x, int) {
+                mx = fmaxf(mx, x);
+                bad |= !(x < f_inf());
+            });
+            const bool any_bad = !block_and(!bad);
+            inv_known = true;
+            invalid = any_bad;
+            if (any_bad) {
+                // Rare: exclude +inf from the maximum (NaN never raises fmaxf).
+                mx = f_ninf();
+                for_chunks<DT>(src, rs, use_smem, [&](float x, int) {
+                    if (x < f_inf()) mx = fmaxf(mx, x);
+                });
+            }
+            if (want_bound && R > 0 && !any_bad) {
+                float me = mx;
+                if (m.eos >= 0) {
+                    // Threads owning an EOS token give no bound (a smaller bound stays valid).
+                    if (rs.owns(m.eos)) me = f_ninf();
+                    for (int i = 0; i < p.n_extra; ++i)
+                        if (rs.owns(p.extra[i])) me = f_ninf();
+                }
+                xthr = warp_rth_largest(me, R);
+            }
+            if (!LOGITS) return;
+            mx = block_max(sh, mx);
+            lse = f_ninf();
+            if (mx != f_ninf()) {
+                // Pass 2: lane tid sums exp(x - max) over v = tid (mod 256) in increasing v.
+                const auto* er = reinterpret_cast<const typename E::T*>(src);
+                float acc = 0.0f;
+                if (!invalid) {
+                    int v = tid;
+                    for (; v + 7 * kLanes < V; v += 8 * kLanes) {
+                        float d[8];
+#pragma unroll
+                        for (int j = 0; j < 8; ++j) d[j] = __fsub_rn(E::to_f32(er[v + j * kLanes]), mx);
+                        float e[8];
+#pragma unroll
+                        for (int j = 0; j < 8; ++j) e[j] = exp_nonpositive_masked(d[j]);
+#pragma unroll
+                        for (int j = 0; j < 8; ++j) acc = __fadd_rn(acc, e[j]);
+                    }
+                    for (; v < V; v += kLanes) acc = __fadd_rn(acc, exp_nonpositive_masked(__fsub_rn(E::to_f32(er[v]), mx)));
+                } else {
+                    for (int v = tid; v < V; v += kLanes) {
+                        const float x = E::to_f32(er[v]);
+                        if (x < f_inf() && x != f_ninf()) acc = __fadd_rn(acc, exp_nonpositive(__fsub_rn(x, mx)));
+                    }
+                }
+                sh.lanes[tid] = acc;
+                block_sync();
+#pragma unroll
+                for (int st = kLanes / 2; st >= 32; st >>= 1) {
+                    if (tid < st) sh.lanes[tid] = __fadd_rn(sh.lanes[tid], sh.lanes[tid + st]);
+                    block_sync();
+                }
+                if (warp == 0) {
+                    float x = sh.lanes[tid];
+#pragma unroll
+                    for (int st = 16; st >= 1; st >>= 1) {
+                        const float o = __shfl_down_sync(0xffffffffu, x, st);
+                        if (tid < st) x = __fadd_rn(x, o);
+                    }
+                    if (tid == 0) sh.lanes[0] = x;
+                }
+                block_sync();
+                lse = logsumexp_from(mx, sh.lanes[0]);
+                block_sync();
+            }
+        };
+
+        // Speculative preparation while example b's previous step is still being selected.
+        if (!ready && maybe && p.staged) {
+            prepare(true);
+            if (aborted) break;
+        }
+
+        if (!ready && warp == 0) {
             const bool ok = wait_flag_warp(p, p.flag + b, t);
             if (lane == 0) sh.is_last = ok ? 0 : -1;
+        } else if (tid == 0) {
+            sh.is_last = 0;
         }
         block_sync();
         if (sh.is_last < 0) break;  // timed out or aborted
 
-        const int64_t s = static_cast<int64_t>(b) * K + k;
-        const int64_t rowi = (static_cast<int64_t>(b) * p.T + t) * K + k;
         bool read = false;
         float pr = 0.0f;
         int plen = 0;
-        if (t < m.steps && k < m.beam) {
+        if (maybe) {
             pr = ld_cg(p.raw + s);
             plen = ld_cg(p.len + s);
             const uint8_t ended = ld_cg(p.ended + s);
             read = f_finite(pr) && !(m.eos >= 0 && ended != 0);
         }
         uint64_t* list = p.keys + s * p.list_len;
-        if (!read) {
-            for (int i = tid; i < p.list_len; i += kThreads) list[i] = 0;
-            if (tid == 0 && p.row_lse) p.row_lse[rowi] = 0.0f;
-        } else {
+        if (read) {
+            if (!prepared) {
+                prepare(p.staged != 0);
+                if (aborted) break;
+            }
             RowCtx c;
             c.pr = pr;
             c.new_len = plen + 1;
             c.k = k;
             c.m = m;
             c.mask_eos = m.eos >= 0 && c.new_len < m.min_length;
-            c.constrained = p.ngram > 0 || p.penalise;
+            c.constrained = constrained;
             c.cv = ConsView{nullptr, 0, true};
-            if (c.constrained) {
+            if (constrained) {
                 const int32_t* pre;
                 int L;
                 if (p.step_api) {
@@ -803,127 +1342,47 @@ __global__ void __launch_bounds__(kThreads) decode_kernel(const __grid_constant_
                 }
                 c.cv = build_constraints(p, sh, pre, L);
             }
-            const char* grow = static_cast<const char*>(p.inputs) + rowi * static_cast<int64_t>(V) * EB;
-            float lse = 0.0f;
-            bool invalid = false;
-            const char* src = grow;  // where passes read the row
-            bool has_cands = true;
-            if constexpr (LOGITS) {
-                bool ok = true;
-                if (p.staged) src = srow + stage_row<EB>(p, sh, srow, grow, V, phase, ok);
-                if (!ok) break;
-                // Pass 1: maximum over entries below +inf, and the NaN/+inf flag.
-                float mx = f_ninf();
-                auto pass1 = [&](float x, int) {
-                    if (x < f_inf()) mx = fmaxf(mx, x);
-                    else invalid = true;
-                };
-                if (p.staged) for_row<DT, false>(src, V, pass1);
-                else for_row<DT, true>(src, V, pass1);
-                mx = block_max(sh, mx);
-                const int any_invalid = block_sum(sh, invalid ? 1 : 0);
-                invalid = any_invalid != 0;
-                lse = f_ninf();
-                if (mx != f_ninf()) {
-                    // Pass 2: lane tid sums exp(x - max) over v = tid (mod 256) in increasing v.
-                    const auto* er = reinterpret_cast<const typename E::T*>(src);
-                    float acc = 0.0f;
-                    if (!invalid) {
-                        int v = tid;
-                        for (; v + 3 * kLanes < V; v += 4 * kLanes) {
-                            const float d0 = __fsub_rn(E::to_f32(er[v]), mx);
-                            const float d1 = __fsub_rn(E::to_f32(er[v + kLanes]), mx);
-                            const float d2 = __fsub_rn(E::to_f32(er[v + 2 * kLanes]), mx);
-                            const float d3 = __fsub_rn(E::to_f32(er[v + 3 * kLanes]), mx);
-                            const float e0 = d0 >= cephes::kMin ? exp_nonpositive_fast(d0) : 0.0f;
-                            const float e1 = d1 >= cephes::kMin ? exp_nonpositive_fast(d1) : 0.0f;
-                            const float e2 = d2 >= cephes::kMin ? exp_nonpositive_fast(d2) : 0.0f;
-                            const float e3 = d3 >= cephes::kMin ? exp_nonpositive_fast(d3) : 0.0f;
-                            acc = __fadd_rn(acc, e0);
-                            acc = __fadd_rn(acc, e1);
-                            acc = __fadd_rn(acc, e2);
-                            acc = __fadd_rn(acc, e3);
-                        }
-                        for (; v < V; v += kLanes) {
-                            const float d = __fsub_rn(E::to_f32(er[v]), mx);
-                            acc = __fadd_rn(acc, d >= cephes::kMin ? exp_nonpositive_fast(d) : 0.0f);
-                        }
-                    } else {
-                        for (int v = tid; v < V; v += kLanes) {
-                            const float x = E::to_f32(er[v]);
-                            if (x < f_inf() && x != f_ninf()) acc = __fadd_rn(acc, exp_nonpositive(__fsub_rn(x, mx)));
-                        }
-                    }
-                    sh.lanes[tid] = acc;
-                    block_sync();
-#pragma unroll
-                    for (int st = kLanes / 2; st >= 32; st >>= 1) {
-                        if (tid < st) sh.lanes[tid] = __fadd_rn(sh.lanes[tid], sh.lanes[tid + st]);
-                        block_sync();
-                    }
-                    if (tid < 32) {
-                        float x = sh.lanes[tid];
-#pragma unroll
-                        for (int st = 16; st >= 1; st >>= 1) {
-                            const float o = __shfl_down_sync(0xffffffffu, x, st);
-                            if (tid < st) x = __fadd_rn(x, o);
-                        }
-                        if (tid == 0) sh.lanes[0] = x;
-                    }
-                    block_sync();
-                    lse = logsumexp_from(mx, sh.lanes[0]);
-                    block_sync();
-                }
-                if (tid == 0 && p.row_lse) p.row_lse[rowi] = lse;
-                has_cands = lse != f_ninf();
-            } else {
-                if (tid == 0 && p.row_lse) p.row_lse[rowi] = 0.0f;
-            }
+            const bool has_cands = !LOGITS || lse != f_ninf();
+            if (tid == 0 && p.row_lse) p.row_lse[rowi] = LOGITS ? lse : 0.0f;
 
             // Pass 3: candidate keys.
             if constexpr (KMAX > 0) {
-                uint64_t best[KMAX];
-#pragma unroll
-                for (int j = 0; j < KMAX; ++j) best[j] = 0;
-                float thr = f_ninf();
-                auto consider = [&](float x, int v) {
+                WarpTopK<KMAX> wt;
+                float bound = f_ninf();
+                if (xthr != f_ninf()) bound = __fadd_rn(pr, LOGITS ? __fsub_rn(xthr, lse) : xthr);
+                wt.init(bound);
+                // x-space prefilter: every entry with raw(x) >= thr has x >= xf, because raw is
+                // non-decreasing in x and raw(float_below(xf)) < thr is checked exactly.
+                auto raw_of = [&](float x) { return __fadd_rn(pr, LOGITS ? __fsub_rn(x, lse) : x); };
+                auto prefilter = [&](float thr) {
+                    if (thr == f_ninf()) return f_ninf();
+                    float xf = LOGITS ? __fadd_rn(__fsub_rn(thr, pr), lse) : __fsub_rn(thr, pr);
+                    if (!(xf < f_inf())) return f_inf();
+                    for (int it = 0; it < 64 && raw_of(float_below(xf)) >= thr; ++it) xf = float_below(xf);
+                    return raw_of(float_below(xf)) >= thr ? f_ninf() : xf;
+                };
+                float xf = prefilter(wt.thr);
+                const bool check_inv = !inv_known;
+                bool inv3 = false;
+                auto exact = [&](float x, int v) -> uint64_t {
                     const float lp = LOGITS ? __fsub_rn(x, lse) : x;
-                    if (!(lp < f_inf())) {
-                        invalid = true;
-                        return;
-                    }
-                    const float raw = __fadd_rn(pr, lp);
-                    if (raw >= thr && lp != f_ninf()) {
-                        const uint64_t key = full_key(p, sh, c, lp, v);
-                        if (key > best[KMAX - 1]) {
-                            best[KMAX - 1] = key;
-#pragma unroll
-                            for (int j = KMAX - 1; j > 0; --j) {
-                                if (best[j] > best[j - 1]) {
-                                    const uint64_t tmp = best[j];
-                                    best[j] = best[j - 1];
-                                    best[j - 1] = tmp;
-                                }
-                            }
-                            if (best[KMAX - 1] != 0) thr = key_raw(best[KMAX - 1]);
-                        }
-                    }
+                    if (!(lp < f_inf()) || lp == f_ninf()) return 0;
+                    if (__fadd_rn(pr, lp) < wt.thr) return 0;
+                    return full_key(p, sh, c, lp, v);
                 };
                 if (has_cands) {
-                    if (LOGITS && p.staged) for_row<DT, false>(src, V, consider);
-                    else for_row<DT, true>(src, V, consider);
+                    scan_chunks_ballot<DT>(src, rs, p.staged != 0 && prepared, [&](float x) {
+                        if (check_inv) inv3 |= !(x < f_inf());
+                        return x >= xf;
+                    }, [&](float x, int v, bool valid) {
+                        const uint64_t key = valid && x >= xf ? exact(x, v) : 0;
+                        const float before = wt.thr;
+                        wt.offer(key, lane);
+                        if (wt.thr != before) xf = prefilter(wt.thr);
+                    });
                 }
-                // Warp lists, then the CTA's list (the row's best KMAX keys).
-                const int R = m.beam < KMAX ? m.beam : KMAX;
-                for (int r = 0; r < R; ++r) {
-                    const uint64_t w = warp_max_u64(best[0]);
-                    if (best[0] == w && w != 0) {
-#pragma unroll
-                        for (int j = 0; j < KMAX - 1; ++j) best[j] = best[j + 1];
-                        best[KMAX - 1] = 0;
-                    }
-                    if (lane == 0) sh.wkeys[warp * KMAX + r] = w;
-                }
+                if (check_inv) invalid = inv3;
+                if (lane < KMAX) sh.wkeys[warp * KMAX + lane] = wt.wl;
                 block_sync();
                 if (warp == 0) {
                     constexpr int kPer = (kWarps * KMAX + 31) / 32;
@@ -931,23 +1390,21 @@ __global__ void __launch_bounds__(kThreads) decode_kernel(const __grid_constant_
 #pragma unroll
                     for (int j = 0; j < kPer; ++j) {
                         const int i = lane + 32 * j;
-                        const int w = i / KMAX, r = i - (i / KMAX) * KMAX;
-                        mine[j] = (i < kWarps * KMAX && r < R) ? sh.wkeys[i] : 0;
-                        (void)w;
+                        mine[j] = i < kWarps * KMAX ? sh.wkeys[i] : 0;
                     }
-                    for (int r = 0; r < KMAX; ++r) {
+                    uint64_t out = 0;
+                    for (int r = 0; r < R; ++r) {
                         uint64_t bst = 0;
 #pragma unroll
                         for (int j = 0; j < kPer; ++j) bst = mine[j] > bst ? mine[j] : bst;
-                        const uint64_t w = r < R ? warp_max_u64(bst) : 0;
+                        const uint64_t w = warp_max_u64(bst);
 #pragma unroll
                         for (int j = 0; j < kPer; ++j)
                             if (w != 0 && mine[j] == w) mine[j] = 0;
-                        if (lane == 0) list[r] = w;
+                        if (lane == r) out = w;
                     }
+                    if (lane < KMAX) list[lane] = out;
                 }
-                const int inv_any = block_sum(sh, invalid ? 1 : 0);
-                if (tid == 0 && inv_any && p.out.invalid_input) p.out.invalid_input[b] = 1;
             } else {
                 // Generic beams: block radix select of the row's best min(beam, V) keys.
                 auto gen = [&](int v) -> uint64_t {
@@ -956,32 +1413,37 @@ __global__ void __launch_bounds__(kThreads) decode_kernel(const __grid_constant_
                     if (!(lp < f_inf()) || lp == f_ninf()) return 0;
                     return full_key(p, sh, c, lp, v);
                 };
-                if (!LOGITS) {
-                    // NaN / +inf anywhere in the row.
+                if (!inv_known) {
                     bool inv = false;
-                    for_row<DT, true>(src, V, [&](float x, int) { inv |= !(x < f_inf()); });
+                    for (int v = tid; v < V; v += kThreads) inv |= !(load_elem<DT>(src, v) < f_inf());
                     invalid = inv;
                 }
                 int cnt = 0;
                 if (has_cands) cnt = block_select(sh, gen, V, m.beam, [&](int pos, uint64_t key) { list[pos] = key; });
                 for (int i = cnt + tid; i < p.list_len; i += kThreads) list[i] = 0;
-                const int inv_any = block_sum(sh, invalid ? 1 : 0);
-                if (tid == 0 && inv_any && p.out.invalid_input) p.out.invalid_input[b] = 1;
             }
+        } else {
+            for (int i = tid; i < p.list_len; i += kThreads) list[i] = 0;
+            if (tid == 0 && p.row_lse) p.row_lse[rowi] = 0.0f;
         }
 
-        // Arrive; the last row of (t, b) selects. Every thread that wrote the row's
-        // list fences its own writes before the arrival is counted.
+        // Arrive; the last row of (t, b) selects. Writers fence their own writes first.
         __threadfence();
-        block_sync();
+        const bool all_valid = block_and(!(read && invalid));
         if (tid == 0) {
+            if (!all_valid && p.out.invalid_input) p.out.invalid_input[b] = 1;
+            __threadfence();
             sh.is_last = atomicAdd(p.arrive + b, 1u) == static_cast<uint32_t>(K) - 1u ? 1 : 0;
         }
         block_sync();
         if (sh.is_last) {
             __threadfence();
-            select_step<KMAX, KCAP>(p, sh, ss, t, b, m);
-            // select_step ends with every writer's fence and a barrier; then one release.
+            if constexpr (KMAX > 0) {
+                if (warp == 0) select_fast<KMAX>(p, t, b, m);
+            } else {
+                select_step<KMAX, KCAP>(p, sh, ss, t, b, m);
+            }
+            block_sync();
             if (tid == 0) {
                 p.arrive[b] = 0;
                 __threadfence();
@@ -991,7 +1453,6 @@ __global__ void __launch_bounds__(kThreads) decode_kernel(const __grid_constant_
         block_sync();
     }
 }
-
 
 // Launch of one (dtype, logits) family: the beam size picks the register
 // top-k width (1..16) or the generic radix-select path.

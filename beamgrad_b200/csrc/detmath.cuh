@@ -163,6 +163,22 @@ __device__ __forceinline__ float exp_nonpositive_fast(float d) {
     return __uint_as_float(__float_as_uint(p) + (__float_as_uint(z) << 23));
 }
 
+// exp_nonpositive(d) for any d <= 0 without a branch: exp_nonpositive_fast(d)
+// where d >= -87, and +0 elsewhere (d < -87, -inf, NaN) through a bit mask.
+__device__ __forceinline__ float exp_nonpositive_masked(float d) {
+    uint32_t keep;
+    asm("set.ge.u32.f32 %0, %1, %2;" : "=r"(keep) : "f"(d), "f"(cephes::kMin));
+    return __uint_as_float(__float_as_uint(exp_nonpositive_fast(d)) & keep);
+}
+
+// The largest float below x (x finite or +inf; -inf stays -inf).
+__device__ __forceinline__ float float_below(float x) {
+    const uint32_t u = __float_as_uint(x);
+    if (x == f_ninf()) return x;
+    if (x == 0.0f) return __uint_as_float(0x80000001u);
+    return __uint_as_float((u & 0x80000000u) ? u + 1u : u - 1u);
+}
+
 // lse = max + (float) ln(sum), sum >= 1 (src/logits.hpp:241-243).
 __device__ __forceinline__ float logsumexp_from(float mx, float sum) {
     return __fadd_rn(mx, __double2float_rn(log_ge1(static_cast<double>(sum))));

@@ -34,7 +34,11 @@ sys.path.insert(0, str(ROOT))
 B, T, K, V = 64, 128, 8, 32000
 EOS, ALPHA = 2, 1.0
 METRIC = "beam candidates/s (B·T·K·V) and HBM GB/s vs roofline at 1/2/4/8 B200"
-WORKLOAD = "C2: bf16 logits [64,128,8,32000] N(0,2)+Zipf(1.1) bias, from_logits, eos=2, alpha=1.0"
+
+
+def workload() -> str:
+    tag = "C2" if (B, T) == (64, 128) else "C2-shaped (reduced, profiling only)"
+    return f"{tag}: bf16 logits [{B},{T},{K},{V}] N(0,2)+Zipf(1.1) bias, from_logits, eos={EOS}, alpha={ALPHA}"
 
 
 def parse():
@@ -45,7 +49,12 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
-    return ap.parse_args()
+    ap.add_argument("--batch", type=int, default=64, help="examples per GPU (C2: 64); smaller only for profiling")
+    ap.add_argument("--seq", type=int, default=128, help="decode steps T (C2: 128); smaller only for profiling")
+    args = ap.parse_args()
+    global B, T
+    B, T = args.batch, args.seq
+    return args
 
 
 def peaks() -> tuple[float, str]:
@@ -162,7 +171,7 @@ def run_reference_arm(args, rank: int, world: int):
         "impl": "reference", "metric": METRIC, "value": value, "unit": "candidates/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": sec * 1e3, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": WORKLOAD, "global_batch": B, "seq_len": T, "beam": K, "vocab": V,
+        "config": {"workload": workload(), "global_batch": B, "seq_len": T, "beam": K, "vocab": V,
                    "parallelism": "host threads"},
         "cpu_baseline": {"value": value, "unit": "candidates/s", "cores": threads, "kind": "reference",
                          "sample": f"full workload ({B} examples) per step, libdbs dbs_decode_batch_into_ex"},
@@ -321,7 +330,7 @@ def main():
             "vs_baseline": None,
             "dtype": "bf16",
             "data": "synthetic",
-            "config": {"workload": WORKLOAD, "global_batch": world * B, "seq_len": T, "beam": K, "vocab": V,
+            "config": {"workload": workload(), "global_batch": world * B, "seq_len": T, "beam": K, "vocab": V,
                        "parallelism": f"batch x{world}" if world > 1 else "single GPU",
                        "l2": "inputs (4.19 GB per GPU) larger than L2"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
