@@ -57,6 +57,8 @@ struct RowShared {
     float lanes[kLanes];
     int hist[256];
     uint64_t wkeys[kWarps * kFastBeam];
+    float wtop[kWarps * kFastBeam];  // each warp's largest per-thread bounds, sorted
+    float xbound;                    // the row's filter bound (R-th largest of all thread bounds)
     int32_t blocked[kConsCap];
     int32_t penal[kConsCap];
     // select bookkeeping
@@ -778,6 +780,21 @@ struct WarpTopK {
     }
 };
 
+// One float per lane sorted descending across the warp (lane 0 = largest), by a bitonic network.
+__device__ __forceinline__ float warp_sort_desc(float v) {
+    const int lane = threadIdx.x & 31;
+#pragma unroll
+    for (int k = 2; k <= 32; k <<= 1) {
+#pragma unroll
+        for (int j = k >> 1; j > 0; j >>= 1) {
+            const float o = __shfl_xor_sync(0xffffffffu, v, j);
+            const bool take_max = ((lane & j) == 0) == ((lane & k) == 0);
+            v = take_max ? fmaxf(v, o) : fminf(v, o);
+        }
+    }
+    return v;
+}
+
 // The r-th largest (r in [1, 32]) of one float per lane, by a bitonic sort of the warp.
 __device__ __forceinline__ float warp_rth_largest(float v, int r) {
     const int lane = threadIdx.x & 31;
@@ -794,6 +811,58 @@ __device__ __forceinline__ float warp_rth_largest(float v, int r) {
         }
     }
     return __shfl_sync(0xffffffffu, v, r - 1);
+}
+
+// ---------------------------------------------------------------------------
+// The smallest float x with raw(x) >= thr, for raw non-decreasing in x with
+// raw(-inf) < thr <= raw(+inf): galloping from an estimate, then bisection, over
+// the order-preserving integer image of the floats (about 2 log2(gap) calls).
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ int32_t float_ord(float x) {
+    const int32_t u = __float_as_int(x);
+    return u >= 0 ? u : static_cast<int32_t>(0x80000000u - static_cast<uint32_t>(u));
+}
+__device__ __forceinline__ float ord_float(int32_t o) {
+    return __int_as_float(o >= 0 ? o : static_cast<int32_t>(0x80000000u - static_cast<uint32_t>(o)));
+}
+
+template <class Raw>
+__device__ __forceinline__ float smallest_x_reaching(float est, float thr, Raw&& raw) {
+    const int32_t kLo = float_ord(f_ninf()), kHi = float_ord(f_inf());
+    int32_t e = (est == est) ? float_ord(est) : 0;  // a NaN estimate starts from 0
+    if (e < kLo) e = kLo;
+    if (e > kHi) e = kHi;
+    int32_t lo, hi;
+    if (raw(ord_float(e)) >= thr) {
+        hi = e;
+        int64_t step = 1;
+        lo = hi;
+        do {
+            lo = static_cast<int32_t>(static_cast<int64_t>(hi) - step > kLo ? static_cast<int64_t>(hi) - step : kLo);
+            if (raw(ord_float(lo)) < thr) break;
+            hi = lo;
+            step <<= 1;
+        } while (lo > kLo);
+        if (lo == hi) return ord_float(hi);  // reached -inf with raw(-inf) >= thr: no filtering
+    } else {
+        lo = e;
+        int64_t step = 1;
+        hi = lo;
+        do {
+            hi = static_cast<int32_t>(static_cast<int64_t>(lo) + step < kHi ? static_cast<int64_t>(lo) + step : kHi);
+            if (raw(ord_float(hi)) >= thr) break;
+            lo = hi;
+            step <<= 1;
+        } while (hi < kHi);
+        if (raw(ord_float(hi)) < thr) return f_inf();
+    }
+    // raw(lo) < thr <= raw(hi)
+    while (hi - lo > 1) {
+        const int32_t mid = lo + (hi - lo) / 2;
+        if (raw(ord_float(mid)) >= thr) hi = mid;
+        else lo = mid;
+    }
+    return ord_float(hi);
 }
 
 // ---------------------------------------------------------------------------
@@ -908,8 +977,14 @@ __device__ __forceinline__ void scan_chunks_ballot(const char* row, const RowSpl
 #pragma unroll
         for (int j = 0; j < PER; ++j) any |= test(x[j]) && valid;
         if (__ballot_sync(0xffffffffu, any)) {
+            // Rolled loop over the chunk's entries; the array shifts through registers so
+            // it is never indexed dynamically.
 #pragma unroll 1
-            for (int j = 0; j < PER; ++j) hit(x[j], rs.head + c * PER + j, valid);
+            for (int j = 0; j < PER; ++j) {
+                hit(x[0], rs.head + c * PER + j, valid);
+#pragma unroll
+                for (int q = 0; q + 1 < PER; ++q) x[q] = x[q + 1];
+            }
         }
     }
     // Ragged ends: one round for every warp (only warp 0 can own them).
@@ -1141,7 +1216,7 @@ __device__ void select_fast(const DecodeParams& p, int t, int b, const Meta& m) 
 // The persistent decode kernel.
 // ---------------------------------------------------------------------------
 template <int DT, bool LOGITS, int KMAX>
-__global__ void __launch_bounds__(kThreads) decode_kernel(const __grid_constant__ DecodeParams p) {
+__global__ void __launch_bounds__(kThreads, 3) decode_kernel(const __grid_constant__ DecodeParams p) {
     constexpr int KCAP = KMAX > 0 ? kFastBeam : kSelectCap;
     using E = Elem<DT>;
     constexpr int EB = E::kBytes;
@@ -1193,7 +1268,7 @@ __global__ void __launch_bounds__(kThreads) decode_kernel(const __grid_constant_
         float lse = 0.0f;
         bool invalid = false;
         bool inv_known = false;  // invalid computed over the whole row
-        float xthr = f_ninf();   // lower bound on this thread's warp's R-th best eligible entry
+        float xthr = f_ninf();   // lower bound on the row's R-th best eligible entry (pass 1)
         const int R = KMAX > 0 ? (m.beam < KMAX ? m.beam : KMAX) : 0;
         bool aborted = false;
         RowSplit rs;
@@ -1217,10 +1292,11 @@ __global__ void __launch_bounds__(kThreads) decode_kernel(const __grid_constant_
             // Pass 1 (16-byte chunks): maximum and the NaN/+inf flag. Every thread's
             // maximum is also a lower bound on its own best entry; the R-th largest of a
             // warp's bounds bounds the warp's R-th best entry from below.
-            float mx = f_ninf();
+            float mx = f_ninf(), mn = f_inf();
             bool bad = false;
             for_chunks<DT>(src, rs, use_smem, [&](float x, int) {
                 mx = fmaxf(mx, x);
+                mn = fminf(mn, x);
                 bad |= !(x < f_inf());
             });
             const bool any_bad = !block_and(!bad);
@@ -1233,7 +1309,8 @@ __global__ void __launch_bounds__(kThreads) decode_kernel(const __grid_constant_
                     if (x < f_inf()) mx = fmaxf(mx, x);
                 });
             }
-            if (want_bound && R > 0 && !any_bad) {
+            const bool make_bound = want_bound && R > 0 && !any_bad;
+            if (make_bound) {
                 float me = mx;
                 if (m.eos >= 0) {
                     // Threads owning an EOS token give no bound (a smaller bound stays valid).
@@ -1241,16 +1318,69 @@ __global__ void __launch_bounds__(kThreads) decode_kernel(const __grid_constant_
                     for (int i = 0; i < p.n_extra; ++i)
                         if (rs.owns(p.extra[i])) me = f_ninf();
                 }
-                xthr = warp_rth_largest(me, R);
+                const float sorted = warp_sort_desc(me);
+                if (lane < R) sh.wtop[warp * kFastBeam + lane] = sorted;
             }
-            if (!LOGITS) return;
-            mx = block_max(sh, mx);
+            if (!LOGITS) {
+                block_sync();
+            } else {
+                mx = block_max(sh, mx);  // its barrier also publishes wtop
+                mn = -block_max(sh, -mn);
+            }
+            if (make_bound && warp == 0) {
+                // The R-th largest of the 256 thread bounds: R rounds of a warp argmax over
+                // the warps' sorted tops (each round removes exactly one value).
+                float v[4];
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const int i = lane + 32 * j;  // i = w * 16 + r
+                    const int w = i >> 4, r = i & 15;
+                    v[j] = (w < kWarps && r < R) ? sh.wtop[w * kFastBeam + r] : f_ninf();
+                }
+                float rth = f_ninf();
+                for (int r = 0; r < R; ++r) {
+                    uint64_t best = 0;
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        const uint32_t u = __float_as_uint(v[j]);
+                        const uint32_t o = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+                        const uint64_t key = (static_cast<uint64_t>(o) << 32) | static_cast<uint32_t>(lane + 32 * j + 1);
+                        best = key > best ? key : best;
+                    }
+                    best = warp_max_u64(best);
+                    const int owner = static_cast<int>(static_cast<uint32_t>(best)) - 1;
+#pragma unroll
+                    for (int j = 0; j < 4; ++j)
+                        if (owner == lane + 32 * j) {
+                            rth = v[j];
+                            v[j] = f_ninf();
+                        }
+                    rth = __shfl_sync(0xffffffffu, rth, owner & 31);
+                }
+                if (lane == 0) sh.xbound = rth;
+            }
+            if (!LOGITS) {
+                block_sync();
+                if (make_bound) xthr = sh.xbound;
+                return;
+            }
             lse = f_ninf();
             if (mx != f_ninf()) {
                 // Pass 2: lane tid sums exp(x - max) over v = tid (mod 256) in increasing v.
                 const auto* er = reinterpret_cast<const typename E::T*>(src);
                 float acc = 0.0f;
-                if (!invalid) {
+                if (!invalid && __fsub_rn(mn, mx) >= cephes::kMin) {
+                    // Every entry is finite with x - max >= -87: no masking needed.
+                    int v = tid;
+                    for (; v + 7 * kLanes < V; v += 8 * kLanes) {
+                        float e[8];
+#pragma unroll
+                        for (int j = 0; j < 8; ++j) e[j] = exp_nonpositive_fast(__fsub_rn(E::to_f32(er[v + j * kLanes]), mx));
+#pragma unroll
+                        for (int j = 0; j < 8; ++j) acc = __fadd_rn(acc, e[j]);
+                    }
+                    for (; v < V; v += kLanes) acc = __fadd_rn(acc, exp_nonpositive_fast(__fsub_rn(E::to_f32(er[v]), mx)));
+                } else if (!invalid) {
                     int v = tid;
                     for (; v + 7 * kLanes < V; v += 8 * kLanes) {
                         float d[8];
@@ -1288,7 +1418,10 @@ __global__ void __launch_bounds__(kThreads) decode_kernel(const __grid_constant_
                 block_sync();
                 lse = logsumexp_from(mx, sh.lanes[0]);
                 block_sync();
+            } else {
+                block_sync();
             }
+            if (make_bound) xthr = sh.xbound;
         };
 
         // Speculative preparation while example b's previous step is still being selected.
@@ -1356,10 +1489,8 @@ __global__ void __launch_bounds__(kThreads) decode_kernel(const __grid_constant_
                 auto raw_of = [&](float x) { return __fadd_rn(pr, LOGITS ? __fsub_rn(x, lse) : x); };
                 auto prefilter = [&](float thr) {
                     if (thr == f_ninf()) return f_ninf();
-                    float xf = LOGITS ? __fadd_rn(__fsub_rn(thr, pr), lse) : __fsub_rn(thr, pr);
-                    if (!(xf < f_inf())) return f_inf();
-                    for (int it = 0; it < 64 && raw_of(float_below(xf)) >= thr; ++it) xf = float_below(xf);
-                    return raw_of(float_below(xf)) >= thr ? f_ninf() : xf;
+                    const float est = LOGITS ? __fadd_rn(__fsub_rn(thr, pr), lse) : __fsub_rn(thr, pr);
+                    return smallest_x_reaching(est, thr, raw_of);
                 };
                 float xf = prefilter(wt.thr);
                 const bool check_inv = !inv_known;
