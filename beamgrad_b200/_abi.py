@@ -155,9 +155,17 @@ SIGNATURES = {
     # additions (include/dbs_cuda_b200.h)
     "dbs_cuda_b200_abi_version": (C.c_int, []),
     "dbs_cuda_backtrack": (C.c_int, [C.POINTER(DecodeArgs), _p, _p, _p, _p]),
+    "dbs_cuda_decode_no_alloc": (
+        C.c_int,
+        [_p, C.c_int, C.c_int, C.POINTER(DecodeArgs), C.POINTER(SearchOptions), C.POINTER(DecodeOutputs), _p, _p],
+    ),
 }
 
-REFERENCE_SYMBOLS = [n for n in SIGNATURES if n not in ("dbs_cuda_b200_abi_version", "dbs_cuda_backtrack")]
+ADDED_SYMBOLS = ("dbs_cuda_b200_abi_version", "dbs_cuda_backtrack", "dbs_cuda_decode_no_alloc")
+REFERENCE_SYMBOLS = [n for n in SIGNATURES if n not in ADDED_SYMBOLS]
+
+# Size of the fixed device array behind dbs_cuda_decode_no_alloc (DBS_CUDA_B200_NO_ALLOC_SCRATCH_BYTES).
+NO_ALLOC_SCRATCH_BYTES = 4 * 1024 * 1024
 
 _lib: C.CDLL | None = None
 
