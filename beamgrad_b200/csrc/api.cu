@@ -21,6 +21,7 @@ cudaError_t launch_decode(const DecodeParams& p, int dtype, bool logits, cudaStr
 cudaError_t launch_init(const DecodeParams& p, cudaStream_t stream);
 cudaError_t launch_validate(const DecodeParams& p, int* status, cudaStream_t stream);
 int decode_list_len(int K);
+int decode_chain_list_len(int K);
 size_t decode_select_smem(int K);
 
 
@@ -82,13 +83,26 @@ bool valid_options(const DBSCudaSearchOptions* o, const DBSCudaDecodeArgs& a) {
     return o->extra_eos_count == 0 || a.eos_token >= 0 || a.eos_tokens_per_example;
 }
 
-// Workspace layout of a decode (step_stride < 0) or of one step.
+// Largest row-record area of a chained decode; larger decodes use the waiting kernel.
+constexpr int64_t kMaxChainRecordBytes = int64_t{4} << 30;
+
+// Workspace layout of a decode or of one step.
 struct DecodeLayout {
     int64_t raw, len, ended, last, keys, arrive, flag, ticket, error, status;
     int64_t prefix[2], prefix_len[2];
+    int64_t rkeys, rlse, rinfo, count;  // chained decode only (else -1)
     int64_t total;
     int list_len;
+    bool chain;
 };
+
+// A decode without n-gram blocking / repetition penalty and with beams up to 16
+// runs chained: rows keep parent-independent records, selections never wait.
+bool chain_eligible(const DBSCudaDecodeArgs& a) {
+    if (constrained(a) || a.beam_size > kFastBeam) return false;
+    const int64_t rows = static_cast<int64_t>(a.batch_size) * a.steps * a.beam_size;
+    return rows * decode_chain_list_len(a.beam_size) * 8 <= kMaxChainRecordBytes;
+}
 
 DecodeLayout make_layout(const DBSCudaDecodeArgs& a, bool step_api) {
     DecodeLayout L{};
@@ -99,7 +113,8 @@ DecodeLayout make_layout(const DBSCudaDecodeArgs& a, bool step_api) {
         off = align_up(off + (bytes > 0 ? bytes : 1));
         return at;
     };
-    L.list_len = decode_list_len(a.beam_size);
+    L.chain = !step_api && chain_eligible(a);
+    L.list_len = L.chain ? decode_chain_list_len(a.beam_size) : decode_list_len(a.beam_size);
     if (!step_api) {
         L.raw = take(B * K * 4);
         L.len = take(B * K * 4);
@@ -119,6 +134,14 @@ DecodeLayout make_layout(const DBSCudaDecodeArgs& a, bool step_api) {
         }
     } else {
         L.prefix[0] = L.prefix[1] = L.prefix_len[0] = L.prefix_len[1] = -1;
+    }
+    L.rkeys = L.rlse = L.rinfo = L.count = -1;
+    if (L.chain) {
+        const int64_t rows = B * T * K;
+        L.rkeys = take(rows * L.list_len * 8);
+        L.rlse = take(rows * 4);
+        L.rinfo = take(rows * 4);
+        L.count = take(B * T * 4);
     }
     L.total = off;
     return L;
@@ -267,6 +290,11 @@ int run_decode(const void* inputs, int dtype, int from_logits, const DBSCudaDeco
     p.flag = ws.at<int32_t>(L.flag);
     p.ticket = ws.at<uint32_t>(L.ticket);
     p.error = ws.at<int32_t>(L.error);
+    p.chain = L.chain ? 1 : 0;
+    p.rkeys = ws.at<uint64_t>(L.rkeys);
+    p.rlse = ws.at<float>(L.rlse);
+    p.rinfo = ws.at<uint32_t>(L.rinfo);
+    p.count = ws.at<uint32_t>(L.count);
     stage_choice(p, dtype, from_logits != 0);
     const int rc = validate_per_example(p, a, ws.at<int32_t>(L.status), stream);
     if (rc != DBS_CUDA_STATUS_OK) return rc;
@@ -309,6 +337,11 @@ int run_step(const void* inputs, int dtype, int from_logits, const DBSCudaDecode
     p.flag = ws.at<int32_t>(L.flag);
     p.ticket = ws.at<uint32_t>(L.ticket);
     p.error = ws.at<int32_t>(L.error);
+    p.chain = L.chain ? 1 : 0;
+    p.rkeys = ws.at<uint64_t>(L.rkeys);
+    p.rlse = ws.at<float>(L.rlse);
+    p.rinfo = ws.at<uint32_t>(L.rinfo);
+    p.count = ws.at<uint32_t>(L.count);
     stage_choice(p, dtype, from_logits != 0);
     const int rc = validate_per_example(p, a, ws.at<int32_t>(L.status), stream);
     if (rc != DBS_CUDA_STATUS_OK) return rc;

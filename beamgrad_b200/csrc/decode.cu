@@ -60,6 +60,7 @@ __global__ void init_decode_kernel(DecodeParams p) {
             if (p.out.invalid_input) p.out.invalid_input[b] = 0;
         }
     }
+    if (p.count && i < static_cast<int64_t>(p.B) * p.T) p.count[i] = 0;
     if (i == 0) {
         *p.ticket = 0;
         *p.error = kErrNone;
@@ -92,6 +93,13 @@ int decode_list_len(int K) {
     return K;
 }
 
+// Entries kept per row record of the chained decode (beams up to 16).
+int decode_chain_list_len(int K) {
+    if (K <= 4) return chain_list_len<4>();
+    if (K <= 8) return chain_list_len<8>();
+    return chain_list_len<16>();
+}
+
 size_t decode_select_smem(int K) {
     return K <= kFastBeam ? sizeof(SelectShared<kFastBeam>) : sizeof(SelectShared<kSelectCap>);
 }
@@ -105,7 +113,8 @@ cudaError_t launch_decode(const DecodeParams& p, int dtype, bool logits, cudaStr
 }
 
 cudaError_t launch_init(const DecodeParams& p, cudaStream_t stream) {
-    const int64_t n = static_cast<int64_t>(p.B) * p.K;
+    int64_t n = static_cast<int64_t>(p.B) * p.K;
+    if (p.count && static_cast<int64_t>(p.B) * p.T > n) n = static_cast<int64_t>(p.B) * p.T;
     const int64_t blocks = (n + 255) / 256;
     init_decode_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(p);
     return cudaGetLastError();

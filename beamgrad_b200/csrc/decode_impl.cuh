@@ -56,14 +56,15 @@ struct RowShared {
     int ired[kWarps];
     float lanes[kLanes];
     int hist[256];
-    uint64_t wkeys[kWarps * kFastBeam];
-    float wtop[kWarps * kFastBeam];  // each warp's largest per-thread bounds, sorted
+    uint64_t wkeys[kWarps * 32];
+    float wtop[kWarps * 32];  // each warp's largest per-thread bounds, sorted
     float xbound;                    // the row's filter bound (R-th largest of all thread bounds)
     int32_t blocked[kConsCap];
     int32_t penal[kConsCap];
     // select bookkeeping
     int n_scanned;
     int n_carry;
+    unsigned fallback;  // chained select: rows whose record is not enough
 };
 
 // Per-example select arrays of capacity KCAP, in dynamic shared memory.
@@ -998,11 +999,193 @@ __device__ __forceinline__ void scan_chunks_ballot(const char* row, const RowSpl
 }
 
 // ---------------------------------------------------------------------------
+// Row preparation, independent of the previous step's selection: stage the row
+// in shared memory (optional), pass 1 (maximum, NaN/+inf flag, per-thread
+// maxima for the filter bound), pass 2 (logsumexp, from logits only).
+// ---------------------------------------------------------------------------
+struct Prep {
+    const char* src;   // the row (shared memory when staged)
+    RowSplit rs;
+    float lse;         // logsumexp (from logits), -inf for a row without finite entries
+    float xthr;        // lower bound on the row's R-th best eligible entry (-inf: none)
+    bool invalid;      // NaN/+inf in the row (valid when inv_known)
+    bool inv_known;
+    bool aborted;      // the staging copy timed out (error word set)
+};
+
+// RCAP: capacity of the bound (R <= RCAP <= 32). want_bound: the caller's candidates are
+// not subject to exclusions the per-thread maxima cannot see (banned tokens, constraints).
+template <int DT, bool LOGITS, int RCAP>
+__device__ __forceinline__ void prepare_row(const DecodeParams& p, RowShared& sh, char* srow, const char* grow,
+                                            uint32_t& phase, bool use_smem, bool want_bound, int R, const Meta& m,
+                                            Prep& o) {
+    using E = Elem<DT>;
+    constexpr int EB = E::kBytes;
+    const int tid = threadIdx.x;
+    const int lane = tid & 31;
+    const int warp = tid >> 5;
+    const int V = p.V;
+    o.src = grow;
+    o.lse = 0.0f;
+    o.xthr = f_ninf();
+    o.invalid = false;
+    o.inv_known = false;
+    o.aborted = false;
+    if (use_smem) {
+        bool ok = true;
+        o.src = srow + stage_row<EB>(p, sh, srow, grow, V, phase, ok);
+        if (!ok) {
+            o.aborted = true;
+            return;
+        }
+    }
+    const char* src = o.src;
+    o.rs = RowSplit::of<EB>(src, V);
+    const RowSplit& rs = o.rs;
+    if (!LOGITS && !(want_bound && use_smem)) return;
+    // Pass 1 (16-byte chunks): maximum and the NaN/+inf flag. Every thread's
+    // maximum is also a lower bound on its own best entry; the R-th largest of
+    // the 256 thread bounds bounds the row's R-th best entry from below.
+    float mx = f_ninf(), mn = f_inf();
+    bool bad = false;
+    for_chunks<DT>(src, rs, use_smem, [&](float x, int) {
+        mx = fmaxf(mx, x);
+        mn = fminf(mn, x);
+        bad |= !(x < f_inf());
+    });
+    const bool any_bad = !block_and(!bad);
+    o.inv_known = true;
+    o.invalid = any_bad;
+    if (any_bad) {
+        // Rare: exclude +inf from the maximum (NaN never raises fmaxf).
+        mx = f_ninf();
+        for_chunks<DT>(src, rs, use_smem, [&](float x, int) {
+            if (x < f_inf()) mx = fmaxf(mx, x);
+        });
+    }
+    const bool make_bound = want_bound && R > 0 && !any_bad;
+    if (make_bound) {
+        float me = mx;
+        if (m.eos >= 0) {
+            // Threads owning an EOS token give no bound (a smaller bound stays valid).
+            if (rs.owns(m.eos)) me = f_ninf();
+            for (int i = 0; i < p.n_extra; ++i)
+                if (rs.owns(p.extra[i])) me = f_ninf();
+        }
+        const float sorted = warp_sort_desc(me);
+        if (lane < R) sh.wtop[warp * RCAP + lane] = sorted;
+    }
+    if (!LOGITS) {
+        block_sync();
+    } else {
+        mx = block_max(sh, mx);  // its barrier also publishes wtop
+        mn = -block_max(sh, -mn);
+    }
+    if (make_bound && warp == 0) {
+        // The R-th largest of the 256 thread bounds: R rounds of a warp argmax over
+        // the warps' sorted tops (each round removes exactly one value).
+        constexpr int kPer = kWarps * RCAP / 32;
+        float v[kPer];
+#pragma unroll
+        for (int j = 0; j < kPer; ++j) {
+            const int i = lane + 32 * j;  // i = w * RCAP + r
+            const int w = i / RCAP, r = i % RCAP;
+            v[j] = (w < kWarps && r < R) ? sh.wtop[w * RCAP + r] : f_ninf();
+        }
+        float rth = f_ninf();
+        for (int r = 0; r < R; ++r) {
+            uint64_t best = 0;
+#pragma unroll
+            for (int j = 0; j < kPer; ++j) {
+                const uint32_t u = __float_as_uint(v[j]);
+                const uint32_t od = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+                const uint64_t key = (static_cast<uint64_t>(od) << 32) | static_cast<uint32_t>(lane + 32 * j + 1);
+                best = key > best ? key : best;
+            }
+            best = warp_max_u64(best);
+            const int owner = static_cast<int>(static_cast<uint32_t>(best)) - 1;
+#pragma unroll
+            for (int j = 0; j < kPer; ++j)
+                if (owner == lane + 32 * j) {
+                    rth = v[j];
+                    v[j] = f_ninf();
+                }
+            rth = __shfl_sync(0xffffffffu, rth, owner & 31);
+        }
+        if (lane == 0) sh.xbound = rth;
+    }
+    if (!LOGITS) {
+        block_sync();
+        if (make_bound) o.xthr = sh.xbound;
+        return;
+    }
+    float lse = f_ninf();
+    if (mx != f_ninf()) {
+        // Pass 2: lane tid sums exp(x - max) over v = tid (mod 256) in increasing v.
+        const auto* er = reinterpret_cast<const typename E::T*>(src);
+        float acc = 0.0f;
+        if (!o.invalid && __fsub_rn(mn, mx) >= cephes::kMin) {
+            // Every entry is finite with x - max >= -87: no masking needed.
+            int v = tid;
+            for (; v + 7 * kLanes < V; v += 8 * kLanes) {
+                float e[8];
+#pragma unroll
+                for (int j = 0; j < 8; ++j) e[j] = exp_nonpositive_fast(__fsub_rn(E::to_f32(er[v + j * kLanes]), mx));
+#pragma unroll
+                for (int j = 0; j < 8; ++j) acc = __fadd_rn(acc, e[j]);
+            }
+            for (; v < V; v += kLanes) acc = __fadd_rn(acc, exp_nonpositive_fast(__fsub_rn(E::to_f32(er[v]), mx)));
+        } else if (!o.invalid) {
+            int v = tid;
+            for (; v + 7 * kLanes < V; v += 8 * kLanes) {
+                float d[8];
+#pragma unroll
+                for (int j = 0; j < 8; ++j) d[j] = __fsub_rn(E::to_f32(er[v + j * kLanes]), mx);
+                float e[8];
+#pragma unroll
+                for (int j = 0; j < 8; ++j) e[j] = exp_nonpositive_masked(d[j]);
+#pragma unroll
+                for (int j = 0; j < 8; ++j) acc = __fadd_rn(acc, e[j]);
+            }
+            for (; v < V; v += kLanes) acc = __fadd_rn(acc, exp_nonpositive_masked(__fsub_rn(E::to_f32(er[v]), mx)));
+        } else {
+            for (int v = tid; v < V; v += kLanes) {
+                const float x = E::to_f32(er[v]);
+                if (x < f_inf() && x != f_ninf()) acc = __fadd_rn(acc, exp_nonpositive(__fsub_rn(x, mx)));
+            }
+        }
+        sh.lanes[tid] = acc;
+        block_sync();
+#pragma unroll
+        for (int st = kLanes / 2; st >= 32; st >>= 1) {
+            if (tid < st) sh.lanes[tid] = __fadd_rn(sh.lanes[tid], sh.lanes[tid + st]);
+            block_sync();
+        }
+        if (warp == 0) {
+            float x = sh.lanes[tid];
+#pragma unroll
+            for (int st = 16; st >= 1; st >>= 1) {
+                const float y = __shfl_down_sync(0xffffffffu, x, st);
+                if (tid < st) x = __fadd_rn(x, y);
+            }
+            if (tid == 0) sh.lanes[0] = x;
+        }
+        block_sync();
+        lse = logsumexp_from(mx, sh.lanes[0]);
+        block_sync();
+    } else {
+        block_sync();
+    }
+    o.lse = lse;
+    if (make_bound) o.xthr = sh.xbound;
+}
+
+// ---------------------------------------------------------------------------
 // Selection of example b at step t for beams up to 16, by warp 0 alone: the
 // step's best keys, the carried-forward finished beams, their merge in the
 // full candidate order, and the new trace / state / prefixes / finals.
 // ---------------------------------------------------------------------------
-template <int KMAX>
+template <int KMAX, int LIST = KMAX>
 __device__ void select_fast(const DecodeParams& p, int t, int b, const Meta& m) {
     const int lane = threadIdx.x & 31;
     const int K = p.K;
@@ -1028,9 +1211,10 @@ __device__ void select_fast(const DecodeParams& p, int t, int b, const Meta& m) 
             s_last = ld_cg(p.last + sbase + lane);
         }
     }
-    constexpr int kPer = (kFastBeam * kFastBeam) / 32;
-    const uint64_t* lists = p.keys + sbase * KMAX;
-    const int n = K * KMAX;
+    // Row lists of LIST keys each (unsorted; zeros for no candidate).
+    constexpr int kPer = (KMAX * LIST + 31) / 32;
+    const uint64_t* lists = p.keys + sbase * LIST;
+    const int n = K * LIST;
     uint64_t mine[kPer];
 #pragma unroll
     for (int j = 0; j < kPer; ++j) {
@@ -1277,151 +1461,16 @@ __global__ void __launch_bounds__(kThreads, 3) decode_kernel(const __grid_consta
         // depends on the selection of the previous step.
         auto prepare = [&](bool use_smem) {
             prepared = true;
-            src = grow;
-            if (use_smem) {
-                bool ok = true;
-                src = srow + stage_row<EB>(p, sh, srow, grow, V, phase, ok);
-                if (!ok) {
-                    aborted = true;
-                    return;
-                }
-            }
-            rs = RowSplit::of<EB>(src, V);
-            const bool want_bound = KMAX > 0 && !constrained && !exclusions;
-            if (!LOGITS && !(want_bound && use_smem)) return;
-            // Pass 1 (16-byte chunks): maximum and the NaN/+inf flag. Every thread's
-            // maximum is also a lower bound on its own best entry; the R-th largest of a
-            // warp's bounds bounds the warp's R-th best entry from below.
-            float mx = f_ninf(), mn = f_inf();
-            bool bad = false;
-            for_chunks<DT>(src, rs, use_smem, [&](float x, int) {
-                mx = fmaxf(mx, x);
-                mn = fminf(mn, x);
-                bad |= !(x < f_inf());
-            });
-            const bool any_bad = !block_and(!bad);
-            inv_known = true;
-            invalid = any_bad;
-            if (any_bad) {
-                // Rare: exclude +inf from the maximum (NaN never raises fmaxf).
-                mx = f_ninf();
-                for_chunks<DT>(src, rs, use_smem, [&](float x, int) {
-                    if (x < f_inf()) mx = fmaxf(mx, x);
-                });
-            }
-            const bool make_bound = want_bound && R > 0 && !any_bad;
-            if (make_bound) {
-                float me = mx;
-                if (m.eos >= 0) {
-                    // Threads owning an EOS token give no bound (a smaller bound stays valid).
-                    if (rs.owns(m.eos)) me = f_ninf();
-                    for (int i = 0; i < p.n_extra; ++i)
-                        if (rs.owns(p.extra[i])) me = f_ninf();
-                }
-                const float sorted = warp_sort_desc(me);
-                if (lane < R) sh.wtop[warp * kFastBeam + lane] = sorted;
-            }
-            if (!LOGITS) {
-                block_sync();
-            } else {
-                mx = block_max(sh, mx);  // its barrier also publishes wtop
-                mn = -block_max(sh, -mn);
-            }
-            if (make_bound && warp == 0) {
-                // The R-th largest of the 256 thread bounds: R rounds of a warp argmax over
-                // the warps' sorted tops (each round removes exactly one value).
-                float v[4];
-#pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    const int i = lane + 32 * j;  // i = w * 16 + r
-                    const int w = i >> 4, r = i & 15;
-                    v[j] = (w < kWarps && r < R) ? sh.wtop[w * kFastBeam + r] : f_ninf();
-                }
-                float rth = f_ninf();
-                for (int r = 0; r < R; ++r) {
-                    uint64_t best = 0;
-#pragma unroll
-                    for (int j = 0; j < 4; ++j) {
-                        const uint32_t u = __float_as_uint(v[j]);
-                        const uint32_t o = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
-                        const uint64_t key = (static_cast<uint64_t>(o) << 32) | static_cast<uint32_t>(lane + 32 * j + 1);
-                        best = key > best ? key : best;
-                    }
-                    best = warp_max_u64(best);
-                    const int owner = static_cast<int>(static_cast<uint32_t>(best)) - 1;
-#pragma unroll
-                    for (int j = 0; j < 4; ++j)
-                        if (owner == lane + 32 * j) {
-                            rth = v[j];
-                            v[j] = f_ninf();
-                        }
-                    rth = __shfl_sync(0xffffffffu, rth, owner & 31);
-                }
-                if (lane == 0) sh.xbound = rth;
-            }
-            if (!LOGITS) {
-                block_sync();
-                if (make_bound) xthr = sh.xbound;
-                return;
-            }
-            lse = f_ninf();
-            if (mx != f_ninf()) {
-                // Pass 2: lane tid sums exp(x - max) over v = tid (mod 256) in increasing v.
-                const auto* er = reinterpret_cast<const typename E::T*>(src);
-                float acc = 0.0f;
-                if (!invalid && __fsub_rn(mn, mx) >= cephes::kMin) {
-                    // Every entry is finite with x - max >= -87: no masking needed.
-                    int v = tid;
-                    for (; v + 7 * kLanes < V; v += 8 * kLanes) {
-                        float e[8];
-#pragma unroll
-                        for (int j = 0; j < 8; ++j) e[j] = exp_nonpositive_fast(__fsub_rn(E::to_f32(er[v + j * kLanes]), mx));
-#pragma unroll
-                        for (int j = 0; j < 8; ++j) acc = __fadd_rn(acc, e[j]);
-                    }
-                    for (; v < V; v += kLanes) acc = __fadd_rn(acc, exp_nonpositive_fast(__fsub_rn(E::to_f32(er[v]), mx)));
-                } else if (!invalid) {
-                    int v = tid;
-                    for (; v + 7 * kLanes < V; v += 8 * kLanes) {
-                        float d[8];
-#pragma unroll
-                        for (int j = 0; j < 8; ++j) d[j] = __fsub_rn(E::to_f32(er[v + j * kLanes]), mx);
-                        float e[8];
-#pragma unroll
-                        for (int j = 0; j < 8; ++j) e[j] = exp_nonpositive_masked(d[j]);
-#pragma unroll
-                        for (int j = 0; j < 8; ++j) acc = __fadd_rn(acc, e[j]);
-                    }
-                    for (; v < V; v += kLanes) acc = __fadd_rn(acc, exp_nonpositive_masked(__fsub_rn(E::to_f32(er[v]), mx)));
-                } else {
-                    for (int v = tid; v < V; v += kLanes) {
-                        const float x = E::to_f32(er[v]);
-                        if (x < f_inf() && x != f_ninf()) acc = __fadd_rn(acc, exp_nonpositive(__fsub_rn(x, mx)));
-                    }
-                }
-                sh.lanes[tid] = acc;
-                block_sync();
-#pragma unroll
-                for (int st = kLanes / 2; st >= 32; st >>= 1) {
-                    if (tid < st) sh.lanes[tid] = __fadd_rn(sh.lanes[tid], sh.lanes[tid + st]);
-                    block_sync();
-                }
-                if (warp == 0) {
-                    float x = sh.lanes[tid];
-#pragma unroll
-                    for (int st = 16; st >= 1; st >>= 1) {
-                        const float o = __shfl_down_sync(0xffffffffu, x, st);
-                        if (tid < st) x = __fadd_rn(x, o);
-                    }
-                    if (tid == 0) sh.lanes[0] = x;
-                }
-                block_sync();
-                lse = logsumexp_from(mx, sh.lanes[0]);
-                block_sync();
-            } else {
-                block_sync();
-            }
-            if (make_bound) xthr = sh.xbound;
+            Prep o;
+            prepare_row<DT, LOGITS, kFastBeam>(p, sh, srow, grow, phase, use_smem,
+                                               KMAX > 0 && !constrained && !exclusions, R, m, o);
+            src = o.src;
+            rs = o.rs;
+            lse = o.lse;
+            xthr = o.xthr;
+            invalid = o.invalid;
+            inv_known = o.inv_known;
+            aborted = o.aborted;
         };
 
         // Speculative preparation while example b's previous step is still being selected.
@@ -1585,6 +1634,291 @@ __global__ void __launch_bounds__(kThreads, 3) decode_kernel(const __grid_consta
     }
 }
 
+// ---------------------------------------------------------------------------
+// Chained decode (beams up to 16, no n-gram blocking or repetition penalty).
+//
+// Nothing waits. A row task (t, b, k) needs nothing from the previous step:
+// it stages the row, computes its logsumexp, and keeps the row's best LIST
+// entries by x (ties: lower token first) as a per-row record. Because a
+// candidate's raw score fadd(parent_raw, lp(x)) never decreases as x grows,
+// every entry left out of the record has raw <= raw of the record's last
+// entry; so once the parent's raw score is known, the record holds the row's
+// best R candidates whenever the R-th entry's raw score is strictly above the
+// last entry's (or the record holds every eligible entry). Otherwise, which is
+// rare, the selecting CTA rescans that row with the parent known.
+//
+// Each (b, t) counts arrivals: its K row tasks and, for t > 0, the selection
+// of step t - 1. The CTA that completes the count selects step t of example b
+// and then arrives for step t + 1, continuing the chain while it completes
+// counts, so example b's selections run one after another without any CTA
+// spinning on a flag.
+// ---------------------------------------------------------------------------
+template <int KMAX>
+__host__ __device__ constexpr int chain_list_len() {
+    return KMAX <= 4 ? 8 : 2 * KMAX;
+}
+
+// The best KMAX full keys of row (t, b, k), parent state known, scanned from global
+// memory: the fallback of the chained select, written as the row's list.
+template <int DT, bool LOGITS, int KMAX, int LIST>
+__device__ void rescan_row(const DecodeParams& p, RowShared& sh, int t, int b, int k, const Meta& m, float lse) {
+    using E = Elem<DT>;
+    const int tid = threadIdx.x;
+    const int lane = tid & 31;
+    const int warp = tid >> 5;
+    const int K = p.K, V = p.V;
+    const int64_t s = static_cast<int64_t>(b) * K + k;
+    const int64_t rowi = (static_cast<int64_t>(b) * p.T + t) * K + k;
+    const char* grow = static_cast<const char*>(p.inputs) + rowi * static_cast<int64_t>(V) * E::kBytes;
+    RowCtx c;
+    c.pr = ld_cg(p.raw + s);
+    c.new_len = ld_cg(p.len + s) + 1;
+    c.k = k;
+    c.m = m;
+    c.mask_eos = m.eos >= 0 && c.new_len < m.min_length;
+    c.constrained = false;
+    c.cv = ConsView{nullptr, 0, true};
+    const RowSplit rs = RowSplit::of<E::kBytes>(grow, V);
+    WarpTopK<KMAX> wt;
+    wt.init(f_ninf());
+    if (!LOGITS || lse != f_ninf()) {
+        scan_chunks_ballot<DT>(grow, rs, false, [&](float x) { return x < f_inf() && x != f_ninf(); },
+                               [&](float x, int v, bool valid) {
+                                   uint64_t key = 0;
+                                   if (valid && x < f_inf() && x != f_ninf()) {
+                                       const float lp = LOGITS ? __fsub_rn(x, lse) : x;
+                                       if (lp < f_inf() && lp != f_ninf()) key = full_key(p, sh, c, lp, v);
+                                   }
+                                   wt.offer(key, lane);
+                               });
+    }
+    if (lane < KMAX) sh.wkeys[warp * KMAX + lane] = wt.wl;
+    block_sync();
+    if (warp == 0) {
+        constexpr int kPer = (kWarps * KMAX + 31) / 32;
+        uint64_t mine[kPer];
+#pragma unroll
+        for (int j = 0; j < kPer; ++j) {
+            const int i = lane + 32 * j;
+            mine[j] = i < kWarps * KMAX ? sh.wkeys[i] : 0;
+        }
+        uint64_t out = 0;
+        for (int r = 0; r < KMAX; ++r) {
+            uint64_t bst = 0;
+#pragma unroll
+            for (int j = 0; j < kPer; ++j) bst = mine[j] > bst ? mine[j] : bst;
+            const uint64_t w = warp_max_u64(bst);
+#pragma unroll
+            for (int j = 0; j < kPer; ++j)
+                if (w != 0 && mine[j] == w) mine[j] = 0;
+            if (lane == r) out = w;
+        }
+        if (lane < LIST) p.keys[s * LIST + lane] = lane < KMAX ? out : 0;
+    }
+    block_sync();
+}
+
+// Selection of step t of example b from the row records (whole CTA).
+template <int DT, bool LOGITS, int KMAX, int LIST>
+__device__ void chain_select(const DecodeParams& p, RowShared& sh, int t, int b, const Meta& m) {
+    const int tid = threadIdx.x;
+    const int lane = tid & 31;
+    const int warp = tid >> 5;
+    const int K = p.K;
+    const uint32_t V = static_cast<uint32_t>(p.V);
+    const bool active = t < m.steps;
+    const int R = m.beam < KMAX ? m.beam : KMAX;
+    if (tid == 0) {
+        sh.fallback = 0;
+        sh.invalid = 0;
+    }
+    block_sync();
+    // Warp w turns the records of rows w, w + 8 into candidate keys of parent slot k.
+    for (int k = warp; k < K; k += kWarps) {
+        const int64_t s = static_cast<int64_t>(b) * K + k;
+        const int64_t rowi = (static_cast<int64_t>(b) * p.T + t) * K + k;
+        bool read = false;
+        float pr = 0.0f;
+        int plen = 0;
+        if (active && k < m.beam && (t > 0 || k == 0)) {
+            pr = ld_cg(p.raw + s);
+            plen = ld_cg(p.len + s);
+            const uint8_t ended = ld_cg(p.ended + s);
+            read = f_finite(pr) && !(m.eos >= 0 && ended != 0);
+        }
+        uint64_t key = 0;
+        float lse = 0.0f;
+        if (read) {
+            const uint32_t info = ld_cg(p.rinfo + rowi);
+            lse = ld_cg(p.rlse + rowi);
+            const int cnt = static_cast<int>(info >> 8);
+            const uint64_t xk = lane < cnt ? ld_cg(p.rkeys + rowi * LIST + lane) : 0;
+            float raw = f_ninf();
+            if (xk != 0) {
+                const float x = key_raw(xk);
+                const float lp = LOGITS ? __fsub_rn(x, lse) : x;
+                if (lp < f_inf() && lp != f_ninf()) {
+                    raw = __fadd_rn(pr, lp);
+                    if (raw != f_ninf()) key = make_key(raw, static_cast<uint32_t>(k) * V + key_index(xk));
+                }
+            }
+            // Exactness of the record (raw is non-increasing along it); the record's EOS
+            // masking assumed parent length t.
+            const float raw_r = __shfl_sync(0xffffffffu, raw, R - 1);
+            const float raw_last = __shfl_sync(0xffffffffu, raw, LIST - 1);
+            const bool exact = plen == t && (cnt < LIST || raw_r > raw_last);
+            if (!exact) {
+                key = 0;
+                if (lane == 0) atomicOr(&sh.fallback, 1u << k);
+            }
+            if (lane == 0 && (info & 1u)) sh.invalid = 1;
+        }
+        if (lane < LIST) p.keys[s * LIST + lane] = key;
+        if (lane == 0 && p.row_lse) p.row_lse[rowi] = (read && LOGITS) ? lse : 0.0f;
+    }
+    block_sync();
+    unsigned fb = sh.fallback;
+    while (fb) {
+        const int k = __ffs(fb) - 1;
+        fb &= fb - 1;
+        const int64_t rowi = (static_cast<int64_t>(b) * p.T + t) * K + k;
+        rescan_row<DT, LOGITS, KMAX, LIST>(p, sh, t, b, k, m, ld_cg(p.rlse + rowi));
+    }
+    if (tid == 0 && sh.invalid && p.out.invalid_input) p.out.invalid_input[b] = 1;
+    block_sync();
+    if (warp == 0) select_fast<KMAX, LIST>(p, t, b, m);
+    block_sync();
+}
+
+template <int DT, bool LOGITS, int KMAX>
+__global__ void __launch_bounds__(kThreads, 3) decode_chain_kernel(const __grid_constant__ DecodeParams p) {
+    constexpr int LIST = chain_list_len<KMAX>();
+    using E = Elem<DT>;
+    __shared__ RowShared sh;
+    extern __shared__ __align__(128) unsigned char dyn[];
+    char* srow = reinterpret_cast<char*>(dyn);
+
+    const int tid = threadIdx.x;
+    const int lane = tid & 31;
+    const int warp = tid >> 5;
+    if (tid == 0) mbar_init(&sh.mbar);
+    block_sync();
+    uint32_t phase = 0;
+
+    const int K = p.K, V = p.V, T = p.T;
+    const uint32_t rows_per_step = static_cast<uint32_t>(p.B) * static_cast<uint32_t>(K);
+    const uint32_t total = rows_per_step * static_cast<uint32_t>(T);
+    const bool exclusions = p.banned != nullptr;
+
+    for (;;) {
+        if (tid == 0) sh.ticket = static_cast<int>(atomicAdd(p.ticket, 1u));
+        block_sync();
+        const uint32_t tk = static_cast<uint32_t>(sh.ticket);
+        if (tk >= total) break;
+        const int t = static_cast<int>(tk / rows_per_step);
+        const uint32_t rem = tk - static_cast<uint32_t>(t) * rows_per_step;
+        const int b = static_cast<int>(rem / static_cast<uint32_t>(K));
+        const int k = static_cast<int>(rem - static_cast<uint32_t>(b) * static_cast<uint32_t>(K));
+        const Meta m = load_meta(p, b);
+        const int64_t rowi = (static_cast<int64_t>(b) * T + t) * K + k;
+
+        // Rows an active step can read (at t = 0, only beam 0).
+        if (t < m.steps && k < m.beam && (t > 0 || k == 0)) {
+            const char* grow = static_cast<const char*>(p.inputs) + rowi * static_cast<int64_t>(V) * E::kBytes;
+            Prep o;
+            prepare_row<DT, LOGITS, LIST>(p, sh, srow, grow, phase, p.staged != 0, !exclusions, LIST, m, o);
+            if (o.aborted) break;
+            // Record: the row's best LIST eligible entries by x. A parent read at step t
+            // has length t, so EOS tokens are masked while t + 1 < min_length.
+            const bool mask_eos = m.eos >= 0 && t + 1 < m.min_length;
+            WarpTopK<LIST> wt;
+            wt.init(o.xthr);
+            const bool check_inv = !o.inv_known;
+            bool inv3 = false;
+            if (!LOGITS || o.lse != f_ninf()) {
+                scan_chunks_ballot<DT>(o.src, o.rs, p.staged != 0, [&](float x) {
+                    if (check_inv) inv3 |= !(x < f_inf());
+                    return x >= wt.thr;
+                }, [&](float x, int v, bool valid) {
+                    uint64_t key = 0;
+                    if (valid && x >= wt.thr && x < f_inf() && x != f_ninf() && !(exclusions && p.banned[v]) &&
+                        !(mask_eos && is_eos(p, m, v)))
+                        key = make_key(x, static_cast<uint32_t>(v));
+                    wt.offer(key, lane);
+                });
+            }
+            const bool invalid = check_inv ? !block_and(!inv3) : o.invalid;
+            if (lane < LIST) sh.wkeys[warp * LIST + lane] = wt.wl;
+            block_sync();
+            if (warp == 0) {
+                constexpr int kPer = kWarps * LIST / 32;
+                uint64_t mine[kPer];
+#pragma unroll
+                for (int j = 0; j < kPer; ++j) mine[j] = sh.wkeys[lane + 32 * j];
+                uint64_t out = 0;
+                for (int r = 0; r < LIST; ++r) {
+                    uint64_t bst = 0;
+#pragma unroll
+                    for (int j = 0; j < kPer; ++j) bst = mine[j] > bst ? mine[j] : bst;
+                    const uint64_t w = warp_max_u64(bst);
+                    if (w == 0) break;
+#pragma unroll
+                    for (int j = 0; j < kPer; ++j)
+                        if (mine[j] == w) mine[j] = 0;
+                    if (lane == r) out = w;
+                }
+                const int cnt = __popc(__ballot_sync(0xffffffffu, lane < LIST && out != 0));
+                if (lane < LIST) p.rkeys[rowi * LIST + lane] = out;
+                if (lane == 0) {
+                    p.rlse[rowi] = o.lse;
+                    p.rinfo[rowi] = (invalid ? 1u : 0u) | (static_cast<uint32_t>(cnt) << 8);
+                }
+            }
+        }
+
+        // Arrive: the K rows of (t, b), prepared or not, and for t > 0 the selection of t - 1.
+        __threadfence();
+        block_sync();
+        if (tid == 0) {
+            const uint32_t target = static_cast<uint32_t>(K) + (t > 0 ? 1u : 0u);
+            sh.is_last = atomicAdd(p.count + static_cast<int64_t>(b) * T + t, 1u) == target - 1u ? t : -1;
+        }
+        block_sync();
+        int ct = sh.is_last;
+        while (ct >= 0) {
+            __threadfence();
+            chain_select<DT, LOGITS, KMAX, LIST>(p, sh, ct, b, m);
+            if (tid == 0) {
+                int nxt = -1;
+                if (ct + 1 < T) {
+                    __threadfence();
+                    if (atomicAdd(p.count + static_cast<int64_t>(b) * T + ct + 1, 1u) == static_cast<uint32_t>(K)) nxt = ct + 1;
+                }
+                sh.is_last = nxt;
+            }
+            block_sync();
+            ct = sh.is_last;
+        }
+    }
+}
+
+template <int DT, bool LOGITS, int KMAX>
+static cudaError_t launch_chain_as(const DecodeParams& p, cudaStream_t stream, int sm_count) {
+    const size_t dyn = p.staged ? static_cast<size_t>(p.row_smem) : 0;
+    auto kernel = decode_chain_kernel<DT, LOGITS, KMAX>;
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(dyn));
+    if (e != cudaSuccess) return e;
+    int per_sm = 0;
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kThreads, dyn);
+    if (e != cudaSuccess) return e;
+    if (per_sm < 1) per_sm = 1;
+    const int64_t tickets = static_cast<int64_t>(p.B) * p.K * p.T;
+    int64_t grid = static_cast<int64_t>(sm_count) * per_sm;
+    if (grid > tickets) grid = tickets;
+    kernel<<<static_cast<unsigned>(grid), kThreads, dyn, stream>>>(p);
+    return cudaGetLastError();
+}
+
 // Launch of one (dtype, logits) family: the beam size picks the register
 // top-k width (1..16) or the generic radix-select path.
 template <int DT, bool LOGITS, int KMAX>
@@ -1609,6 +1943,13 @@ static cudaError_t launch_decode_as(const DecodeParams& p, cudaStream_t stream, 
 template <int DT, bool LOGITS>
 static cudaError_t launch_decode_k(const DecodeParams& p, cudaStream_t stream, int sm_count) {
     const int K = p.K;
+    if (p.chain) {
+        if (K <= 1) return launch_chain_as<DT, LOGITS, 1>(p, stream, sm_count);
+        if (K <= 2) return launch_chain_as<DT, LOGITS, 2>(p, stream, sm_count);
+        if (K <= 4) return launch_chain_as<DT, LOGITS, 4>(p, stream, sm_count);
+        if (K <= 8) return launch_chain_as<DT, LOGITS, 8>(p, stream, sm_count);
+        return launch_chain_as<DT, LOGITS, 16>(p, stream, sm_count);
+    }
     if (K <= 1) return launch_decode_as<DT, LOGITS, 1>(p, stream, sm_count);
     if (K <= 2) return launch_decode_as<DT, LOGITS, 2>(p, stream, sm_count);
     if (K <= 4) return launch_decode_as<DT, LOGITS, 4>(p, stream, sm_count);

@@ -72,6 +72,12 @@ struct DecodeParams {
     int staged;             // rows are staged in shared memory (from logits)
     int row_smem;           // bytes of the shared-memory row buffer
     unsigned long long timeout_ns;
+    // chained decode (no inter-CTA waits): per-row records and per-step arrival counts
+    int chain;              // 1: decode_chain_kernel runs this decode
+    uint64_t* rkeys;        // [B, T, K, list_len] each row's best entries by x (x-keys)
+    float* rlse;            // [B, T, K] each row's logsumexp (from logits)
+    uint32_t* rinfo;        // [B, T, K] bit 0: NaN/+inf in the row; bits 8..: entries in rkeys
+    uint32_t* count;        // [B, T] rows (and the previous step's selection) that arrived
 };
 
 

@@ -14,7 +14,7 @@ import numpy as np
 import pytest
 import torch
 
-from _cases import make_problem, random_case
+from _cases import encode, make_problem, random_case
 from beamgrad_b200 import _abi as A
 from oracle import oracle
 
@@ -63,6 +63,26 @@ REFERENCE_CASES = [
     ((1, 3, 64, 5000), dict(eos=0)),
     ((1, 2, 1024, 7), dict(eos=-1)),
 ]
+
+
+@pytest.mark.parametrize("seed", range(6))
+@pytest.mark.parametrize("from_logits", [False, True])
+def test_rounding_ties_between_distinct_entries(seed, from_logits):
+    """Distinct entries whose raw scores round to one value once the parent score is large.
+
+    Entries of a row are spaced 2^-18 apart near -150 while parent scores reach about -150
+    after the first step (ulp 2^-16), so groups of entries with different x tie on raw and
+    are ordered by token; the chained decode's per-row records must then either prove
+    themselves sufficient or be rescanned.
+    """
+    rng = np.random.default_rng(900 + seed)
+    B, T, K, V = 3, 5, 8, 700
+    base = rng.uniform(-160.0, -140.0, size=(B, T, K, 1))
+    x = (base + rng.integers(0, 96, size=(B, T, K, V)) * 2.0 ** -18).astype(np.float32)
+    if from_logits:
+        x = x + np.float32(150.0)
+    pb = oracle.Problem(encode(x, A.DTYPE_F32), dtype=A.DTYPE_F32, from_logits=from_logits, eos=3, alpha=0.6)
+    assert_same(G.engine_decode(pb), oracle.oracle_decode(pb), ctx=f"seed {seed}")
 
 
 @pytest.mark.parametrize("case", range(len(REFERENCE_CASES)))
