@@ -234,6 +234,8 @@ void fill_params(DecodeParams& p, const DBSCudaDecodeArgs& a, const DBSCudaSearc
     p.minlen_pe = a.min_lengths_per_example;
     p.banned = a.banned_tokens;
     p.timeout_ns = kTimeoutNs;
+    p.one2 = 0x3f8000003f800000ull;    // (1.0f, 1.0f)
+    p.nzero2 = 0x8000000080000000ull;  // (-0.0f, -0.0f)
 }
 
 // Range check of per-example arrays on the device (one synchronization).

@@ -30,6 +30,8 @@
 // parent, token) (src/common.hpp:269-276 of beamgrad 2.3.0). Carried-forward
 // candidates are merged with the full comparator.
 #pragma once
+#include <type_traits>
+
 #include "engine.cuh"
 
 namespace dbsb {
@@ -53,7 +55,9 @@ struct RowShared {
     unsigned long long sel_prefix;
     unsigned long long sel_mask;
     float wred[kWarps];
+    float wred2[kWarps];
     int ired[kWarps];
+    float row_lse;
     float lanes[kLanes];
     int hist[256];
     uint64_t wkeys[kWarps * 32];
@@ -952,20 +956,20 @@ __device__ __forceinline__ void for_chunks(const char* row, const RowSplit& rs, 
     }
 }
 
-// Warp-uniform scan of the same assignment: test(x) on every owned entry; a chunk
-// round in which any lane of the warp has a hit calls hit(x, v, valid) for each of
-// its PER entries on every lane (valid = the lane owns the entry), so the callee
-// may use warp collectives.
-template <int DT, class Test, class Hit>
-__device__ __forceinline__ void scan_chunks_ballot(const char* row, const RowSplit& rs, bool smem, Test&& test,
-                                                   Hit&& hit) {
+// Warp-uniform scan by a group of NT threads (local index ltid): chunk c belongs to
+// thread c mod NT, the ragged ends to threads 0..n_ends-1. test(x) on every owned
+// entry; a chunk round in which any lane of the warp has a hit calls hit(x, v, valid)
+// for each of its PER entries on every lane (valid = the lane owns the entry), so the
+// callee may use warp collectives.
+template <int DT, int NT, class Test, class Hit>
+__device__ __forceinline__ void scan_chunks_ballot_n(const char* row, const RowSplit& rs, bool smem, int ltid,
+                                                     Test&& test, Hit&& hit) {
     using E = Elem<DT>;
     constexpr int PER = 16 / E::kBytes;
-    const int tid = threadIdx.x;
     const char* body = row + static_cast<size_t>(rs.head) * E::kBytes;
-    const int rounds = (rs.nvec + kThreads - 1) / kThreads;
+    const int rounds = (rs.nvec + NT - 1) / NT;
     for (int r = 0; r < rounds; ++r) {
-        const int c = tid + r * kThreads;
+        const int c = ltid + r * NT;
         const bool valid = c < rs.nvec;
         float x[PER];
         if (valid) {
@@ -988,14 +992,21 @@ __device__ __forceinline__ void scan_chunks_ballot(const char* row, const RowSpl
             }
         }
     }
-    // Ragged ends: one round for every warp (only warp 0 can own them).
+    // Ragged ends: one round for every warp of the group.
     {
-        const bool valid = tid < rs.n_ends();
-        const int v = valid ? rs.end_entry(tid) : 0;
+        const bool valid = ltid < rs.n_ends();
+        const int v = valid ? rs.end_entry(ltid) : 0;
         const float x = valid ? load_elem<DT>(row, v) : f_ninf();
         const bool any = valid && test(x);
         if (__ballot_sync(0xffffffffu, any)) hit(x, v, valid);
     }
+}
+
+// The same over the whole CTA, chunk c on thread c mod 256 (the pass-1 assignment).
+template <int DT, class Test, class Hit>
+__device__ __forceinline__ void scan_chunks_ballot(const char* row, const RowSplit& rs, bool smem, Test&& test,
+                                                   Hit&& hit) {
+    scan_chunks_ballot_n<DT, kThreads>(row, rs, smem, static_cast<int>(threadIdx.x), test, hit);
 }
 
 // ---------------------------------------------------------------------------
@@ -1013,12 +1024,109 @@ struct Prep {
     bool aborted;      // the staging copy timed out (error word set)
 };
 
-// RCAP: capacity of the bound (R <= RCAP <= 32). want_bound: the caller's candidates are
-// not subject to exclusions the per-thread maxima cannot see (banned tokens, constraints).
-template <int DT, bool LOGITS, int RCAP>
+__device__ __forceinline__ float max_nan(float a, float b) {
+    float r;
+    asm("max.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+    return r;
+}
+// Barrier among the 128 threads of warps 0-3 (id 2) or of warps 4-7 (id 1).
+__device__ __forceinline__ void half_sync(int id) { asm volatile("barrier.sync %0, 128;" ::"r"(id) : "memory"); }
+
+// The R-th largest (R <= RCAP) of the warps' sorted per-thread bounds in sh.wtop, by
+// R rounds of a warp argmax (each round removes exactly one value). One warp.
+template <int RCAP>
+__device__ __forceinline__ float rth_of_thread_bounds(const RowShared& sh, int R) {
+    const int lane = threadIdx.x & 31;
+    constexpr int kPer = kWarps * RCAP / 32;
+    float v[kPer];
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) {
+        const int i = lane + 32 * j;  // i = w * RCAP + r
+        const int w = i / RCAP, r = i % RCAP;
+        v[j] = (w < kWarps && r < R) ? sh.wtop[w * RCAP + r] : f_ninf();
+    }
+    float rth = f_ninf();
+    for (int r = 0; r < R; ++r) {
+        uint64_t best = 0;
+#pragma unroll
+        for (int j = 0; j < kPer; ++j) {
+            const uint32_t u = __float_as_uint(v[j]);
+            const uint32_t od = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+            const uint64_t key = (static_cast<uint64_t>(od) << 32) | static_cast<uint32_t>(lane + 32 * j + 1);
+            best = key > best ? key : best;
+        }
+        best = warp_max_u64(best);
+        const int owner = static_cast<int>(static_cast<uint32_t>(best)) - 1;
+#pragma unroll
+        for (int j = 0; j < kPer; ++j)
+            if (owner == lane + 32 * j) {
+                rth = v[j];
+                v[j] = f_ninf();
+            }
+        rth = __shfl_sync(0xffffffffu, rth, owner & 31);
+    }
+    return rth;
+}
+
+// Entries (v, v + 1) of a row as a packed pair (v even; the pair is aligned).
+template <int DT>
+__device__ __forceinline__ uint64_t load_pair(const char* row, int v) {
+    if constexpr (DT == 0) {
+        return *reinterpret_cast<const uint64_t*>(row + static_cast<size_t>(v) * 4);
+    } else {
+        const uint32_t w = *reinterpret_cast<const uint32_t*>(row + static_cast<size_t>(v) * 2);
+        return f2_pack(Elem<DT>::to_f32(static_cast<uint16_t>(w & 0xffffu)), Elem<DT>::to_f32(static_cast<uint16_t>(w >> 16)));
+    }
+}
+
+// Pass 2 over the full 256-entry blocks for logsumexp lanes (2j, 2j + 1): thread j sums
+// exp(x - max) of both lanes in increasing v, packed. MASKED: entries with x - max below
+// -87 contribute +0 (adding +0 leaves a non-negative sum unchanged).
+template <int DT, bool MASKED>
+__device__ __forceinline__ uint64_t lane_pair_sums(const Pack2& q, const char* row, int nfull, float mx, int j) {
+    const uint64_t mx2 = f2_splat(mx);
+    uint64_t acc = f2_pack(0.0f, 0.0f);
+    auto one = [&](uint64_t x2) {
+        const uint64_t d = f2_sub(q, x2, mx2);
+        float lo, hi;
+        exp_nonpositive_fast2(q, d, lo, hi);
+        if constexpr (MASKED) {
+            float d_lo, d_hi;
+            f2_unpack(d, d_lo, d_hi);
+            uint32_t k_lo, k_hi;
+            asm("set.ge.u32.f32 %0, %1, %2;" : "=r"(k_lo) : "f"(d_lo), "f"(cephes::kMin));
+            asm("set.ge.u32.f32 %0, %1, %2;" : "=r"(k_hi) : "f"(d_hi), "f"(cephes::kMin));
+            lo = __uint_as_float(__float_as_uint(lo) & k_lo);
+            hi = __uint_as_float(__float_as_uint(hi) & k_hi);
+        }
+        return f2_pack(lo, hi);
+    };
+    int i = 0;
+    for (; i + 4 <= nfull; i += 4) {
+        uint64_t x2[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) x2[u] = load_pair<DT>(row, (i + u) * kLanes + 2 * j);
+        uint64_t e[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) e[u] = one(x2[u]);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) acc = f2_add(q, acc, e[u]);
+    }
+    for (; i < nfull; ++i) acc = f2_add(q, acc, one(load_pair<DT>(row, i * kLanes + 2 * j)));
+    return acc;
+}
+
+// Row preparation, independent of the previous step's selection: stage the row in
+// shared memory (optional); pass 1: maximum, minimum, NaN/+inf flag and the per-thread
+// maxima behind the filter bound; from logits, pass 2: logsumexp on warps 0-3 (two
+// lanes per thread, packed) while warps 4-7 compute the bound and then run
+// side(src, rs, xthr), e.g. the chained decode's record scan. RCAP: capacity of the
+// bound (R <= RCAP <= 32). want_bound: the candidates are not subject to exclusions
+// the per-thread maxima cannot see (banned tokens, constraints).
+template <int DT, bool LOGITS, int RCAP, class Side>
 __device__ __forceinline__ void prepare_row(const DecodeParams& p, RowShared& sh, char* srow, const char* grow,
                                             uint32_t& phase, bool use_smem, bool want_bound, int R, const Meta& m,
-                                            Prep& o) {
+                                            Prep& o, Side&& side) {
     using E = Elem<DT>;
     constexpr int EB = E::kBytes;
     const int tid = threadIdx.x;
@@ -1043,29 +1151,17 @@ __device__ __forceinline__ void prepare_row(const DecodeParams& p, RowShared& sh
     o.rs = RowSplit::of<EB>(src, V);
     const RowSplit& rs = o.rs;
     if (!LOGITS && !(want_bound && use_smem)) return;
-    // Pass 1 (16-byte chunks): maximum and the NaN/+inf flag. Every thread's
-    // maximum is also a lower bound on its own best entry; the R-th largest of
-    // the 256 thread bounds bounds the row's R-th best entry from below.
-    float mx = f_ninf(), mn = f_inf();
-    bool bad = false;
+    // Pass 1 (16-byte chunks): maximum (NaN-propagating, so one test flags NaN/+inf),
+    // minimum, and each thread's maximum, a lower bound on its own best entry; the R-th
+    // largest of the 256 thread bounds bounds the row's R-th best entry from below.
+    float mxn = f_ninf(), mn = f_inf();
     for_chunks<DT>(src, rs, use_smem, [&](float x, int) {
-        mx = fmaxf(mx, x);
+        mxn = max_nan(mxn, x);
         mn = fminf(mn, x);
-        bad |= !(x < f_inf());
     });
-    const bool any_bad = !block_and(!bad);
-    o.inv_known = true;
-    o.invalid = any_bad;
-    if (any_bad) {
-        // Rare: exclude +inf from the maximum (NaN never raises fmaxf).
-        mx = f_ninf();
-        for_chunks<DT>(src, rs, use_smem, [&](float x, int) {
-            if (x < f_inf()) mx = fmaxf(mx, x);
-        });
-    }
-    const bool make_bound = want_bound && R > 0 && !any_bad;
-    if (make_bound) {
-        float me = mx;
+    const bool bad = !(mxn < f_inf());
+    if (want_bound) {
+        float me = bad ? f_ninf() : mxn;
         if (m.eos >= 0) {
             // Threads owning an EOS token give no bound (a smaller bound stays valid).
             if (rs.owns(m.eos)) me = f_ninf();
@@ -1075,108 +1171,114 @@ __device__ __forceinline__ void prepare_row(const DecodeParams& p, RowShared& sh
         const float sorted = warp_sort_desc(me);
         if (lane < R) sh.wtop[warp * RCAP + lane] = sorted;
     }
-    if (!LOGITS) {
+    {
+        const float wmx = warp_max_f32(bad ? f_ninf() : mxn);
+        const float wmn = -warp_max_f32(-mn);
+        const unsigned wbad = __ballot_sync(0xffffffffu, bad);
+        if (lane == 0) {
+            sh.wred[warp] = wmx;
+            sh.wred2[warp] = wmn;
+            sh.ired[warp] = wbad != 0;
+        }
+    }
+    block_sync();
+    float mx = sh.wred[0];
+    mn = sh.wred2[0];
+    bool any_bad = sh.ired[0] != 0;
+#pragma unroll
+    for (int w = 1; w < kWarps; ++w) {
+        mx = fmaxf(mx, sh.wred[w]);
+        mn = fminf(mn, sh.wred2[w]);
+        any_bad |= sh.ired[w] != 0;
+    }
+    o.inv_known = true;
+    o.invalid = any_bad;
+    if (any_bad) {
+        // Rare: the maximum over entries below +inf (NaN never raises fmaxf).
         block_sync();
-    } else {
-        mx = block_max(sh, mx);  // its barrier also publishes wtop
-        mn = -block_max(sh, -mn);
+        mx = f_ninf();
+        for_chunks<DT>(src, rs, use_smem, [&](float x, int) {
+            if (x < f_inf()) mx = fmaxf(mx, x);
+        });
+        mx = block_max(sh, mx);
     }
-    if (make_bound && warp == 0) {
-        // The R-th largest of the 256 thread bounds: R rounds of a warp argmax over
-        // the warps' sorted tops (each round removes exactly one value).
-        constexpr int kPer = kWarps * RCAP / 32;
-        float v[kPer];
-#pragma unroll
-        for (int j = 0; j < kPer; ++j) {
-            const int i = lane + 32 * j;  // i = w * RCAP + r
-            const int w = i / RCAP, r = i % RCAP;
-            v[j] = (w < kWarps && r < R) ? sh.wtop[w * RCAP + r] : f_ninf();
-        }
-        float rth = f_ninf();
-        for (int r = 0; r < R; ++r) {
-            uint64_t best = 0;
-#pragma unroll
-            for (int j = 0; j < kPer; ++j) {
-                const uint32_t u = __float_as_uint(v[j]);
-                const uint32_t od = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
-                const uint64_t key = (static_cast<uint64_t>(od) << 32) | static_cast<uint32_t>(lane + 32 * j + 1);
-                best = key > best ? key : best;
-            }
-            best = warp_max_u64(best);
-            const int owner = static_cast<int>(static_cast<uint32_t>(best)) - 1;
-#pragma unroll
-            for (int j = 0; j < kPer; ++j)
-                if (owner == lane + 32 * j) {
-                    rth = v[j];
-                    v[j] = f_ninf();
-                }
-            rth = __shfl_sync(0xffffffffu, rth, owner & 31);
-        }
-        if (lane == 0) sh.xbound = rth;
-    }
+    const bool make_bound = want_bound && R > 0 && !any_bad;
     if (!LOGITS) {
+        if (make_bound && warp == 4) {
+            const float rth = rth_of_thread_bounds<RCAP>(sh, R);
+            if (lane == 0) sh.xbound = rth;
+        }
         block_sync();
         if (make_bound) o.xthr = sh.xbound;
         return;
     }
-    float lse = f_ninf();
-    if (mx != f_ninf()) {
-        // Pass 2: lane tid sums exp(x - max) over v = tid (mod 256) in increasing v.
-        const auto* er = reinterpret_cast<const typename E::T*>(src);
-        float acc = 0.0f;
-        if (!o.invalid && __fsub_rn(mn, mx) >= cephes::kMin) {
-            // Every entry is finite with x - max >= -87: no masking needed.
-            int v = tid;
-            for (; v + 7 * kLanes < V; v += 8 * kLanes) {
-                float e[8];
-#pragma unroll
-                for (int j = 0; j < 8; ++j) e[j] = exp_nonpositive_fast(__fsub_rn(E::to_f32(er[v + j * kLanes]), mx));
-#pragma unroll
-                for (int j = 0; j < 8; ++j) acc = __fadd_rn(acc, e[j]);
-            }
-            for (; v < V; v += kLanes) acc = __fadd_rn(acc, exp_nonpositive_fast(__fsub_rn(E::to_f32(er[v]), mx)));
-        } else if (!o.invalid) {
-            int v = tid;
-            for (; v + 7 * kLanes < V; v += 8 * kLanes) {
-                float d[8];
-#pragma unroll
-                for (int j = 0; j < 8; ++j) d[j] = __fsub_rn(E::to_f32(er[v + j * kLanes]), mx);
-                float e[8];
-#pragma unroll
-                for (int j = 0; j < 8; ++j) e[j] = exp_nonpositive_masked(d[j]);
-#pragma unroll
-                for (int j = 0; j < 8; ++j) acc = __fadd_rn(acc, e[j]);
-            }
-            for (; v < V; v += kLanes) acc = __fadd_rn(acc, exp_nonpositive_masked(__fsub_rn(E::to_f32(er[v]), mx)));
-        } else {
-            for (int v = tid; v < V; v += kLanes) {
-                const float x = E::to_f32(er[v]);
-                if (x < f_inf() && x != f_ninf()) acc = __fadd_rn(acc, exp_nonpositive(__fsub_rn(x, mx)));
-            }
+    if (warp >= 4) {
+        if (make_bound && warp == 4) {
+            const float rth = rth_of_thread_bounds<RCAP>(sh, R);
+            if (lane == 0) sh.xbound = rth;
         }
-        sh.lanes[tid] = acc;
-        block_sync();
-#pragma unroll
-        for (int st = kLanes / 2; st >= 32; st >>= 1) {
-            if (tid < st) sh.lanes[tid] = __fadd_rn(sh.lanes[tid], sh.lanes[tid + st]);
-            block_sync();
-        }
-        if (warp == 0) {
-            float x = sh.lanes[tid];
-#pragma unroll
-            for (int st = 16; st >= 1; st >>= 1) {
-                const float y = __shfl_down_sync(0xffffffffu, x, st);
-                if (tid < st) x = __fadd_rn(x, y);
-            }
-            if (tid == 0) sh.lanes[0] = x;
-        }
-        block_sync();
-        lse = logsumexp_from(mx, sh.lanes[0]);
-        block_sync();
+        half_sync(1);
+        side(src, rs, make_bound ? sh.xbound : f_ninf());
     } else {
-        block_sync();
+        // Pass 2: logsumexp lanes a = 2j and b = 2j + 1 on thread j < 128.
+        const int j = tid;
+        float lse = f_ninf();
+        if (mx != f_ninf()) {
+            const auto* er = reinterpret_cast<const typename E::T*>(src);
+            const int nfull = V / kLanes;
+            const int a = 2 * j, b = 2 * j + 1;
+            float acc_a = 0.0f, acc_b = 0.0f;
+            if (!o.invalid) {
+                const Pack2 q{p.one2, p.nzero2};
+                const bool fast = __fsub_rn(mn, mx) >= cephes::kMin;  // every x - max >= -87
+                const bool paired = (reinterpret_cast<uintptr_t>(src) & (2 * EB - 1)) == 0;
+                if (paired) {
+                    const uint64_t acc = fast ? lane_pair_sums<DT, false>(q, src, nfull, mx, j)
+                                              : lane_pair_sums<DT, true>(q, src, nfull, mx, j);
+                    f2_unpack(acc, acc_a, acc_b);
+                } else {
+                    for (int i = 0; i < nfull; ++i) {
+                        acc_a = __fadd_rn(acc_a, exp_nonpositive_masked(__fsub_rn(E::to_f32(er[i * kLanes + a]), mx)));
+                        acc_b = __fadd_rn(acc_b, exp_nonpositive_masked(__fsub_rn(E::to_f32(er[i * kLanes + b]), mx)));
+                    }
+                }
+                // The partial last block.
+                const int va = nfull * kLanes + a, vb = nfull * kLanes + b;
+                if (va < V) acc_a = __fadd_rn(acc_a, exp_nonpositive_masked(__fsub_rn(E::to_f32(er[va]), mx)));
+                if (vb < V) acc_b = __fadd_rn(acc_b, exp_nonpositive_masked(__fsub_rn(E::to_f32(er[vb]), mx)));
+            } else {
+                for (int v = a; v < V; v += kLanes) {
+                    const float x = E::to_f32(er[v]);
+                    if (x < f_inf() && x != f_ninf()) acc_a = __fadd_rn(acc_a, exp_nonpositive(__fsub_rn(x, mx)));
+                }
+                for (int v = b; v < V; v += kLanes) {
+                    const float x = E::to_f32(er[v]);
+                    if (x < f_inf() && x != f_ninf()) acc_b = __fadd_rn(acc_b, exp_nonpositive(__fsub_rn(x, mx)));
+                }
+            }
+            sh.lanes[a] = acc_a;
+            sh.lanes[b] = acc_b;
+            half_sync(2);
+            // Pairwise tree lanes[i] += lanes[i + s], s = 128 ... 1 (src/kernels.hpp:197-202).
+#pragma unroll
+            for (int st = kLanes / 2; st >= 32; st >>= 1) {
+                if (tid < st) sh.lanes[tid] = __fadd_rn(sh.lanes[tid], sh.lanes[tid + st]);
+                half_sync(2);
+            }
+            if (warp == 0) {
+                float x = sh.lanes[tid];
+#pragma unroll
+                for (int st = 16; st >= 1; st >>= 1) {
+                    const float y = __shfl_down_sync(0xffffffffu, x, st);
+                    if (tid < st) x = __fadd_rn(x, y);
+                }
+                lse = logsumexp_from(mx, x);
+            }
+        }
+        if (tid == 0) sh.row_lse = lse;
     }
-    o.lse = lse;
+    block_sync();
+    o.lse = sh.row_lse;
     if (make_bound) o.xthr = sh.xbound;
 }
 
@@ -1463,7 +1565,8 @@ __global__ void __launch_bounds__(kThreads, 3) decode_kernel(const __grid_consta
             prepared = true;
             Prep o;
             prepare_row<DT, LOGITS, kFastBeam>(p, sh, srow, grow, phase, use_smem,
-                                               KMAX > 0 && !constrained && !exclusions, R, m, o);
+                                               KMAX > 0 && !constrained && !exclusions, R, m, o,
+                                               [](const char*, const RowSplit&, float) {});
             src = o.src;
             rs = o.rs;
             lse = o.lse;
@@ -1825,18 +1928,17 @@ __global__ void __launch_bounds__(kThreads, 3) decode_chain_kernel(const __grid_
         // Rows an active step can read (at t = 0, only beam 0).
         if (t < m.steps && k < m.beam && (t > 0 || k == 0)) {
             const char* grow = static_cast<const char*>(p.inputs) + rowi * static_cast<int64_t>(V) * E::kBytes;
-            Prep o;
-            prepare_row<DT, LOGITS, LIST>(p, sh, srow, grow, phase, p.staged != 0, !exclusions, LIST, m, o);
-            if (o.aborted) break;
             // Record: the row's best LIST eligible entries by x. A parent read at step t
             // has length t, so EOS tokens are masked while t + 1 < min_length.
             const bool mask_eos = m.eos >= 0 && t + 1 < m.min_length;
             WarpTopK<LIST> wt;
-            wt.init(o.xthr);
-            const bool check_inv = !o.inv_known;
             bool inv3 = false;
-            if (!LOGITS || o.lse != f_ninf()) {
-                scan_chunks_ballot<DT>(o.src, o.rs, p.staged != 0, [&](float x) {
+            bool check_inv = false;
+            // NT threads (local index ltid) scan the row; each of their warps keeps a list.
+            auto record_scan = [&](auto nt, const char* src, const RowSplit& rs, float xthr, int ltid) {
+                constexpr int NT = decltype(nt)::value;
+                wt.init(xthr);
+                scan_chunks_ballot_n<DT, NT>(src, rs, p.staged != 0, ltid, [&](float x) {
                     if (check_inv) inv3 |= !(x < f_inf());
                     return x >= wt.thr;
                 }, [&](float x, int v, bool valid) {
@@ -1846,12 +1948,26 @@ __global__ void __launch_bounds__(kThreads, 3) decode_chain_kernel(const __grid_
                         key = make_key(x, static_cast<uint32_t>(v));
                     wt.offer(key, lane);
                 });
+            };
+            Prep o;
+            // From logits, warps 4-7 scan while warps 0-3 compute the logsumexp.
+            prepare_row<DT, LOGITS, LIST>(p, sh, srow, grow, phase, p.staged != 0, !exclusions, LIST, m, o,
+                                          [&](const char* src, const RowSplit& rs, float xthr) {
+                                              record_scan(std::integral_constant<int, kThreads / 2>{}, src, rs, xthr,
+                                                          tid - kThreads / 2);
+                                          });
+            if (o.aborted) break;
+            constexpr int kLists = LOGITS ? kWarps / 2 : kWarps;
+            const int list_warp = LOGITS ? warp - kWarps / 2 : warp;
+            if constexpr (!LOGITS) {
+                check_inv = !o.inv_known;
+                record_scan(std::integral_constant<int, kThreads>{}, o.src, o.rs, o.xthr, tid);
             }
             const bool invalid = check_inv ? !block_and(!inv3) : o.invalid;
-            if (lane < LIST) sh.wkeys[warp * LIST + lane] = wt.wl;
+            if (list_warp >= 0 && lane < LIST) sh.wkeys[list_warp * LIST + lane] = wt.wl;
             block_sync();
             if (warp == 0) {
-                constexpr int kPer = kWarps * LIST / 32;
+                constexpr int kPer = kLists * LIST / 32;
                 uint64_t mine[kPer];
 #pragma unroll
                 for (int j = 0; j < kPer; ++j) mine[j] = sh.wkeys[lane + 32 * j];

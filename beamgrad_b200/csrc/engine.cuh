@@ -78,6 +78,8 @@ struct DecodeParams {
     float* rlse;            // [B, T, K] each row's logsumexp (from logits)
     uint32_t* rinfo;        // [B, T, K] bit 0: NaN/+inf in the row; bits 8..: entries in rkeys
     uint32_t* count;        // [B, T] rows (and the previous step's selection) that arrived
+    // packed-arithmetic constants (1.0f, 1.0f) and (-0.0f, -0.0f), supplied at run time
+    uint64_t one2, nzero2;
 };
 
 
