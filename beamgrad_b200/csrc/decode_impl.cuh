@@ -57,6 +57,7 @@ struct RowShared {
     float wred[kWarps];
     float wred2[kWarps];
     int ired[kWarps];
+    int nlist[kWarps];  // chained decode: nonzero keys of each warp's record list
     float row_lse;
     float lanes[kLanes];
     int hist[256];
@@ -1032,40 +1033,57 @@ __device__ __forceinline__ float max_nan(float a, float b) {
 // Barrier among the 128 threads of warps 0-3 (id 2) or of warps 4-7 (id 1).
 __device__ __forceinline__ void half_sync(int id) { asm volatile("barrier.sync %0, 128;" ::"r"(id) : "memory"); }
 
-// The R-th largest (R <= RCAP) of the warps' sorted per-thread bounds in sh.wtop, by
-// R rounds of a warp argmax (each round removes exactly one value). One warp.
+// The R-th largest (R <= RCAP) of the warps' sorted per-thread bounds in sh.wtop
+// (warp w's R largest at wtop[w * RCAP + r], descending), written to sh.xbound by the
+// 128 threads of warps 4-7: every value finds its rank in the total order (value,
+// then warp index) by a binary search of each other warp's list; the value of rank
+// R - 1 is the answer.
 template <int RCAP>
-__device__ __forceinline__ float rth_of_thread_bounds(const RowShared& sh, int R) {
-    const int lane = threadIdx.x & 31;
-    constexpr int kPer = kWarps * RCAP / 32;
-    float v[kPer];
-#pragma unroll
-    for (int j = 0; j < kPer; ++j) {
-        const int i = lane + 32 * j;  // i = w * RCAP + r
-        const int w = i / RCAP, r = i % RCAP;
-        v[j] = (w < kWarps && r < R) ? sh.wtop[w * RCAP + r] : f_ninf();
-    }
-    float rth = f_ninf();
-    for (int r = 0; r < R; ++r) {
-        uint64_t best = 0;
-#pragma unroll
-        for (int j = 0; j < kPer; ++j) {
-            const uint32_t u = __float_as_uint(v[j]);
-            const uint32_t od = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
-            const uint64_t key = (static_cast<uint64_t>(od) << 32) | static_cast<uint32_t>(lane + 32 * j + 1);
-            best = key > best ? key : best;
-        }
-        best = warp_max_u64(best);
-        const int owner = static_cast<int>(static_cast<uint32_t>(best)) - 1;
-#pragma unroll
-        for (int j = 0; j < kPer; ++j)
-            if (owner == lane + 32 * j) {
-                rth = v[j];
-                v[j] = f_ninf();
+__device__ __forceinline__ void rth_of_thread_bounds(RowShared& sh, int R) {
+    const int i0 = static_cast<int>(threadIdx.x) - kThreads / 2;
+    for (int i = i0; i < kWarps * R; i += kThreads / 2) {
+        const int w = i / R, r = i - w * R;
+        const float v = sh.wtop[w * RCAP + r];
+        int rank = r;
+        for (int w2 = 0; w2 < kWarps; ++w2) {
+            if (w2 == w) continue;
+            const float* list = sh.wtop + w2 * RCAP;
+            int lo = 0, hi = R;  // entries of w2 ahead of (v, w) form a prefix
+            while (lo < hi) {
+                const int mid = (lo + hi) >> 1;
+                const float e = list[mid];
+                if (e > v || (e == v && w2 < w)) lo = mid + 1;
+                else hi = mid;
             }
-        rth = __shfl_sync(0xffffffffu, rth, owner & 31);
+            rank += lo;
+        }
+        if (rank == R - 1) sh.xbound = v;
     }
-    return rth;
+}
+
+// Rank merge of sorted warp lists: warp w of `nl` list warps holds its LIST best keys
+// in lanes 0..LIST-1 (descending, zeros last, keys unique). Each key's rank is its
+// position plus the number of larger keys in the other lists (binary search); keys
+// of rank < LIST go to out[rank]. Returns the number of nonzero keys of this warp.
+// Called by the nl list warps only, after their lists are in sh.wkeys[w * LIST + lane].
+template <int LIST>
+__device__ __forceinline__ void rank_merge(const RowShared& sh, int nl, int lw, uint64_t key, uint64_t* out) {
+    const int lane = threadIdx.x & 31;
+    if (lane < LIST && key != 0) {
+        int rank = lane;
+        for (int w2 = 0; w2 < nl; ++w2) {
+            if (w2 == lw) continue;
+            const uint64_t* list = sh.wkeys + w2 * LIST;
+            int lo = 0, hi = LIST;
+            while (lo < hi) {
+                const int mid = (lo + hi) >> 1;
+                if (list[mid] > key) lo = mid + 1;
+                else hi = mid;
+            }
+            rank += lo;
+        }
+        if (rank < LIST) out[rank] = key;
+    }
 }
 
 // Entries (v, v + 1) of a row as a packed pair (v even; the pair is aligned).
@@ -1204,19 +1222,13 @@ __device__ __forceinline__ void prepare_row(const DecodeParams& p, RowShared& sh
     }
     const bool make_bound = want_bound && R > 0 && !any_bad;
     if (!LOGITS) {
-        if (make_bound && warp == 4) {
-            const float rth = rth_of_thread_bounds<RCAP>(sh, R);
-            if (lane == 0) sh.xbound = rth;
-        }
+        if (make_bound && warp >= 4) rth_of_thread_bounds<RCAP>(sh, R);
         block_sync();
         if (make_bound) o.xthr = sh.xbound;
         return;
     }
     if (warp >= 4) {
-        if (make_bound && warp == 4) {
-            const float rth = rth_of_thread_bounds<RCAP>(sh, R);
-            if (lane == 0) sh.xbound = rth;
-        }
+        if (make_bound) rth_of_thread_bounds<RCAP>(sh, R);
         half_sync(1);
         side(src, rs, make_bound ? sh.xbound : f_ninf());
     } else {
@@ -1913,8 +1925,14 @@ __global__ void __launch_bounds__(kThreads, 3) decode_chain_kernel(const __grid_
     const uint32_t total = rows_per_step * static_cast<uint32_t>(T);
     const bool exclusions = p.banned != nullptr;
 
+    // Tickets are fetched one row ahead, so the atomic's round trip overlaps a row.
+    uint32_t next_ticket = 0;
+    if (tid == 0) next_ticket = atomicAdd(p.ticket, 1u);
     for (;;) {
-        if (tid == 0) sh.ticket = static_cast<int>(atomicAdd(p.ticket, 1u));
+        if (tid == 0) {
+            sh.ticket = static_cast<int>(next_ticket);
+            if (next_ticket < total) next_ticket = atomicAdd(p.ticket, 1u);
+        }
         block_sync();
         const uint32_t tk = static_cast<uint32_t>(sh.ticket);
         if (tk >= total) break;
@@ -1955,40 +1973,35 @@ __global__ void __launch_bounds__(kThreads, 3) decode_chain_kernel(const __grid_
                                           [&](const char* src, const RowSplit& rs, float xthr) {
                                               record_scan(std::integral_constant<int, kThreads / 2>{}, src, rs, xthr,
                                                           tid - kThreads / 2);
+                                              const int lw = warp - kWarps / 2;
+                                              if (lane < LIST) sh.wkeys[lw * LIST + lane] = wt.wl;
+                                              const unsigned nz = __ballot_sync(0xffffffffu, lane < LIST && wt.wl != 0);
+                                              if (lane == 0) sh.nlist[warp] = __popc(nz);
+                                              half_sync(1);
+                                              rank_merge<LIST>(sh, kWarps / 2, lw, wt.wl, p.rkeys + rowi * LIST);
                                           });
             if (o.aborted) break;
             constexpr int kLists = LOGITS ? kWarps / 2 : kWarps;
-            const int list_warp = LOGITS ? warp - kWarps / 2 : warp;
             if constexpr (!LOGITS) {
                 check_inv = !o.inv_known;
                 record_scan(std::integral_constant<int, kThreads>{}, o.src, o.rs, o.xthr, tid);
             }
             const bool invalid = check_inv ? !block_and(!inv3) : o.invalid;
-            if (list_warp >= 0 && lane < LIST) sh.wkeys[list_warp * LIST + lane] = wt.wl;
-            block_sync();
-            if (warp == 0) {
-                constexpr int kPer = kLists * LIST / 32;
-                uint64_t mine[kPer];
+            // The record: rank merge of the list warps' lists (from logits, warps 4-7 already
+            // did it while warps 0-3 finished the logsumexp).
+            if constexpr (!LOGITS) {
+                if (lane < LIST) sh.wkeys[warp * LIST + lane] = wt.wl;
+                const unsigned nz = __ballot_sync(0xffffffffu, lane < LIST && wt.wl != 0);
+                if (lane == 0) sh.nlist[warp] = __popc(nz);
+                block_sync();
+                rank_merge<LIST>(sh, kWarps, warp, wt.wl, p.rkeys + rowi * LIST);
+            }
+            if (tid == 0) {
+                int total = 0;
 #pragma unroll
-                for (int j = 0; j < kPer; ++j) mine[j] = sh.wkeys[lane + 32 * j];
-                uint64_t out = 0;
-                for (int r = 0; r < LIST; ++r) {
-                    uint64_t bst = 0;
-#pragma unroll
-                    for (int j = 0; j < kPer; ++j) bst = mine[j] > bst ? mine[j] : bst;
-                    const uint64_t w = warp_max_u64(bst);
-                    if (w == 0) break;
-#pragma unroll
-                    for (int j = 0; j < kPer; ++j)
-                        if (mine[j] == w) mine[j] = 0;
-                    if (lane == r) out = w;
-                }
-                const int cnt = __popc(__ballot_sync(0xffffffffu, lane < LIST && out != 0));
-                if (lane < LIST) p.rkeys[rowi * LIST + lane] = out;
-                if (lane == 0) {
-                    p.rlse[rowi] = o.lse;
-                    p.rinfo[rowi] = (invalid ? 1u : 0u) | (static_cast<uint32_t>(cnt) << 8);
-                }
+                for (int w = 0; w < kLists; ++w) total += sh.nlist[kWarps - kLists + w];
+                p.rlse[rowi] = o.lse;
+                p.rinfo[rowi] = (invalid ? 1u : 0u) | (static_cast<uint32_t>(total < LIST ? total : LIST) << 8);
             }
         }
 
