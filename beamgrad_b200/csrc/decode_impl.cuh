@@ -41,6 +41,14 @@ namespace {  // internal to each translation unit that includes this file
 // Shared memory
 // ---------------------------------------------------------------------------
 
+// Scratch of one selecting group.
+struct SelScratch {
+    uint64_t wkeys[kWarps * kFastBeam];
+    unsigned fallback;  // rows whose record is not enough
+    int invalid;
+    int next;           // broadcast of the chain's next step
+};
+
 struct RowShared {
     unsigned long long mbar;
     int ticket;
@@ -69,7 +77,7 @@ struct RowShared {
     // select bookkeeping
     int n_scanned;
     int n_carry;
-    unsigned fallback;  // chained select: rows whose record is not enough
+    SelScratch sel;  // chained decode: the selecting CTA's scratch
 };
 
 // Per-example select arrays of capacity KCAP, in dynamic shared memory.
@@ -130,13 +138,25 @@ __device__ __forceinline__ bool mbar_try_wait(unsigned long long* mbar, uint32_t
     return ok != 0;
 }
 
+// try_wait with a suspend-time hint: the thread sleeps in hardware until the phase
+// completes or about hint_ns pass, instead of spinning.
+__device__ __forceinline__ bool mbar_try_wait_sleep(unsigned long long* mbar, uint32_t phase, uint32_t hint_ns) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred P;\n mbarrier.try_wait.parity.shared::cta.b64 P, [%1], %2, %3;\n selp.u32 %0, 1, 0, P;\n}\n"
+        : "=r"(ok)
+        : "r"(smem_u32(mbar)), "r"(phase), "r"(hint_ns)
+        : "memory");
+    return ok != 0;
+}
+
 // Bounded wait for the row's bulk copy. On timeout: records the error and keeps
 // waiting (bounded again) so no copy is left writing into shared memory.
 __device__ __forceinline__ bool mbar_wait(const DecodeParams& p, unsigned long long* mbar, uint32_t phase) {
     if (mbar_try_wait(mbar, phase)) return true;
     const unsigned long long start = global_ns();
     for (;;) {
-        if (mbar_try_wait(mbar, phase)) return true;
+        if (mbar_try_wait_sleep(mbar, phase, 20000u)) return true;
         if (global_ns() - start > p.timeout_ns) {
             atomicCAS(p.error, kErrNone, kErrTimeout);
             const unsigned long long again = global_ns();
@@ -1033,21 +1053,19 @@ __device__ __forceinline__ float max_nan(float a, float b) {
 // Barrier among the 128 threads of warps 0-3 (id 2) or of warps 4-7 (id 1).
 __device__ __forceinline__ void half_sync(int id) { asm volatile("barrier.sync %0, 128;" ::"r"(id) : "memory"); }
 
-// The R-th largest (R <= RCAP) of the warps' sorted per-thread bounds in sh.wtop
-// (warp w's R largest at wtop[w * RCAP + r], descending), written to sh.xbound by the
-// 128 threads of warps 4-7: every value finds its rank in the total order (value,
-// then warp index) by a binary search of each other warp's list; the value of rank
-// R - 1 is the answer.
-template <int RCAP>
-__device__ __forceinline__ void rth_of_thread_bounds(RowShared& sh, int R) {
-    const int i0 = static_cast<int>(threadIdx.x) - kThreads / 2;
-    for (int i = i0; i < kWarps * R; i += kThreads / 2) {
+// The R-th largest (R <= RCAP) of NW warps' sorted per-thread bounds (warp w's R
+// largest at wtop[w * RCAP + r], descending), written to *out by a group of NT threads
+// (local index ltid): every value finds its rank in the total order (value, then warp
+// index) by a binary search of each other warp's list; the value of rank R - 1 wins.
+template <int NW, int RCAP, int NT>
+__device__ __forceinline__ void rank_rth(const float* wtop, int R, int ltid, float* out) {
+    for (int i = ltid; i < NW * R; i += NT) {
         const int w = i / R, r = i - w * R;
-        const float v = sh.wtop[w * RCAP + r];
+        const float v = wtop[w * RCAP + r];
         int rank = r;
-        for (int w2 = 0; w2 < kWarps; ++w2) {
+        for (int w2 = 0; w2 < NW; ++w2) {
             if (w2 == w) continue;
-            const float* list = sh.wtop + w2 * RCAP;
+            const float* list = wtop + w2 * RCAP;
             int lo = 0, hi = R;  // entries of w2 ahead of (v, w) form a prefix
             while (lo < hi) {
                 const int mid = (lo + hi) >> 1;
@@ -1057,23 +1075,23 @@ __device__ __forceinline__ void rth_of_thread_bounds(RowShared& sh, int R) {
             }
             rank += lo;
         }
-        if (rank == R - 1) sh.xbound = v;
+        if (rank == R - 1) *out = v;
     }
 }
 
-// Rank merge of sorted warp lists: warp w of `nl` list warps holds its LIST best keys
+// Rank merge of sorted warp lists: warp lw of `nl` list warps holds its LIST best keys
 // in lanes 0..LIST-1 (descending, zeros last, keys unique). Each key's rank is its
 // position plus the number of larger keys in the other lists (binary search); keys
-// of rank < LIST go to out[rank]. Returns the number of nonzero keys of this warp.
-// Called by the nl list warps only, after their lists are in sh.wkeys[w * LIST + lane].
+// of rank < LIST go to out[rank]. Called by the nl list warps only, after their lists
+// are in wkeys[w * LIST + lane].
 template <int LIST>
-__device__ __forceinline__ void rank_merge(const RowShared& sh, int nl, int lw, uint64_t key, uint64_t* out) {
+__device__ __forceinline__ void rank_merge(const uint64_t* wkeys, int nl, int lw, uint64_t key, uint64_t* out) {
     const int lane = threadIdx.x & 31;
     if (lane < LIST && key != 0) {
         int rank = lane;
         for (int w2 = 0; w2 < nl; ++w2) {
             if (w2 == lw) continue;
-            const uint64_t* list = sh.wkeys + w2 * LIST;
+            const uint64_t* list = wkeys + w2 * LIST;
             int lo = 0, hi = LIST;
             while (lo < hi) {
                 const int mid = (lo + hi) >> 1;
@@ -1083,6 +1101,111 @@ __device__ __forceinline__ void rank_merge(const RowShared& sh, int nl, int lw, 
             rank += lo;
         }
         if (rank < LIST) out[rank] = key;
+    }
+}
+
+// Entries of a staged row owned by thread ltid of an NT-thread group (chunk c on thread
+// c mod NT, ragged ends on threads 0..n_ends-1), in increasing v.
+template <int DT, int NT, class F>
+__device__ __forceinline__ void for_chunks_n(const char* row, const RowSplit& rs, int ltid, F&& f) {
+    using E = Elem<DT>;
+    constexpr int PER = 16 / E::kBytes;
+    const char* body = row + static_cast<size_t>(rs.head) * E::kBytes;
+    int c = ltid;
+    for (; c + NT < rs.nvec; c += 2 * NT) {
+        const uint4 q0 = *reinterpret_cast<const uint4*>(body + static_cast<size_t>(c) * 16);
+        const uint4 q1 = *reinterpret_cast<const uint4*>(body + static_cast<size_t>(c + NT) * 16);
+        float x0[PER], x1[PER];
+        unpack16<DT>(q0, x0);
+        unpack16<DT>(q1, x1);
+#pragma unroll
+        for (int j = 0; j < PER; ++j) f(x0[j], rs.head + c * PER + j);
+#pragma unroll
+        for (int j = 0; j < PER; ++j) f(x1[j], rs.head + (c + NT) * PER + j);
+    }
+    for (; c < rs.nvec; c += NT) {
+        float x0[PER];
+        unpack16<DT>(*reinterpret_cast<const uint4*>(body + static_cast<size_t>(c) * 16), x0);
+#pragma unroll
+        for (int j = 0; j < PER; ++j) f(x0[j], rs.head + c * PER + j);
+    }
+    if (ltid < rs.n_ends()) {
+        const int v = rs.end_entry(ltid);
+        f(load_elem<DT>(row, v), v);
+    }
+}
+// ---------------------------------------------------------------------------
+// Packed 16-bit pairs (bf16x2 / f16x2 in one 32-bit register). max and min never
+// round, so pass 1 and the record scan can work on pairs: running max / min over a
+// thread's chunks, and a chunk test "largest entry >= threshold" (every threshold
+// is itself an input value or -inf, so the 16-bit comparison is exact).
+// ---------------------------------------------------------------------------
+template <int DT>
+__device__ __forceinline__ uint32_t h2_max_nan(uint32_t a, uint32_t b) {
+    uint32_t r;
+    if constexpr (DT == 2) asm("max.NaN.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+    else asm("max.NaN.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+    return r;
+}
+template <int DT>
+__device__ __forceinline__ uint32_t h2_max(uint32_t a, uint32_t b) {
+    uint32_t r;
+    if constexpr (DT == 2) asm("max.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+    else asm("max.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+    return r;
+}
+template <int DT>
+__device__ __forceinline__ uint32_t h2_min(uint32_t a, uint32_t b) {
+    uint32_t r;
+    if constexpr (DT == 2) asm("min.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+    else asm("min.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+    return r;
+}
+template <int DT>
+__device__ __forceinline__ float h2_lo(uint32_t w) { return Elem<DT>::to_f32(static_cast<uint16_t>(w & 0xffffu)); }
+template <int DT>
+__device__ __forceinline__ float h2_hi(uint32_t w) { return Elem<DT>::to_f32(static_cast<uint16_t>(w >> 16)); }
+template <int DT>
+constexpr uint32_t h2_ninf() { return DT == 2 ? 0xff80ff80u : 0xfc00fc00u; }
+template <int DT>
+constexpr uint32_t h2_inf() { return DT == 2 ? 0x7f807f80u : 0x7c007c00u; }
+
+// Pass 1 of a staged row over one group: NaN-propagating maximum and minimum of the
+// entries the thread owns (for_chunks_n's assignment).
+template <int DT, int NT>
+__device__ __forceinline__ void group_pass1(const char* row, const RowSplit& rs, int ltid, float& mxn, float& mn) {
+    using E = Elem<DT>;
+    mxn = f_ninf();
+    mn = f_inf();
+    if constexpr (E::kBytes == 2) {
+        const char* body = row + static_cast<size_t>(rs.head) * 2;
+        uint32_t mx2 = h2_ninf<DT>(), mn2 = h2_inf<DT>();
+        int c = ltid;
+        for (; c + NT < rs.nvec; c += 2 * NT) {
+            const uint4 q0 = *reinterpret_cast<const uint4*>(body + static_cast<size_t>(c) * 16);
+            const uint4 q1 = *reinterpret_cast<const uint4*>(body + static_cast<size_t>(c + NT) * 16);
+            mx2 = h2_max_nan<DT>(mx2, h2_max_nan<DT>(h2_max_nan<DT>(q0.x, q0.y), h2_max_nan<DT>(q0.z, q0.w)));
+            mn2 = h2_min<DT>(mn2, h2_min<DT>(h2_min<DT>(q0.x, q0.y), h2_min<DT>(q0.z, q0.w)));
+            mx2 = h2_max_nan<DT>(mx2, h2_max_nan<DT>(h2_max_nan<DT>(q1.x, q1.y), h2_max_nan<DT>(q1.z, q1.w)));
+            mn2 = h2_min<DT>(mn2, h2_min<DT>(h2_min<DT>(q1.x, q1.y), h2_min<DT>(q1.z, q1.w)));
+        }
+        for (; c < rs.nvec; c += NT) {
+            const uint4 q0 = *reinterpret_cast<const uint4*>(body + static_cast<size_t>(c) * 16);
+            mx2 = h2_max_nan<DT>(mx2, h2_max_nan<DT>(h2_max_nan<DT>(q0.x, q0.y), h2_max_nan<DT>(q0.z, q0.w)));
+            mn2 = h2_min<DT>(mn2, h2_min<DT>(h2_min<DT>(q0.x, q0.y), h2_min<DT>(q0.z, q0.w)));
+        }
+        mxn = max_nan(h2_lo<DT>(mx2), h2_hi<DT>(mx2));
+        mn = fminf(h2_lo<DT>(mn2), h2_hi<DT>(mn2));
+        if (ltid < rs.n_ends()) {
+            const float x = load_elem<DT>(row, rs.end_entry(ltid));
+            mxn = max_nan(mxn, x);
+            mn = fminf(mn, x);
+        }
+    } else {
+        for_chunks_n<DT, NT>(row, rs, ltid, [&](float x, int) {
+            mxn = max_nan(mxn, x);
+            mn = fminf(mn, x);
+        });
     }
 }
 
@@ -1172,11 +1295,8 @@ __device__ __forceinline__ void prepare_row(const DecodeParams& p, RowShared& sh
     // Pass 1 (16-byte chunks): maximum (NaN-propagating, so one test flags NaN/+inf),
     // minimum, and each thread's maximum, a lower bound on its own best entry; the R-th
     // largest of the 256 thread bounds bounds the row's R-th best entry from below.
-    float mxn = f_ninf(), mn = f_inf();
-    for_chunks<DT>(src, rs, use_smem, [&](float x, int) {
-        mxn = max_nan(mxn, x);
-        mn = fminf(mn, x);
-    });
+    float mxn, mn;
+    group_pass1<DT, kThreads>(src, rs, tid, mxn, mn);
     const bool bad = !(mxn < f_inf());
     if (want_bound) {
         float me = bad ? f_ninf() : mxn;
@@ -1222,13 +1342,13 @@ __device__ __forceinline__ void prepare_row(const DecodeParams& p, RowShared& sh
     }
     const bool make_bound = want_bound && R > 0 && !any_bad;
     if (!LOGITS) {
-        if (make_bound && warp >= 4) rth_of_thread_bounds<RCAP>(sh, R);
+        if (make_bound && warp >= 4) rank_rth<kWarps, RCAP, kThreads / 2>(sh.wtop, R, tid - kThreads / 2, &sh.xbound);
         block_sync();
         if (make_bound) o.xthr = sh.xbound;
         return;
     }
     if (warp >= 4) {
-        if (make_bound) rth_of_thread_bounds<RCAP>(sh, R);
+        if (make_bound) rank_rth<kWarps, RCAP, kThreads / 2>(sh.wtop, R, tid - kThreads / 2, &sh.xbound);
         half_sync(1);
         side(src, rs, make_bound ? sh.xbound : f_ninf());
     } else {
@@ -1773,49 +1893,58 @@ __host__ __device__ constexpr int chain_list_len() {
     return KMAX <= 4 ? 8 : 2 * KMAX;
 }
 
+// A group of NT threads (NT / 32 whole warps; local thread index ltid) that
+// synchronizes on its own named barrier (id 0 with NT = kThreads: the whole CTA).
+template <int NT>
+__device__ __forceinline__ void group_sync(int id) {
+    if (NT == kThreads && id == 0) block_sync();
+    else asm volatile("barrier.sync %0, %1;" ::"r"(id), "r"(NT) : "memory");
+}
+
 // The best KMAX full keys of row (t, b, k), parent state known, scanned from global
-// memory: the fallback of the chained select, written as the row's list.
-template <int DT, bool LOGITS, int KMAX, int LIST>
-__device__ void rescan_row(const DecodeParams& p, RowShared& sh, int t, int b, int k, const Meta& m, float lse) {
+// memory by the group: the fallback of the chained select, written as the row's list.
+template <int DT, bool LOGITS, int KMAX, int LIST, int NT>
+__device__ void rescan_row(const DecodeParams& p, SelScratch& ss, int t, int b, int k, const Meta& m, float lse,
+                           int ltid, int bar) {
     using E = Elem<DT>;
-    const int tid = threadIdx.x;
-    const int lane = tid & 31;
-    const int warp = tid >> 5;
+    constexpr int NW = NT / 32;
+    const int lane = ltid & 31;
+    const int lw = ltid >> 5;
     const int K = p.K, V = p.V;
     const int64_t s = static_cast<int64_t>(b) * K + k;
     const int64_t rowi = (static_cast<int64_t>(b) * p.T + t) * K + k;
     const char* grow = static_cast<const char*>(p.inputs) + rowi * static_cast<int64_t>(V) * E::kBytes;
-    RowCtx c;
-    c.pr = ld_cg(p.raw + s);
-    c.new_len = ld_cg(p.len + s) + 1;
-    c.k = k;
-    c.m = m;
-    c.mask_eos = m.eos >= 0 && c.new_len < m.min_length;
-    c.constrained = false;
-    c.cv = ConsView{nullptr, 0, true};
+    const float pr = ld_cg(p.raw + s);
+    const int new_len = ld_cg(p.len + s) + 1;
+    const bool mask_eos = m.eos >= 0 && new_len < m.min_length;
+    const uint32_t base = static_cast<uint32_t>(k) * static_cast<uint32_t>(V);
     const RowSplit rs = RowSplit::of<E::kBytes>(grow, V);
     WarpTopK<KMAX> wt;
     wt.init(f_ninf());
     if (!LOGITS || lse != f_ninf()) {
-        scan_chunks_ballot<DT>(grow, rs, false, [&](float x) { return x < f_inf() && x != f_ninf(); },
-                               [&](float x, int v, bool valid) {
-                                   uint64_t key = 0;
-                                   if (valid && x < f_inf() && x != f_ninf()) {
-                                       const float lp = LOGITS ? __fsub_rn(x, lse) : x;
-                                       if (lp < f_inf() && lp != f_ninf()) key = full_key(p, sh, c, lp, v);
-                                   }
-                                   wt.offer(key, lane);
-                               });
+        scan_chunks_ballot_n<DT, NT>(grow, rs, false, ltid, [&](float x) { return x < f_inf() && x != f_ninf(); },
+                                     [&](float x, int v, bool valid) {
+                                         uint64_t key = 0;
+                                         if (valid && x < f_inf() && x != f_ninf() && !(p.banned && p.banned[v]) &&
+                                             !(mask_eos && is_eos(p, m, v))) {
+                                             const float lp = LOGITS ? __fsub_rn(x, lse) : x;
+                                             if (lp < f_inf() && lp != f_ninf()) {
+                                                 const float raw = __fadd_rn(pr, lp);
+                                                 if (raw != f_ninf()) key = make_key(raw, base + static_cast<uint32_t>(v));
+                                             }
+                                         }
+                                         wt.offer(key, lane);
+                                     });
     }
-    if (lane < KMAX) sh.wkeys[warp * KMAX + lane] = wt.wl;
-    block_sync();
-    if (warp == 0) {
-        constexpr int kPer = (kWarps * KMAX + 31) / 32;
+    if (lane < KMAX) ss.wkeys[lw * KMAX + lane] = wt.wl;
+    group_sync<NT>(bar);
+    if (lw == 0) {
+        constexpr int kPer = (NW * KMAX + 31) / 32;
         uint64_t mine[kPer];
 #pragma unroll
         for (int j = 0; j < kPer; ++j) {
             const int i = lane + 32 * j;
-            mine[j] = i < kWarps * KMAX ? sh.wkeys[i] : 0;
+            mine[j] = i < NW * KMAX ? ss.wkeys[i] : 0;
         }
         uint64_t out = 0;
         for (int r = 0; r < KMAX; ++r) {
@@ -1830,26 +1959,26 @@ __device__ void rescan_row(const DecodeParams& p, RowShared& sh, int t, int b, i
         }
         if (lane < LIST) p.keys[s * LIST + lane] = lane < KMAX ? out : 0;
     }
-    block_sync();
+    group_sync<NT>(bar);
 }
 
-// Selection of step t of example b from the row records (whole CTA).
-template <int DT, bool LOGITS, int KMAX, int LIST>
-__device__ void chain_select(const DecodeParams& p, RowShared& sh, int t, int b, const Meta& m) {
-    const int tid = threadIdx.x;
-    const int lane = tid & 31;
-    const int warp = tid >> 5;
+// Selection of step t of example b from the row records, by a group of NT threads.
+template <int DT, bool LOGITS, int KMAX, int LIST, int NT>
+__device__ void chain_select(const DecodeParams& p, SelScratch& ss, int t, int b, const Meta& m, int ltid, int bar) {
+    constexpr int NW = NT / 32;
+    const int lane = ltid & 31;
+    const int lw = ltid >> 5;
     const int K = p.K;
     const uint32_t V = static_cast<uint32_t>(p.V);
     const bool active = t < m.steps;
     const int R = m.beam < KMAX ? m.beam : KMAX;
-    if (tid == 0) {
-        sh.fallback = 0;
-        sh.invalid = 0;
+    if (ltid == 0) {
+        ss.fallback = 0;
+        ss.invalid = 0;
     }
-    block_sync();
-    // Warp w turns the records of rows w, w + 8 into candidate keys of parent slot k.
-    for (int k = warp; k < K; k += kWarps) {
+    group_sync<NT>(bar);
+    // Warp w of the group turns the records of rows w, w + NW, ... into candidate keys.
+    for (int k = lw; k < K; k += NW) {
         const int64_t s = static_cast<int64_t>(b) * K + k;
         const int64_t rowi = (static_cast<int64_t>(b) * p.T + t) * K + k;
         bool read = false;
@@ -1884,25 +2013,55 @@ __device__ void chain_select(const DecodeParams& p, RowShared& sh, int t, int b,
             const bool exact = plen == t && (cnt < LIST || raw_r > raw_last);
             if (!exact) {
                 key = 0;
-                if (lane == 0) atomicOr(&sh.fallback, 1u << k);
+                if (lane == 0) atomicOr(&ss.fallback, 1u << k);
             }
-            if (lane == 0 && (info & 1u)) sh.invalid = 1;
+            if (lane == 0 && (info & 1u)) ss.invalid = 1;
         }
         if (lane < LIST) p.keys[s * LIST + lane] = key;
         if (lane == 0 && p.row_lse) p.row_lse[rowi] = (read && LOGITS) ? lse : 0.0f;
     }
-    block_sync();
-    unsigned fb = sh.fallback;
+    group_sync<NT>(bar);
+    unsigned fb = ss.fallback;
     while (fb) {
         const int k = __ffs(fb) - 1;
         fb &= fb - 1;
         const int64_t rowi = (static_cast<int64_t>(b) * p.T + t) * K + k;
-        rescan_row<DT, LOGITS, KMAX, LIST>(p, sh, t, b, k, m, ld_cg(p.rlse + rowi));
+        rescan_row<DT, LOGITS, KMAX, LIST, NT>(p, ss, t, b, k, m, ld_cg(p.rlse + rowi), ltid, bar);
     }
-    if (tid == 0 && sh.invalid && p.out.invalid_input) p.out.invalid_input[b] = 1;
-    block_sync();
-    if (warp == 0) select_fast<KMAX, LIST>(p, t, b, m);
-    block_sync();
+    if (ltid == 0 && ss.invalid && p.out.invalid_input) p.out.invalid_input[b] = 1;
+    group_sync<NT>(bar);
+    if (lw == 0) select_fast<KMAX, LIST>(p, t, b, m);
+    group_sync<NT>(bar);
+}
+
+// Arrival of one finished row (or, with from_step, of the selection of step t - 1) on
+// example b's step-t count; while the group completes counts it selects those steps and
+// arrives for the next. Called by all NT threads of the group after their writes.
+template <int DT, bool LOGITS, int KMAX, int LIST, int NT>
+__device__ __forceinline__ void chain_arrive(const DecodeParams& p, SelScratch& ss, int t, int b, const Meta& m,
+                                             int ltid, int bar) {
+    __threadfence();
+    group_sync<NT>(bar);
+    if (ltid == 0) {
+        const uint32_t target = static_cast<uint32_t>(p.K) + (t > 0 ? 1u : 0u);
+        ss.next = atomicAdd(p.count + static_cast<int64_t>(b) * p.T + t, 1u) == target - 1u ? t : -1;
+    }
+    group_sync<NT>(bar);
+    int ct = ss.next;
+    while (ct >= 0) {
+        __threadfence();
+        chain_select<DT, LOGITS, KMAX, LIST, NT>(p, ss, ct, b, m, ltid, bar);
+        if (ltid == 0) {
+            int nxt = -1;
+            if (ct + 1 < p.T) {
+                __threadfence();
+                if (atomicAdd(p.count + static_cast<int64_t>(b) * p.T + ct + 1, 1u) == static_cast<uint32_t>(p.K)) nxt = ct + 1;
+            }
+            ss.next = nxt;
+        }
+        group_sync<NT>(bar);
+        ct = ss.next;
+    }
 }
 
 template <int DT, bool LOGITS, int KMAX>
@@ -1978,7 +2137,7 @@ __global__ void __launch_bounds__(kThreads, 3) decode_chain_kernel(const __grid_
                                               const unsigned nz = __ballot_sync(0xffffffffu, lane < LIST && wt.wl != 0);
                                               if (lane == 0) sh.nlist[warp] = __popc(nz);
                                               half_sync(1);
-                                              rank_merge<LIST>(sh, kWarps / 2, lw, wt.wl, p.rkeys + rowi * LIST);
+                                              rank_merge<LIST>(sh.wkeys, kWarps / 2, lw, wt.wl, p.rkeys + rowi * LIST);
                                           });
             if (o.aborted) break;
             constexpr int kLists = LOGITS ? kWarps / 2 : kWarps;
@@ -1994,7 +2153,7 @@ __global__ void __launch_bounds__(kThreads, 3) decode_chain_kernel(const __grid_
                 const unsigned nz = __ballot_sync(0xffffffffu, lane < LIST && wt.wl != 0);
                 if (lane == 0) sh.nlist[warp] = __popc(nz);
                 block_sync();
-                rank_merge<LIST>(sh, kWarps, warp, wt.wl, p.rkeys + rowi * LIST);
+                rank_merge<LIST>(sh.wkeys, kWarps, warp, wt.wl, p.rkeys + rowi * LIST);
             }
             if (tid == 0) {
                 int total = 0;
@@ -2006,28 +2165,7 @@ __global__ void __launch_bounds__(kThreads, 3) decode_chain_kernel(const __grid_
         }
 
         // Arrive: the K rows of (t, b), prepared or not, and for t > 0 the selection of t - 1.
-        __threadfence();
-        block_sync();
-        if (tid == 0) {
-            const uint32_t target = static_cast<uint32_t>(K) + (t > 0 ? 1u : 0u);
-            sh.is_last = atomicAdd(p.count + static_cast<int64_t>(b) * T + t, 1u) == target - 1u ? t : -1;
-        }
-        block_sync();
-        int ct = sh.is_last;
-        while (ct >= 0) {
-            __threadfence();
-            chain_select<DT, LOGITS, KMAX, LIST>(p, sh, ct, b, m);
-            if (tid == 0) {
-                int nxt = -1;
-                if (ct + 1 < T) {
-                    __threadfence();
-                    if (atomicAdd(p.count + static_cast<int64_t>(b) * T + ct + 1, 1u) == static_cast<uint32_t>(K)) nxt = ct + 1;
-                }
-                sh.is_last = nxt;
-            }
-            block_sync();
-            ct = sh.is_last;
-        }
+        chain_arrive<DT, LOGITS, KMAX, LIST, kThreads>(p, sh.sel, t, b, m, tid, 0);
     }
 }
 
@@ -2069,6 +2207,9 @@ static cudaError_t launch_decode_as(const DecodeParams& p, cudaStream_t stream, 
     return cudaGetLastError();
 }
 
+// Launch of one (dtype, logits) family: the beam size picks the register top-k width
+// (1..16) or the generic radix-select path; decodes without n-gram blocking or
+// repetition penalty and beams up to 16 run chained.
 template <int DT, bool LOGITS>
 static cudaError_t launch_decode_k(const DecodeParams& p, cudaStream_t stream, int sm_count) {
     const int K = p.K;
