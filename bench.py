@@ -85,25 +85,40 @@ class ClockSampler:
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, index: int):
+    def __init__(self, index: str):
         self.index = index
-        self.rows: list[list[str]] = []
+        self.rows: list[tuple[float, list[str]]] = []
         self.proc = None
+        self.window = (0.0, 0.0)
+        self.extended = False
 
     def __enter__(self):
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
-                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+                 "-lms", "20"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.thread = threading.Thread(target=self._read, daemon=True)
             self.thread.start()
+            deadline = time.monotonic() + 5.0  # start timing only once samples flow
+            while not self.rows and time.monotonic() < deadline:
+                time.sleep(0.01)
         except (OSError, FileNotFoundError):
             self.proc = None
         return self
 
     def _read(self):
         for line in self.proc.stdout:
-            self.rows.append([c.strip() for c in line.split(",")])
+            self.rows.append((time.monotonic(), [c.strip() for c in line.split(",")]))
+
+    def start(self):
+        self.window = (time.monotonic(), float("inf"))
+
+    def stop(self):
+        self.window = (self.window[0], time.monotonic())
+
+    def in_window(self) -> list[list[str]]:
+        t0, t1 = self.window
+        return [r for t, r in self.rows if t0 <= t <= t1]
 
     def __exit__(self, *exc):
         if self.proc is not None:
@@ -114,18 +129,22 @@ class ClockSampler:
                 self.proc.kill()
 
     def summary(self) -> dict:
-        if not self.rows:
+        rows = self.in_window()
+        if not rows:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
-        sm = [float(r[1]) for r in self.rows if len(r) > 2 and r[1].replace(".", "").isdigit()]
-        mx = [float(r[2]) for r in self.rows if len(r) > 2 and r[2].replace(".", "").isdigit()]
+        sm = [float(r[1]) for r in rows if len(r) > 2 and r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if len(r) > 2 and r[2].replace(".", "").isdigit()]
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         reasons = set()
-        for r in self.rows:
+        for r in rows:
             for i, n in enumerate(names):
                 if len(r) > 5 + i and r[5 + i].lower().startswith("active"):
                     reasons.add(n)
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": sorted(reasons), "samples": len(self.rows)}
+        out = {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+               "reasons": sorted(reasons), "samples": len(rows)}
+        if self.extended:
+            out["window"] = "timed region plus untimed decodes after it (the timed region was shorter than a sample)"
+        return out
 
 
 def make_inputs(torch, seed: int, device):
@@ -257,8 +276,13 @@ def main():
     barrier()
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     launch_ms = []
-    with ClockSampler(local) as clocks:
+    try:  # nvidia-smi names the GPU by UUID, whatever CUDA_VISIBLE_DEVICES maps it to
+        gpu_id = f"GPU-{torch.cuda.get_device_properties(dev).uuid}"
+    except (AttributeError, RuntimeError):
+        gpu_id = str(local)
+    with ClockSampler(gpu_id) as clocks:
         barrier()
+        clocks.start()
         start.record(stream)
         for _ in range(args.steps):
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -268,6 +292,16 @@ def main():
             launch_ms.append((e0, e1))
         stop.record(stream)
         barrier()
+        clocks.stop()
+        if clocks.proc is not None and not clocks.in_window():
+            # The timed region fell between two samples: keep the GPU on the same work
+            # (untimed) until one arrives, and say so in the line.
+            clocks.extended = True
+            deadline = time.monotonic() + 2.0
+            while not clocks.in_window() and time.monotonic() < deadline:
+                decode(x)
+                torch.cuda.synchronize(dev)
+                clocks.stop()
     elapsed = start.elapsed_time(stop) / 1e3
     per_launch = statistics.mean(e0.elapsed_time(e1) for e0, e1 in launch_ms) / 1e3
     t_all = torch.tensor([elapsed], device=dev, dtype=torch.float64)
