@@ -90,6 +90,10 @@ def build_lib(force: bool = False, verbose: bool = False, ptxas_info: bool = Fal
     tmp = LIB.with_suffix(".so.tmp")
     _run([nvcc, *ARCH, "-shared", "-Xlinker", "-soname,libdbs_cuda.so.10", "-o", str(tmp), *objs, "-lcudart"], verbose)
     os.replace(tmp, LIB)
+    soname = PKG / "libdbs_cuda.so.10"  # what modules linked against the library ask for
+    if soname.is_symlink() or soname.exists():
+        soname.unlink()
+    soname.symlink_to(LIB.name)
     return LIB
 
 
@@ -110,7 +114,10 @@ def build_torch_ext(force: bool = False, verbose: bool = False) -> Path:
     if not force and not _stale(out, [src, LIB, *INCLUDE.glob("*.h")]):
         return out
     includes = cpp_extension.include_paths(device_type="cuda") if "device_type" in cpp_extension.include_paths.__code__.co_varnames else cpp_extension.include_paths(cuda=True)
-    cxx = os.environ.get("CXX", "g++")
+    # The module must share torch's C++ runtime: errors raised in an operator are C++
+    # exceptions caught inside torch, which breaks if libstdc++ is linked statically
+    # (as some compiler wrappers do). Use the system compiler and verify below.
+    cxx = "/usr/bin/g++" if Path("/usr/bin/g++").exists() else os.environ.get("CXX", "g++")
     py_inc = sysconfig.get_paths()["include"]
     torch_lib = Path(torch.__file__).parent / "lib"
     abi = int(torch._C._GLIBCXX_USE_CXX11_ABI)
@@ -124,6 +131,9 @@ def build_torch_ext(force: bool = False, verbose: bool = False) -> Path:
         "-L/usr/local/cuda/lib64", "-lcudart",
     ]
     _run(cmd, verbose)
+    syms = subprocess.run(["nm", "-D", "--defined-only", str(out.with_suffix(".tmp"))], capture_output=True, text=True).stdout
+    if " __cxa_throw" in syms:
+        raise RuntimeError(f"{out.name} carries its own copy of libstdc++ (built by {cxx}); torch could not catch its errors")
     os.replace(out.with_suffix(".tmp"), out)
     return out
 
