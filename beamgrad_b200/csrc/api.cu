@@ -22,6 +22,7 @@ cudaError_t launch_init(const DecodeParams& p, cudaStream_t stream);
 cudaError_t launch_validate(const DecodeParams& p, int* status, cudaStream_t stream);
 int decode_list_len(int K);
 int decode_chain_list_len(int K);
+size_t decode_chain_wide_smem(int K);
 size_t decode_select_smem(int K);
 
 
@@ -96,10 +97,10 @@ struct DecodeLayout {
     bool chain;
 };
 
-// A decode without n-gram blocking / repetition penalty and with beams up to 16
-// runs chained: rows keep parent-independent records, selections never wait.
+// A decode without n-gram blocking / repetition penalty runs chained: rows keep
+// parent-independent records, selections never wait (the record area is capped).
 bool chain_eligible(const DBSCudaDecodeArgs& a) {
-    if (constrained(a) || a.beam_size > kFastBeam) return false;
+    if (constrained(a)) return false;
     const int64_t rows = static_cast<int64_t>(a.batch_size) * a.steps * a.beam_size;
     return rows * decode_chain_list_len(a.beam_size) * 8 <= kMaxChainRecordBytes;
 }
@@ -252,7 +253,8 @@ int validate_per_example(const DecodeParams& p, const DBSCudaDecodeArgs& a, int3
 void stage_choice(DecodeParams& p, int dtype, bool from_logits) {
     const int64_t row_bytes = static_cast<int64_t>(p.V) * elem_bytes(dtype) + 16;
     const int64_t row_smem = (row_bytes + 127) / 128 * 128;
-    const int64_t sel = static_cast<int64_t>(decode_select_smem(p.K));
+    const int64_t sel = static_cast<int64_t>(p.chain && p.K > kFastBeam ? decode_chain_wide_smem(p.K)
+                                                                         : decode_select_smem(p.K));
     // Rows that fit are staged in shared memory: from logits the three passes read them
     // there; from log-probs the staging lets the load start before the previous step's
     // selection is known.

@@ -93,11 +93,19 @@ int decode_list_len(int K) {
     return K;
 }
 
-// Entries kept per row record of the chained decode (beams up to 16).
+// Entries kept per row record of the chained decode.
 int decode_chain_list_len(int K) {
     if (K <= 4) return chain_list_len<4>();
     if (K <= 8) return chain_list_len<8>();
-    return chain_list_len<16>();
+    if (K <= 16) return chain_list_len<16>();
+    return 2 * K;
+}
+
+// Dynamic shared memory of the chained decode's selection scratch (beams above 16).
+size_t decode_chain_wide_smem(int K) {
+    if (K <= 64) return wide_dyn_smem<64>();
+    if (K <= 256) return wide_dyn_smem<256>();
+    return wide_dyn_smem<kSelectCap>();
 }
 
 size_t decode_select_smem(int K) {

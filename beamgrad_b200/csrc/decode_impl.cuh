@@ -1079,6 +1079,35 @@ __device__ __forceinline__ void rank_rth(const float* wtop, int R, int ltid, flo
     }
 }
 
+// The R-th largest of the warps' sorted thread maxima (R <= kWarps * RCAP) into
+// sh.xbound, by the 128 threads of warps 4-7: R <= RCAP ranks the R largest of each warp;
+// larger R ranks every value of the RCAP-entry lists.
+template <int RCAP>
+__device__ __forceinline__ void bound_rank(RowShared& sh, int R, int ltid) {
+    if (R <= RCAP) {
+        rank_rth<kWarps, RCAP, kThreads / 2>(sh.wtop, R, ltid, &sh.xbound);
+        return;
+    }
+    for (int i = ltid; i < kWarps * RCAP; i += kThreads / 2) {
+        const int w = i / RCAP, r = i - w * RCAP;
+        const float v = sh.wtop[i];
+        int rank = r;
+        for (int w2 = 0; w2 < kWarps; ++w2) {
+            if (w2 == w) continue;
+            const float* list = sh.wtop + w2 * RCAP;
+            int lo = 0, hi = RCAP;
+            while (lo < hi) {
+                const int mid = (lo + hi) >> 1;
+                const float e = list[mid];
+                if (e > v || (e == v && w2 < w)) lo = mid + 1;
+                else hi = mid;
+            }
+            rank += lo;
+        }
+        if (rank == R - 1) sh.xbound = v;
+    }
+}
+
 // Rank merge of sorted warp lists: warp lw of `nl` list warps holds its LIST best keys
 // in lanes 0..LIST-1 (descending, zeros last, keys unique). Each key's rank is its
 // position plus the number of larger keys in the other lists (binary search); keys
@@ -1307,7 +1336,7 @@ __device__ __forceinline__ void prepare_row(const DecodeParams& p, RowShared& sh
                 if (rs.owns(p.extra[i])) me = f_ninf();
         }
         const float sorted = warp_sort_desc(me);
-        if (lane < R) sh.wtop[warp * RCAP + lane] = sorted;
+        if (lane < R && lane < RCAP) sh.wtop[warp * RCAP + lane] = sorted;
     }
     {
         const float wmx = warp_max_f32(bad ? f_ninf() : mxn);
@@ -1340,15 +1369,15 @@ __device__ __forceinline__ void prepare_row(const DecodeParams& p, RowShared& sh
         });
         mx = block_max(sh, mx);
     }
-    const bool make_bound = want_bound && R > 0 && !any_bad;
+    const bool make_bound = want_bound && R > 0 && R <= kWarps * RCAP && !any_bad;
     if (!LOGITS) {
-        if (make_bound && warp >= 4) rank_rth<kWarps, RCAP, kThreads / 2>(sh.wtop, R, tid - kThreads / 2, &sh.xbound);
+        if (make_bound && warp >= 4) bound_rank<RCAP>(sh, R, tid - kThreads / 2);
         block_sync();
         if (make_bound) o.xthr = sh.xbound;
         return;
     }
     if (warp >= 4) {
-        if (make_bound) rank_rth<kWarps, RCAP, kThreads / 2>(sh.wtop, R, tid - kThreads / 2, &sh.xbound);
+        if (make_bound) bound_rank<RCAP>(sh, R, tid - kThreads / 2);
         half_sync(1);
         side(src, rs, make_bound ? sh.xbound : f_ninf());
     } else {
@@ -2034,12 +2063,12 @@ __device__ void chain_select(const DecodeParams& p, SelScratch& ss, int t, int b
     group_sync<NT>(bar);
 }
 
-// Arrival of one finished row (or, with from_step, of the selection of step t - 1) on
-// example b's step-t count; while the group completes counts it selects those steps and
+// Arrival of one finished row (or of the selection of step t - 1) on example b's step-t
+// count; while the group completes counts it selects those steps (select(step)) and
 // arrives for the next. Called by all NT threads of the group after their writes.
-template <int DT, bool LOGITS, int KMAX, int LIST, int NT>
-__device__ __forceinline__ void chain_arrive(const DecodeParams& p, SelScratch& ss, int t, int b, const Meta& m,
-                                             int ltid, int bar) {
+template <int NT, class Select>
+__device__ __forceinline__ void chain_arrive_with(const DecodeParams& p, SelScratch& ss, int t, int b, int ltid,
+                                                  int bar, Select&& select) {
     __threadfence();
     group_sync<NT>(bar);
     if (ltid == 0) {
@@ -2050,7 +2079,7 @@ __device__ __forceinline__ void chain_arrive(const DecodeParams& p, SelScratch& 
     int ct = ss.next;
     while (ct >= 0) {
         __threadfence();
-        chain_select<DT, LOGITS, KMAX, LIST, NT>(p, ss, ct, b, m, ltid, bar);
+        select(ct);
         if (ltid == 0) {
             int nxt = -1;
             if (ct + 1 < p.T) {
@@ -2062,6 +2091,13 @@ __device__ __forceinline__ void chain_arrive(const DecodeParams& p, SelScratch& 
         group_sync<NT>(bar);
         ct = ss.next;
     }
+}
+
+template <int DT, bool LOGITS, int KMAX, int LIST, int NT>
+__device__ __forceinline__ void chain_arrive(const DecodeParams& p, SelScratch& ss, int t, int b, const Meta& m,
+                                             int ltid, int bar) {
+    chain_arrive_with<NT>(p, ss, t, b, ltid, bar,
+                          [&](int ct) { chain_select<DT, LOGITS, KMAX, LIST, NT>(p, ss, ct, b, m, ltid, bar); });
 }
 
 template <int DT, bool LOGITS, int KMAX>
@@ -2207,6 +2243,322 @@ static cudaError_t launch_decode_as(const DecodeParams& p, cudaStream_t stream, 
     return cudaGetLastError();
 }
 
+// ---------------------------------------------------------------------------
+// Chained decode for beams above 16 (up to DBS_CUDA_MAX_BEAM). Row records hold
+// LIST = 2K entries: the entries that reach the filter bound (the LIST-th largest of
+// the 256 thread maxima, LIST <= 256) are collected into shared memory and
+// bitonic-sorted; without a bound, or when more than kWideCand entries reach it, a
+// block radix select over the row takes the LIST best. The selection turns the K
+// records into row lists and merges them with a block radix select (select_step).
+// ---------------------------------------------------------------------------
+constexpr int kWideCand = 2048;  // candidate buffer of the wide record (u64 keys)
+
+struct WideShared {
+    uint64_t cand[kWideCand];
+    int n_cand;
+    unsigned fb[DBS_CUDA_MAX_BEAM / 32];  // rows whose record is not enough
+};
+
+// Every eligible entry of the group's share with x >= thr, appended as an x-key to
+// ws.cand (counted in ws.n_cand; entries past kWideCand are counted, not stored). Four
+// chunks are tested per round, each by its largest entry.
+template <int DT, int NT, class Elig>
+__device__ __forceinline__ void collect_candidates(WideShared& ws, const char* row, const RowSplit& rs, int ltid,
+                                                   float thr, Elig&& eligible) {
+    using E = Elem<DT>;
+    constexpr int PER = 16 / E::kBytes;
+    constexpr int UR = 4;
+    const int lane = ltid & 31;
+    const char* body = row + static_cast<size_t>(rs.head) * E::kBytes;
+    auto push = [&](float x, int v, bool cond) {
+        const unsigned mask = __ballot_sync(0xffffffffu, cond);
+        if (!mask) return;
+        int base = 0;
+        if (lane == 0) base = atomicAdd(&ws.n_cand, __popc(mask));
+        base = __shfl_sync(0xffffffffu, base, 0);
+        const int pos = base + __popc(mask & ((1u << lane) - 1u));
+        if (cond && pos < kWideCand) ws.cand[pos] = make_key(x, static_cast<uint32_t>(v));
+    };
+    auto chunk_top = [&](const uint4& q) -> float {
+        if constexpr (E::kBytes == 2) {
+            const uint32_t m2 = h2_max<DT>(h2_max<DT>(q.x, q.y), h2_max<DT>(q.z, q.w));
+            return fmaxf(h2_lo<DT>(m2), h2_hi<DT>(m2));
+        } else {
+            return fmaxf(fmaxf(__uint_as_float(q.x), __uint_as_float(q.y)), fmaxf(__uint_as_float(q.z), __uint_as_float(q.w)));
+        }
+    };
+    const int rounds = (rs.nvec + NT - 1) / NT;
+    for (int r0 = 0; r0 < rounds; r0 += UR) {
+        uint4 q[UR];
+        bool hit[UR];
+        bool any = false;
+#pragma unroll
+        for (int u = 0; u < UR; ++u) {
+            const int c = ltid + (r0 + u) * NT;
+            q[u] = make_uint4(0u, 0u, 0u, 0u);
+            hit[u] = false;
+            if (r0 + u < rounds && c < rs.nvec) {
+                q[u] = *reinterpret_cast<const uint4*>(body + static_cast<size_t>(c) * 16);
+                hit[u] = chunk_top(q[u]) >= thr;
+            }
+            any |= hit[u];
+        }
+        if (!__any_sync(0xffffffffu, any)) continue;
+#pragma unroll
+        for (int u = 0; u < UR; ++u) {
+            if (!__any_sync(0xffffffffu, hit[u])) continue;
+            const int c = ltid + (r0 + u) * NT;
+            float x[PER];
+            unpack16<DT>(q[u], x);
+#pragma unroll
+            for (int j = 0; j < PER; ++j) {
+                const int v = rs.head + c * PER + j;
+                push(x[j], v, hit[u] && x[j] >= thr && x[j] < f_inf() && x[j] != f_ninf() && eligible(v));
+            }
+        }
+    }
+    const bool valid = ltid < rs.n_ends();
+    const int v = valid ? rs.end_entry(ltid) : 0;
+    const float x = valid ? load_elem<DT>(row, v) : f_ninf();
+    push(x, v, valid && x >= thr && x < f_inf() && eligible(v));
+}
+
+// Sorts ws.cand[0, n) descending (n <= kWideCand) and writes the first min(n, LIST) to out.
+__device__ __forceinline__ int sort_candidates(WideShared& ws, int n, int LIST, uint64_t* out) {
+    int n2 = 1;
+    while (n2 < n) n2 <<= 1;
+    for (int i = n + static_cast<int>(threadIdx.x); i < n2; i += kThreads) ws.cand[i] = 0;
+    block_sync();
+    bitonic_desc(ws.cand, n2);
+    const int cnt = n < LIST ? n : LIST;
+    for (int i = threadIdx.x; i < cnt; i += kThreads) out[i] = ws.cand[i];
+    block_sync();
+    return cnt;
+}
+
+// Fallback of the wide selection: the best K full keys of row (t, b, k) with the parent
+// known, by a block radix select over the row, written as the row's list.
+template <int DT, bool LOGITS>
+__device__ void rescan_row_wide(const DecodeParams& p, RowShared& sh, WideShared& ws, int t, int b, int k,
+                                const Meta& m, float lse) {
+    using E = Elem<DT>;
+    const int K = p.K, V = p.V, LIST = p.list_len;
+    const int64_t s = static_cast<int64_t>(b) * K + k;
+    const int64_t rowi = (static_cast<int64_t>(b) * p.T + t) * K + k;
+    const char* grow = static_cast<const char*>(p.inputs) + rowi * static_cast<int64_t>(V) * E::kBytes;
+    const float pr = ld_cg(p.raw + s);
+    const bool mask_eos = m.eos >= 0 && ld_cg(p.len + s) + 1 < m.min_length;
+    const uint32_t base = static_cast<uint32_t>(k) * static_cast<uint32_t>(V);
+    auto gen = [&](int v) -> uint64_t {
+        const float x = load_elem<DT>(grow, v);
+        if (!(x < f_inf()) || x == f_ninf()) return 0;
+        if (p.banned && p.banned[v]) return 0;
+        if (mask_eos && is_eos(p, m, v)) return 0;
+        const float lp = LOGITS ? __fsub_rn(x, lse) : x;
+        if (!(lp < f_inf()) || lp == f_ninf()) return 0;
+        const float raw = __fadd_rn(pr, lp);
+        return raw == f_ninf() ? 0 : make_key(raw, base + static_cast<uint32_t>(v));
+    };
+    uint64_t* list = p.keys + s * LIST;
+    int cnt = 0;
+    if (!LOGITS || lse != f_ninf()) cnt = block_select(sh, gen, V, K, [&](int pos, uint64_t key) { list[pos] = key; });
+    for (int i = cnt + static_cast<int>(threadIdx.x); i < LIST; i += kThreads) list[i] = 0;
+    block_sync();
+}
+
+// Selection of step t of example b for beams above 16 (whole CTA).
+template <int DT, bool LOGITS, int KCAP>
+__device__ void chain_select_wide(const DecodeParams& p, RowShared& sh, WideShared& ws, SelectShared<KCAP>& ss,
+                                  int t, int b, const Meta& m) {
+    const int tid = threadIdx.x;
+    const int lane = tid & 31;
+    const int warp = tid >> 5;
+    const int K = p.K, LIST = p.list_len;
+    const uint32_t V = static_cast<uint32_t>(p.V);
+    const bool active = t < m.steps;
+    const int R = m.beam;
+    for (int i = tid; i < DBS_CUDA_MAX_BEAM / 32; i += kThreads) ws.fb[i] = 0;
+    if (tid == 0) sh.sel.invalid = 0;
+    block_sync();
+    for (int k = warp; k < K; k += kWarps) {
+        const int64_t s = static_cast<int64_t>(b) * K + k;
+        const int64_t rowi = (static_cast<int64_t>(b) * p.T + t) * K + k;
+        uint64_t* list = p.keys + s * LIST;
+        bool read = false;
+        float pr = 0.0f;
+        int plen = 0;
+        if (active && k < m.beam && (t > 0 || k == 0)) {
+            pr = ld_cg(p.raw + s);
+            plen = ld_cg(p.len + s);
+            const uint8_t ended = ld_cg(p.ended + s);
+            read = f_finite(pr) && !(m.eos >= 0 && ended != 0);
+        }
+        float lse = 0.0f;
+        if (read) {
+            const uint32_t info = ld_cg(p.rinfo + rowi);
+            lse = ld_cg(p.rlse + rowi);
+            const int cnt = static_cast<int>(info >> 8);
+            const uint64_t* rec = p.rkeys + rowi * LIST;
+            auto raw_of = [&](int i) -> float {
+                if (i >= cnt) return f_ninf();
+                const float x = key_raw(ld_cg(rec + i));
+                const float lp = LOGITS ? __fsub_rn(x, lse) : x;
+                return (lp < f_inf() && lp != f_ninf()) ? __fadd_rn(pr, lp) : f_ninf();
+            };
+            // Exactness of the record (raw is non-increasing along it); the record's EOS
+            // masking assumed parent length t.
+            const bool exact = plen == t && (cnt < LIST || raw_of(R - 1) > raw_of(LIST - 1));
+            for (int i = lane; i < LIST; i += 32) {
+                uint64_t key = 0;
+                if (exact && i < cnt) {
+                    const uint64_t xk = ld_cg(rec + i);
+                    const float x = key_raw(xk);
+                    const float lp = LOGITS ? __fsub_rn(x, lse) : x;
+                    if (lp < f_inf() && lp != f_ninf()) {
+                        const float raw = __fadd_rn(pr, lp);
+                        if (raw != f_ninf()) key = make_key(raw, static_cast<uint32_t>(k) * V + key_index(xk));
+                    }
+                }
+                list[i] = key;
+            }
+            if (lane == 0) {
+                if (!exact) atomicOr(&ws.fb[k >> 5], 1u << (k & 31));
+                if (info & 1u) sh.sel.invalid = 1;
+            }
+        } else {
+            for (int i = lane; i < LIST; i += 32) list[i] = 0;
+        }
+        if (lane == 0 && p.row_lse) p.row_lse[rowi] = (read && LOGITS) ? lse : 0.0f;
+    }
+    block_sync();
+    for (int w = 0; w < (K + 31) / 32; ++w) {
+        unsigned bits = ws.fb[w];
+        while (bits) {
+            const int k = w * 32 + __ffs(bits) - 1;
+            bits &= bits - 1;
+            const int64_t rowi = (static_cast<int64_t>(b) * p.T + t) * K + k;
+            rescan_row_wide<DT, LOGITS>(p, sh, ws, t, b, k, m, ld_cg(p.rlse + rowi));
+        }
+    }
+    if (tid == 0 && sh.sel.invalid && p.out.invalid_input) p.out.invalid_input[b] = 1;
+    __threadfence_block();
+    block_sync();
+    select_step<0, KCAP>(p, sh, ss, t, b, m);
+    __threadfence();
+    block_sync();
+}
+
+template <int DT, bool LOGITS, int KCAP>
+__global__ void __launch_bounds__(kThreads, 2) decode_chain_wide_kernel(const __grid_constant__ DecodeParams p) {
+    using E = Elem<DT>;
+    __shared__ RowShared sh;
+    extern __shared__ __align__(128) unsigned char dyn[];
+    auto& ss = *reinterpret_cast<SelectShared<KCAP>*>(dyn);
+    constexpr size_t kSelBytes = (sizeof(SelectShared<KCAP>) + 127) & ~static_cast<size_t>(127);
+    auto& ws = *reinterpret_cast<WideShared*>(dyn + kSelBytes);
+    char* srow = reinterpret_cast<char*>(dyn) + kSelBytes + ((sizeof(WideShared) + 127) & ~static_cast<size_t>(127));
+
+    const int tid = threadIdx.x;
+    const int warp = tid >> 5;
+    if (tid == 0) mbar_init(&sh.mbar);
+    block_sync();
+    uint32_t phase = 0;
+
+    const int K = p.K, V = p.V, T = p.T, LIST = p.list_len;
+    const uint32_t rows_per_step = static_cast<uint32_t>(p.B) * static_cast<uint32_t>(K);
+    const uint32_t total = rows_per_step * static_cast<uint32_t>(T);
+    const bool exclusions = p.banned != nullptr;
+    const bool want_bound = !exclusions && LIST <= kWarps * 32;
+
+    uint32_t next_ticket = 0;
+    if (tid == 0) next_ticket = atomicAdd(p.ticket, 1u);
+    for (;;) {
+        if (tid == 0) {
+            sh.ticket = static_cast<int>(next_ticket);
+            if (next_ticket < total) next_ticket = atomicAdd(p.ticket, 1u);
+        }
+        block_sync();
+        const uint32_t tk = static_cast<uint32_t>(sh.ticket);
+        if (tk >= total) break;
+        const int t = static_cast<int>(tk / rows_per_step);
+        const uint32_t rem = tk - static_cast<uint32_t>(t) * rows_per_step;
+        const int b = static_cast<int>(rem / static_cast<uint32_t>(K));
+        const int k = static_cast<int>(rem - static_cast<uint32_t>(b) * static_cast<uint32_t>(K));
+        const Meta m = load_meta(p, b);
+        const int64_t rowi = (static_cast<int64_t>(b) * T + t) * K + k;
+
+        if (t < m.steps && k < m.beam && (t > 0 || k == 0)) {
+            const char* grow = static_cast<const char*>(p.inputs) + rowi * static_cast<int64_t>(V) * E::kBytes;
+            const bool mask_eos = m.eos >= 0 && t + 1 < m.min_length;
+            auto eligible = [&](int v) { return !(exclusions && p.banned[v]) && !(mask_eos && is_eos(p, m, v)); };
+            if (tid == 0) ws.n_cand = 0;
+            Prep o;
+            // From logits, warps 4-7 collect the entries at or above the bound during pass 2.
+            prepare_row<DT, LOGITS, 32>(p, sh, srow, grow, phase, p.staged != 0, want_bound, LIST, m, o,
+                                        [&](const char* src, const RowSplit& rs, float xthr) {
+                                            if (xthr != f_ninf())
+                                                collect_candidates<DT, kThreads / 2>(ws, src, rs, tid - kThreads / 2,
+                                                                                     xthr, eligible);
+                                        });
+            if (o.aborted) break;
+            bool invalid = o.invalid;
+            if constexpr (!LOGITS) {
+                if (o.xthr != f_ninf()) collect_candidates<DT, kThreads>(ws, o.src, o.rs, tid, o.xthr, eligible);
+                if (!o.inv_known) {
+                    bool bad = false;
+                    for (int v = tid; v < V; v += kThreads) bad |= !(load_elem<DT>(o.src, v) < f_inf());
+                    invalid = !block_and(!bad);
+                }
+            }
+            block_sync();
+            uint64_t* rec = p.rkeys + rowi * LIST;
+            const int n = ws.n_cand;
+            int cnt;
+            if (o.xthr != f_ninf() && n <= kWideCand) {
+                cnt = sort_candidates(ws, n, LIST, rec);
+            } else {
+                auto gen = [&](int v) -> uint64_t {
+                    const float x = load_elem<DT>(o.src, v);
+                    return (x < f_inf() && x != f_ninf() && eligible(v)) ? make_key(x, static_cast<uint32_t>(v)) : 0;
+                };
+                int got = 0;
+                if (!LOGITS || o.lse != f_ninf())
+                    got = block_select(sh, gen, V, LIST, [&](int pos, uint64_t key) { ws.cand[pos] = key; });
+                cnt = sort_candidates(ws, got, LIST, rec);
+            }
+            if (tid == 0) {
+                p.rlse[rowi] = o.lse;
+                p.rinfo[rowi] = (invalid ? 1u : 0u) | (static_cast<uint32_t>(cnt) << 8);
+            }
+        }
+        chain_arrive_with<kThreads>(p, sh.sel, t, b, tid, 0,
+                                    [&](int ct) { chain_select_wide<DT, LOGITS, KCAP>(p, sh, ws, ss, ct, b, m); });
+        (void)warp;
+    }
+}
+
+template <int KCAP>
+constexpr size_t wide_dyn_smem() {
+    return ((sizeof(SelectShared<KCAP>) + 127) & ~static_cast<size_t>(127)) + ((sizeof(WideShared) + 127) & ~static_cast<size_t>(127));
+}
+
+template <int DT, bool LOGITS, int KCAP>
+static cudaError_t launch_chain_wide_as(const DecodeParams& p, cudaStream_t stream, int sm_count) {
+    const size_t dyn = wide_dyn_smem<KCAP>() + (p.staged ? static_cast<size_t>(p.row_smem) : 0);
+    auto kernel = decode_chain_wide_kernel<DT, LOGITS, KCAP>;
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(dyn));
+    if (e != cudaSuccess) return e;
+    int per_sm = 0;
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kThreads, dyn);
+    if (e != cudaSuccess) return e;
+    if (per_sm < 1) per_sm = 1;
+    const int64_t tickets = static_cast<int64_t>(p.B) * p.K * p.T;
+    int64_t grid = static_cast<int64_t>(sm_count) * per_sm;
+    if (grid > tickets) grid = tickets;
+    kernel<<<static_cast<unsigned>(grid), kThreads, dyn, stream>>>(p);
+    return cudaGetLastError();
+}
+
 // Launch of one (dtype, logits) family: the beam size picks the register top-k width
 // (1..16) or the generic radix-select path; decodes without n-gram blocking or
 // repetition penalty and beams up to 16 run chained.
@@ -2218,7 +2570,10 @@ static cudaError_t launch_decode_k(const DecodeParams& p, cudaStream_t stream, i
         if (K <= 2) return launch_chain_as<DT, LOGITS, 2>(p, stream, sm_count);
         if (K <= 4) return launch_chain_as<DT, LOGITS, 4>(p, stream, sm_count);
         if (K <= 8) return launch_chain_as<DT, LOGITS, 8>(p, stream, sm_count);
-        return launch_chain_as<DT, LOGITS, 16>(p, stream, sm_count);
+        if (K <= 16) return launch_chain_as<DT, LOGITS, 16>(p, stream, sm_count);
+        if (K <= 64) return launch_chain_wide_as<DT, LOGITS, 64>(p, stream, sm_count);
+        if (K <= 256) return launch_chain_wide_as<DT, LOGITS, 256>(p, stream, sm_count);
+        return launch_chain_wide_as<DT, LOGITS, kSelectCap>(p, stream, sm_count);
     }
     if (K <= 1) return launch_decode_as<DT, LOGITS, 1>(p, stream, sm_count);
     if (K <= 2) return launch_decode_as<DT, LOGITS, 2>(p, stream, sm_count);
