@@ -97,10 +97,9 @@ struct DecodeLayout {
     bool chain;
 };
 
-// A decode without n-gram blocking / repetition penalty runs chained: rows keep
-// parent-independent records, selections never wait (the record area is capped).
+// A decode runs chained (rows keep parent-independent records, selections never wait)
+// unless its record area would exceed the cap.
 bool chain_eligible(const DBSCudaDecodeArgs& a) {
-    if (constrained(a)) return false;
     const int64_t rows = static_cast<int64_t>(a.batch_size) * a.steps * a.beam_size;
     return rows * decode_chain_list_len(a.beam_size) * 8 <= kMaxChainRecordBytes;
 }

@@ -462,8 +462,8 @@ __device__ __forceinline__ bool sorted_has(const int32_t* a, int n, int v) {
     return lo < n && a[lo] == v;
 }
 
-__device__ __forceinline__ bool cons_blocked(const DecodeParams& p, const RowShared& sh, const ConsView& cv, int v) {
-    if (cv.in_smem) return sorted_has(sh.blocked, sh.n_blocked, v);
+// n-gram blocking / repetition penalty of token v after a prefix read from global memory.
+__device__ __forceinline__ bool prefix_blocked(const DecodeParams& p, const ConsView& cv, int v) {
     const int n = p.ngram;
     if (n == 1) {
         for (int i = 0; i < cv.L; ++i)
@@ -476,13 +476,44 @@ __device__ __forceinline__ bool cons_blocked(const DecodeParams& p, const RowSha
     }
     return false;
 }
-
-__device__ __forceinline__ bool cons_penalised(const DecodeParams& p, const RowShared& sh, const ConsView& cv, int v) {
+__device__ __forceinline__ bool prefix_penalised(const DecodeParams& p, const ConsView& cv, int v) {
     if (!p.penalise) return false;
-    if (cv.in_smem) return sorted_has(sh.penal, sh.n_penal, v);
     for (int i = 0; i < cv.L; ++i)
         if (ld_cg(cv.prefix + i) == v) return true;
     return false;
+}
+
+__device__ __forceinline__ bool cons_blocked(const DecodeParams& p, const RowShared& sh, const ConsView& cv, int v) {
+    return cv.in_smem ? sorted_has(sh.blocked, sh.n_blocked, v) : prefix_blocked(p, cv, v);
+}
+__device__ __forceinline__ bool cons_penalised(const DecodeParams& p, const RowShared& sh, const ConsView& cv, int v) {
+    if (!p.penalise) return false;
+    return cv.in_smem ? sorted_has(sh.penal, sh.n_penal, v) : prefix_penalised(p, cv, v);
+}
+
+// The parent's prefix during a chained decode (double-buffered by step parity), for the
+// constraint checks at selection time; an empty view without constraints.
+__device__ __forceinline__ ConsView chain_prefix(const DecodeParams& p, int t, int64_t s) {
+    ConsView cv{nullptr, 0, false};
+    if ((p.ngram > 0 || p.penalise) && p.prefix[0]) {
+        cv.prefix = p.prefix[t & 1] + s * p.T;
+        cv.L = ld_cg(p.prefix_len[t & 1] + s);
+    }
+    return cv;
+}
+
+// Raw score of record entry x (token v) for a parent with raw pr under the parent's
+// constraints: -inf when the entry is no candidate (blocked, or the score underflows).
+template <bool LOGITS>
+__device__ __forceinline__ float constrained_raw(const DecodeParams& p, const ConsView& cv, float pr, float x, float lse,
+                                                 int v) {
+    float lp = LOGITS ? __fsub_rn(x, lse) : x;
+    if (!(lp < f_inf()) || lp == f_ninf()) return f_ninf();
+    if (cv.prefix) {
+        if (prefix_blocked(p, cv, v)) return f_ninf();
+        if (prefix_penalised(p, cv, v)) lp = __fsub_rn(lp, p.log_penalty);
+    }
+    return __fadd_rn(pr, lp);
 }
 
 // ---------------------------------------------------------------------------
@@ -1947,6 +1978,7 @@ __device__ void rescan_row(const DecodeParams& p, SelScratch& ss, int t, int b, 
     const int new_len = ld_cg(p.len + s) + 1;
     const bool mask_eos = m.eos >= 0 && new_len < m.min_length;
     const uint32_t base = static_cast<uint32_t>(k) * static_cast<uint32_t>(V);
+    const ConsView cv = chain_prefix(p, t, s);
     const RowSplit rs = RowSplit::of<E::kBytes>(grow, V);
     WarpTopK<KMAX> wt;
     wt.init(f_ninf());
@@ -1956,11 +1988,8 @@ __device__ void rescan_row(const DecodeParams& p, SelScratch& ss, int t, int b, 
                                          uint64_t key = 0;
                                          if (valid && x < f_inf() && x != f_ninf() && !(p.banned && p.banned[v]) &&
                                              !(mask_eos && is_eos(p, m, v))) {
-                                             const float lp = LOGITS ? __fsub_rn(x, lse) : x;
-                                             if (lp < f_inf() && lp != f_ninf()) {
-                                                 const float raw = __fadd_rn(pr, lp);
-                                                 if (raw != f_ninf()) key = make_key(raw, base + static_cast<uint32_t>(v));
-                                             }
+                                             const float raw = constrained_raw<LOGITS>(p, cv, pr, x, lse, v);
+                                             if (raw != f_ninf()) key = make_key(raw, base + static_cast<uint32_t>(v));
                                          }
                                          wt.offer(key, lane);
                                      });
@@ -2026,20 +2055,24 @@ __device__ void chain_select(const DecodeParams& p, SelScratch& ss, int t, int b
             lse = ld_cg(p.rlse + rowi);
             const int cnt = static_cast<int>(info >> 8);
             const uint64_t xk = lane < cnt ? ld_cg(p.rkeys + rowi * LIST + lane) : 0;
-            float raw = f_ninf();
+            const ConsView cv = chain_prefix(p, t, s);
+            float raw_plain = f_ninf(), raw = f_ninf();
             if (xk != 0) {
                 const float x = key_raw(xk);
                 const float lp = LOGITS ? __fsub_rn(x, lse) : x;
                 if (lp < f_inf() && lp != f_ninf()) {
-                    raw = __fadd_rn(pr, lp);
+                    raw_plain = __fadd_rn(pr, lp);
+                    raw = cv.prefix ? constrained_raw<LOGITS>(p, cv, pr, x, lse, static_cast<int>(key_index(xk))) : raw_plain;
                     if (raw != f_ninf()) key = make_key(raw, static_cast<uint32_t>(k) * V + key_index(xk));
                 }
             }
-            // Exactness of the record (raw is non-increasing along it); the record's EOS
-            // masking assumed parent length t.
-            const float raw_r = __shfl_sync(0xffffffffu, raw, R - 1);
-            const float raw_last = __shfl_sync(0xffffffffu, raw, LIST - 1);
-            const bool exact = plen == t && (cnt < LIST || raw_r > raw_last);
+            // Exactness of the record: every entry left out has an unconstrained raw score
+            // no higher than the last entry's (raw never decreases as x grows; blocking and
+            // penalties only lower it), so R entries strictly above that prove the row's
+            // best R are here. The record's EOS masking assumed parent length t.
+            const float raw_last = __shfl_sync(0xffffffffu, raw_plain, LIST - 1);
+            const int n_above = __popc(__ballot_sync(0xffffffffu, raw > raw_last));
+            const bool exact = plen == t && (cnt < LIST || n_above >= R);
             if (!exact) {
                 key = 0;
                 if (lane == 0) atomicOr(&ss.fallback, 1u << k);
@@ -2349,14 +2382,13 @@ __device__ void rescan_row_wide(const DecodeParams& p, RowShared& sh, WideShared
     const float pr = ld_cg(p.raw + s);
     const bool mask_eos = m.eos >= 0 && ld_cg(p.len + s) + 1 < m.min_length;
     const uint32_t base = static_cast<uint32_t>(k) * static_cast<uint32_t>(V);
+    const ConsView cv = chain_prefix(p, t, s);
     auto gen = [&](int v) -> uint64_t {
         const float x = load_elem<DT>(grow, v);
         if (!(x < f_inf()) || x == f_ninf()) return 0;
         if (p.banned && p.banned[v]) return 0;
         if (mask_eos && is_eos(p, m, v)) return 0;
-        const float lp = LOGITS ? __fsub_rn(x, lse) : x;
-        if (!(lp < f_inf()) || lp == f_ninf()) return 0;
-        const float raw = __fadd_rn(pr, lp);
+        const float raw = constrained_raw<LOGITS>(p, cv, pr, x, lse, v);
         return raw == f_ninf() ? 0 : make_key(raw, base + static_cast<uint32_t>(v));
     };
     uint64_t* list = p.keys + s * LIST;
@@ -2399,28 +2431,29 @@ __device__ void chain_select_wide(const DecodeParams& p, RowShared& sh, WideShar
             lse = ld_cg(p.rlse + rowi);
             const int cnt = static_cast<int>(info >> 8);
             const uint64_t* rec = p.rkeys + rowi * LIST;
-            auto raw_of = [&](int i) -> float {
-                if (i >= cnt) return f_ninf();
-                const float x = key_raw(ld_cg(rec + i));
+            const ConsView cv = chain_prefix(p, t, s);
+            float raw_last = f_ninf();
+            if (cnt >= LIST) {
+                const float x = key_raw(ld_cg(rec + LIST - 1));
                 const float lp = LOGITS ? __fsub_rn(x, lse) : x;
-                return (lp < f_inf() && lp != f_ninf()) ? __fadd_rn(pr, lp) : f_ninf();
-            };
-            // Exactness of the record (raw is non-increasing along it); the record's EOS
-            // masking assumed parent length t.
-            const bool exact = plen == t && (cnt < LIST || raw_of(R - 1) > raw_of(LIST - 1));
+                if (lp < f_inf() && lp != f_ninf()) raw_last = __fadd_rn(pr, lp);
+            }
+            // Exactness of the record (as in the narrow case): R entries whose constrained raw
+            // is strictly above the last entry's unconstrained raw. The record's EOS masking
+            // assumed parent length t.
+            int above = 0;
             for (int i = lane; i < LIST; i += 32) {
                 uint64_t key = 0;
-                if (exact && i < cnt) {
+                if (i < cnt) {
                     const uint64_t xk = ld_cg(rec + i);
-                    const float x = key_raw(xk);
-                    const float lp = LOGITS ? __fsub_rn(x, lse) : x;
-                    if (lp < f_inf() && lp != f_ninf()) {
-                        const float raw = __fadd_rn(pr, lp);
-                        if (raw != f_ninf()) key = make_key(raw, static_cast<uint32_t>(k) * V + key_index(xk));
-                    }
+                    const float raw = constrained_raw<LOGITS>(p, cv, pr, key_raw(xk), lse, static_cast<int>(key_index(xk)));
+                    if (raw != f_ninf()) key = make_key(raw, static_cast<uint32_t>(k) * V + key_index(xk));
+                    above += raw > raw_last ? 1 : 0;
                 }
                 list[i] = key;
             }
+            above = warp_sum_i32(above);
+            const bool exact = plen == t && (cnt < LIST || above >= R);
             if (lane == 0) {
                 if (!exact) atomicOr(&ws.fb[k >> 5], 1u << (k & 31));
                 if (info & 1u) sh.sel.invalid = 1;

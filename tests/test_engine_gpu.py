@@ -128,6 +128,18 @@ def test_constraints_extra_eos_per_example():
         assert_same(G.engine_decode(pb), oracle.oracle_decode(pb), ctx=f"seed {seed}")
 
 
+@pytest.mark.parametrize("seed", range(6))
+def test_heavy_blocking_records_fall_back(seed):
+    """1-gram blocking over long prefixes in a small vocabulary removes many of a row's best
+    entries at selection time, so row records often cannot prove themselves and the row is
+    rescanned with the parent's constraints."""
+    K = [2, 4, 8, 16, 17, 40][seed]
+    pb = make_problem(2, 14, K, 48 + 3 * seed, seed=500 + seed, eos=5, alpha=0.6, ngram=1,
+                      rep_penalty=1.0 + 0.4 * (seed % 2), from_logits=seed % 2 == 1, dtype=seed % 3,
+                      mode="ties" if seed % 3 == 2 else "continuous")
+    assert_same(G.engine_decode(pb), oracle.oracle_decode(pb), ctx=f"seed {seed}")
+
+
 def test_nan_flags_and_never_selected():
     pb = make_problem(4, 5, 3, 64, mode="naninf", seed=3, eos=1)
     ours = G.engine_decode(pb)
