@@ -1269,6 +1269,45 @@ __device__ __forceinline__ void group_pass1(const char* row, const RowSplit& rs,
     }
 }
 
+// The record scan's ballot loop over one group: a chunk whose largest entry reaches
+// thr() is a hit; hit(x, v, valid) is then called for each of its entries on every
+// lane of the warp (valid = the lane owns the entry), so it may use warp collectives.
+template <int DT, int NT, class Thr, class Hit>
+__device__ __forceinline__ void group_scan(const char* row, const RowSplit& rs, int ltid, Thr&& thr, Hit&& hit) {
+    using E = Elem<DT>;
+    if constexpr (E::kBytes == 2) {
+        const char* body = row + static_cast<size_t>(rs.head) * 2;
+        const int rounds = (rs.nvec + NT - 1) / NT;
+        for (int r = 0; r < rounds; ++r) {
+            const int c = ltid + r * NT;
+            const bool valid = c < rs.nvec;
+            uint4 q = make_uint4(h2_ninf<DT>(), h2_ninf<DT>(), h2_ninf<DT>(), h2_ninf<DT>());
+            if (valid) q = *reinterpret_cast<const uint4*>(body + static_cast<size_t>(c) * 16);
+            const uint32_t m2 = h2_max<DT>(h2_max<DT>(q.x, q.y), h2_max<DT>(q.z, q.w));
+            const float top = fmaxf(h2_lo<DT>(m2), h2_hi<DT>(m2));
+            if (__ballot_sync(0xffffffffu, valid && top >= thr())) {
+                uint32_t w0 = q.x, w1 = q.y, w2 = q.z, w3 = q.w;
+#pragma unroll 1
+                for (int j = 0; j < 8; ++j) {
+                    const float x = (j & 1) ? h2_hi<DT>(w0) : h2_lo<DT>(w0);
+                    hit(x, rs.head + c * 8 + j, valid);
+                    if (j & 1) {
+                        w0 = w1;
+                        w1 = w2;
+                        w2 = w3;
+                    }
+                }
+            }
+        }
+        const bool valid = ltid < rs.n_ends();
+        const int v = valid ? rs.end_entry(ltid) : 0;
+        const float x = valid ? load_elem<DT>(row, v) : f_ninf();
+        if (__ballot_sync(0xffffffffu, valid && x >= thr())) hit(x, v, valid);
+    } else {
+        scan_chunks_ballot_n<DT, NT>(row, rs, true, ltid, [&](float x) { return x >= thr(); }, hit);
+    }
+}
+
 // Entries (v, v + 1) of a row as a packed pair (v even; the pair is aligned).
 template <int DT>
 __device__ __forceinline__ uint64_t load_pair(const char* row, int v) {
@@ -2184,16 +2223,23 @@ __global__ void __launch_bounds__(kThreads, 3) decode_chain_kernel(const __grid_
             auto record_scan = [&](auto nt, const char* src, const RowSplit& rs, float xthr, int ltid) {
                 constexpr int NT = decltype(nt)::value;
                 wt.init(xthr);
-                scan_chunks_ballot_n<DT, NT>(src, rs, p.staged != 0, ltid, [&](float x) {
-                    if (check_inv) inv3 |= !(x < f_inf());
-                    return x >= wt.thr;
-                }, [&](float x, int v, bool valid) {
+                auto hit = [&](float x, int v, bool valid) {
                     uint64_t key = 0;
                     if (valid && x >= wt.thr && x < f_inf() && x != f_ninf() && !(exclusions && p.banned[v]) &&
                         !(mask_eos && is_eos(p, m, v)))
                         key = make_key(x, static_cast<uint32_t>(v));
                     wt.offer(key, lane);
-                });
+                };
+                if (check_inv) {
+                    // No pass 1 ran: the NaN/+inf test needs every entry.
+                    scan_chunks_ballot_n<DT, NT>(src, rs, p.staged != 0, ltid, [&](float x) {
+                        inv3 |= !(x < f_inf());
+                        return x >= wt.thr;
+                    }, hit);
+                } else {
+                    // A chunk is looked at only when its largest entry reaches the threshold.
+                    group_scan<DT, NT>(src, rs, ltid, [&]() { return wt.thr; }, hit);
+                }
             };
             Prep o;
             // From logits, warps 4-7 scan while warps 0-3 compute the logsumexp.
