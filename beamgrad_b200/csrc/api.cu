@@ -254,11 +254,10 @@ void stage_choice(DecodeParams& p, int dtype, bool from_logits) {
     const int64_t row_smem = (row_bytes + 127) / 128 * 128;
     const int64_t sel = static_cast<int64_t>(p.chain && p.K > kFastBeam ? decode_chain_wide_smem(p.K)
                                                                          : decode_select_smem(p.K));
-    // Rows that fit are staged in shared memory: from logits the three passes read them
-    // there; from log-probs the staging lets the load start before the previous step's
-    // selection is known.
-    (void)from_logits;
-    p.staged = row_smem + sel <= kMaxRowSmem ? 1 : 0;
+    // From logits, rows that fit are staged in shared memory, where the three passes read
+    // them. Chained log-prob rows are read from global memory (pass 1, then the record
+    // scan from L2): without a row buffer more CTAs share each SM.
+    p.staged = row_smem + sel <= kMaxRowSmem && (from_logits || !p.chain) ? 1 : 0;
     p.row_smem = p.staged ? static_cast<int>(row_smem) : 0;
 }
 

@@ -168,31 +168,38 @@ __device__ __forceinline__ bool mbar_wait(const DecodeParams& p, unsigned long l
 }
 
 // Row layout in shared memory: the row keeps its global address modulo 16,
-// so the 16-byte-aligned body moves with one bulk copy and the ragged head
-// and tail (under 16 bytes each) with plain loads. Returns the offset of
-// element 0 in the buffer.
+// so the 16-byte-aligned body moves with bulk copies and the ragged head and
+// tail (under 16 bytes each) with plain loads.
+//
+// stage_issue (one thread): the body's bulk copies, completing on mbar.
 template <int EB>
-__device__ __forceinline__ int stage_row(const DecodeParams& p, RowShared& sh, char* sbuf, const char* g,
-                                         int V, uint32_t& phase, bool& ok) {
+__device__ __forceinline__ void stage_issue(char* sbuf, const char* g, int V, unsigned long long* mbar) {
     const uintptr_t g0 = reinterpret_cast<uintptr_t>(g);
     const uintptr_t g1 = g0 + static_cast<uintptr_t>(V) * EB;
     const uintptr_t a0 = (g0 + 15) & ~static_cast<uintptr_t>(15);
     const uintptr_t a1 = g1 & ~static_cast<uintptr_t>(15);
-    const int off = static_cast<int>(g0 & 15);
+    if (a1 <= a0) return;
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    const uint32_t bytes = static_cast<uint32_t>(a1 - a0);
+    mbar_expect_tx(mbar, bytes);
+    constexpr uint32_t kChunk = 1u << 16;
+    for (uint32_t c = 0; c < bytes; c += kChunk) {
+        const uint32_t n = bytes - c < kChunk ? bytes - c : kChunk;
+        bulk_g2s(sbuf + (a0 - (g0 & ~static_cast<uintptr_t>(15))) + c, reinterpret_cast<const char*>(a0) + c, n, mbar);
+    }
+}
+
+// stage_finish (whole CTA): the ragged ends, then the bounded wait for the body (one
+// thread waits, the CTA follows at the barrier). Returns the offset of element 0.
+template <int EB>
+__device__ __forceinline__ int stage_finish(const DecodeParams& p, char* sbuf, const char* g, int V,
+                                            unsigned long long* mbar, uint32_t& phase, bool& ok) {
+    const uintptr_t g0 = reinterpret_cast<uintptr_t>(g);
+    const uintptr_t g1 = g0 + static_cast<uintptr_t>(V) * EB;
+    const uintptr_t a0 = (g0 + 15) & ~static_cast<uintptr_t>(15);
+    const uintptr_t a1 = g1 & ~static_cast<uintptr_t>(15);
     const int tid = threadIdx.x;
     const bool bulk = a1 > a0;
-    if (tid == 0 && bulk) {
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-        const uint32_t bytes = static_cast<uint32_t>(a1 - a0);
-        mbar_expect_tx(&sh.mbar, bytes);
-        constexpr uint32_t kChunk = 1u << 16;
-        for (uint32_t c = 0; c < bytes; c += kChunk) {
-            const uint32_t n = bytes - c < kChunk ? bytes - c : kChunk;
-            bulk_g2s(sbuf + (a0 - (g0 & ~static_cast<uintptr_t>(15))) + c, reinterpret_cast<const char*>(a0) + c, n,
-                     &sh.mbar);
-        }
-    }
-    // Ragged head / tail bytes (element granularity), or the whole row when tiny.
     const uintptr_t head_end = bulk ? a0 : g1;
     const int n_head = static_cast<int>((head_end - g0) / EB);
     const int n_tail = bulk ? static_cast<int>((g1 - a1) / EB) : 0;
@@ -204,11 +211,18 @@ __device__ __forceinline__ int stage_row(const DecodeParams& p, RowShared& sh, c
     }
     ok = true;
     if (bulk) {
-        ok = mbar_wait(p, &sh.mbar, phase);
+        if (tid == 0) ok = mbar_wait(p, mbar, phase);
         phase ^= 1u;
     }
     ok = block_and(ok);
-    return off;
+    return static_cast<int>(g0 & 15);
+}
+
+template <int EB>
+__device__ __forceinline__ int stage_row(const DecodeParams& p, RowShared& sh, char* sbuf, const char* g,
+                                         int V, uint32_t& phase, bool& ok) {
+    if (threadIdx.x == 0) stage_issue<EB>(sbuf, g, V, &sh.mbar);
+    return stage_finish<EB>(p, sbuf, g, V, &sh.mbar, phase, ok);
 }
 
 // ---------------------------------------------------------------------------
@@ -1366,7 +1380,7 @@ __device__ __forceinline__ uint64_t lane_pair_sums(const Pack2& q, const char* r
 template <int DT, bool LOGITS, int RCAP, class Side>
 __device__ __forceinline__ void prepare_row(const DecodeParams& p, RowShared& sh, char* srow, const char* grow,
                                             uint32_t& phase, bool use_smem, bool want_bound, int R, const Meta& m,
-                                            Prep& o, Side&& side) {
+                                            Prep& o, Side&& side, unsigned long long* issued_on = nullptr) {
     using E = Elem<DT>;
     constexpr int EB = E::kBytes;
     const int tid = threadIdx.x;
@@ -1380,8 +1394,10 @@ __device__ __forceinline__ void prepare_row(const DecodeParams& p, RowShared& sh
     o.inv_known = false;
     o.aborted = false;
     if (use_smem) {
+        // issued_on: the body's bulk copy was issued earlier on that mbarrier.
         bool ok = true;
-        o.src = srow + stage_row<EB>(p, sh, srow, grow, V, phase, ok);
+        o.src = srow + (issued_on ? stage_finish<EB>(p, srow, grow, V, issued_on, phase, ok)
+                                  : stage_row<EB>(p, sh, srow, grow, V, phase, ok));
         if (!ok) {
             o.aborted = true;
             return;
@@ -1390,7 +1406,7 @@ __device__ __forceinline__ void prepare_row(const DecodeParams& p, RowShared& sh
     const char* src = o.src;
     o.rs = RowSplit::of<EB>(src, V);
     const RowSplit& rs = o.rs;
-    if (!LOGITS && !(want_bound && use_smem)) return;
+    if (!LOGITS && !want_bound) return;
     // Pass 1 (16-byte chunks): maximum (NaN-propagating, so one test flags NaN/+inf),
     // minimum, and each thread's maximum, a lower bound on its own best entry; the R-th
     // largest of the 256 thread bounds bounds the row's R-th best entry from below.
@@ -2141,16 +2157,19 @@ __device__ void chain_select(const DecodeParams& p, SelScratch& ss, int t, int b
 template <int NT, class Select>
 __device__ __forceinline__ void chain_arrive_with(const DecodeParams& p, SelScratch& ss, int t, int b, int ltid,
                                                   int bar, Select&& select) {
-    __threadfence();
+    // The group's writes are ordered before the arrival by the barrier and the arriving
+    // thread's (cumulative) fence.
     group_sync<NT>(bar);
     if (ltid == 0) {
+        __threadfence();
         const uint32_t target = static_cast<uint32_t>(p.K) + (t > 0 ? 1u : 0u);
         ss.next = atomicAdd(p.count + static_cast<int64_t>(b) * p.T + t, 1u) == target - 1u ? t : -1;
     }
     group_sync<NT>(bar);
     int ct = ss.next;
     while (ct >= 0) {
-        __threadfence();
+        if (ltid == 0) __threadfence();
+        group_sync<NT>(bar);
         select(ct);
         if (ltid == 0) {
             int nxt = -1;
