@@ -1380,7 +1380,7 @@ __device__ __forceinline__ uint64_t lane_pair_sums(const Pack2& q, const char* r
 template <int DT, bool LOGITS, int RCAP, class Side>
 __device__ __forceinline__ void prepare_row(const DecodeParams& p, RowShared& sh, char* srow, const char* grow,
                                             uint32_t& phase, bool use_smem, bool want_bound, int R, const Meta& m,
-                                            Prep& o, Side&& side, unsigned long long* issued_on = nullptr) {
+                                            Prep& o, Side&& side) {
     using E = Elem<DT>;
     constexpr int EB = E::kBytes;
     const int tid = threadIdx.x;
@@ -1394,10 +1394,8 @@ __device__ __forceinline__ void prepare_row(const DecodeParams& p, RowShared& sh
     o.inv_known = false;
     o.aborted = false;
     if (use_smem) {
-        // issued_on: the body's bulk copy was issued earlier on that mbarrier.
         bool ok = true;
-        o.src = srow + (issued_on ? stage_finish<EB>(p, srow, grow, V, issued_on, phase, ok)
-                                  : stage_row<EB>(p, sh, srow, grow, V, phase, ok));
+        o.src = srow + stage_row<EB>(p, sh, srow, grow, V, phase, ok);
         if (!ok) {
             o.aborted = true;
             return;
