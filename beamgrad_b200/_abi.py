@@ -109,6 +109,64 @@ class SearchOptions(C.Structure):
     ]
 
 
+class VocabShardPlan(C.Structure):
+    """DBSCudaVocabShardPlan."""
+
+    _fields_ = [
+        ("world_size", C.c_int32),
+        ("rank", C.c_int32),
+        ("shard_vocab", C.c_int32),
+        ("lanes", C.c_int32),
+        ("list_len", C.c_int32),
+        ("shard_list_len", C.c_int32),
+        ("row_words", C.c_int32),
+        ("reserved0", C.c_int32),
+        ("rows", C.c_int64),
+        ("workspace_bytes", C.c_int64),
+    ]
+
+
+class VocabShardBuffers(C.Structure):
+    """DBSCudaVocabShardBuffers."""
+
+    _fields_ = [
+        ("row_max", _p),
+        ("row_min", _p),
+        ("exchange", _p),
+        ("exchange_all", _p),
+        ("resume", _p),
+        ("stalled", _p),
+        ("rescan_rows", _p),
+        ("rescan_slot", _p),
+        ("rescan", _p),
+        ("rescan_all", _p),
+        ("n_rescan", C.c_int64),
+        ("workspace", _p),
+        ("workspace_bytes", C.c_int64),
+    ]
+
+
+class VocabShardCall(C.Structure):
+    """DBSCudaVocabShardCall."""
+
+    _fields_ = [
+        ("shard_inputs", _p),
+        ("data_type", C.c_int32),
+        ("from_logits", C.c_int32),
+        ("world_size", C.c_int32),
+        ("rank", C.c_int32),
+        ("shard_list_len", C.c_int32),
+        ("reserved0", C.c_int32),
+        ("args", C.POINTER(DecodeArgs)),
+        ("options", C.POINTER(SearchOptions)),
+        ("buffers", VocabShardBuffers),
+        ("outputs", DecodeOutputs),
+        ("row_lse", _p),
+    ]
+
+
+VSHARD_MAX_WORLD = 8
+
 # name -> (restype, argtypes). The 17 reference entry points, then this engine's additions.
 SIGNATURES = {
     "dbs_cuda_available": (C.c_int, []),
@@ -159,9 +217,18 @@ SIGNATURES = {
         C.c_int,
         [_p, C.c_int, C.c_int, C.POINTER(DecodeArgs), C.POINTER(SearchOptions), C.POINTER(DecodeOutputs), _p, _p],
     ),
+    "dbs_cuda_vshard_plan": (C.c_int, [C.POINTER(DecodeArgs), C.c_int, C.c_int, C.c_int, C.c_int,
+                                       C.POINTER(VocabShardPlan)]),
+    "dbs_cuda_vshard_scan": (C.c_int, [C.POINTER(VocabShardCall), _p]),
+    "dbs_cuda_vshard_lanes": (C.c_int, [C.POINTER(VocabShardCall), _p]),
+    "dbs_cuda_vshard_merge": (C.c_int, [C.POINTER(VocabShardCall), _p]),
+    "dbs_cuda_vshard_select": (C.c_int, [C.POINTER(VocabShardCall), _p]),
+    "dbs_cuda_vshard_rescan": (C.c_int, [C.POINTER(VocabShardCall), _p]),
 }
 
-ADDED_SYMBOLS = ("dbs_cuda_b200_abi_version", "dbs_cuda_backtrack", "dbs_cuda_decode_no_alloc")
+VSHARD_SYMBOLS = ("dbs_cuda_vshard_plan", "dbs_cuda_vshard_scan", "dbs_cuda_vshard_lanes", "dbs_cuda_vshard_merge",
+                  "dbs_cuda_vshard_select", "dbs_cuda_vshard_rescan")
+ADDED_SYMBOLS = ("dbs_cuda_b200_abi_version", "dbs_cuda_backtrack", "dbs_cuda_decode_no_alloc") + VSHARD_SYMBOLS
 REFERENCE_SYMBOLS = [n for n in SIGNATURES if n not in ADDED_SYMBOLS]
 
 # Size of the fixed device array behind dbs_cuda_decode_no_alloc (DBS_CUDA_B200_NO_ALLOC_SCRATCH_BYTES).

@@ -39,7 +39,8 @@ NVCC_FLAGS = [
     "-Xcompiler",
     "-fPIC,-ffp-contract=off,-fvisibility=hidden",
 ]
-LIB_SOURCES = ["decode.cu", "decode_f32.cu", "decode_f16.cu", "decode_bf16.cu", "backward.cu", "api.cu", "static_scratch.cu"]
+LIB_SOURCES = ["decode.cu", "decode_f32.cu", "decode_f16.cu", "decode_bf16.cu", "backward.cu", "api.cu", "static_scratch.cu",
+               "vshard.cu"]
 
 
 def _nvcc() -> str:

@@ -33,11 +33,19 @@ cudaError_t launch_length_penalty(const int32_t* lengths, int64_t count, float a
 cudaError_t launch_backtrack(int B, int T, int K, const int32_t* tokens, const int32_t* parents,
                              const int32_t* steps_pe, int64_t* out, cudaStream_t stream);
 
+// vshard.cu
+cudaError_t launch_vshard_scan(const VShardParams& q, int dtype, cudaStream_t stream, int sm_count);
+cudaError_t launch_vshard_lanes(const VShardParams& q, int dtype, cudaStream_t stream, int sm_count);
+cudaError_t launch_vshard_merge(const VShardParams& q, bool logits, cudaStream_t stream, int sm_count);
+cudaError_t launch_vshard_select(const VShardParams& q, bool logits, cudaStream_t stream);
+cudaError_t launch_vshard_rescan(const VShardParams& q, int dtype, bool logits, cudaStream_t stream, int sm_count);
+
 namespace {
 
 constexpr int64_t kAlign = 256;
 constexpr unsigned long long kTimeoutNs = 20ull * 1000ull * 1000ull * 1000ull;  // bounded inter-CTA waits
 constexpr int kMaxRowSmem = 160 * 1024;  // largest row staged in shared memory
+constexpr int64_t kLanesPerRow = 256;     // logsumexp lanes of a row (the reference's fixed order)
 
 std::atomic<int> g_sync{0};
 
@@ -104,7 +112,7 @@ bool chain_eligible(const DBSCudaDecodeArgs& a) {
     return rows * decode_chain_list_len(a.beam_size) * 8 <= kMaxChainRecordBytes;
 }
 
-DecodeLayout make_layout(const DBSCudaDecodeArgs& a, bool step_api) {
+DecodeLayout make_layout(const DBSCudaDecodeArgs& a, bool step_api, bool force_chain = false) {
     DecodeLayout L{};
     const int64_t B = a.batch_size, K = a.beam_size, T = a.steps;
     int64_t off = 0;
@@ -113,7 +121,7 @@ DecodeLayout make_layout(const DBSCudaDecodeArgs& a, bool step_api) {
         off = align_up(off + (bytes > 0 ? bytes : 1));
         return at;
     };
-    L.chain = !step_api && chain_eligible(a);
+    L.chain = !step_api && (force_chain || chain_eligible(a));
     L.list_len = L.chain ? decode_chain_list_len(a.beam_size) : decode_list_len(a.beam_size);
     if (!step_api) {
         L.raw = take(B * K * 4);
@@ -371,6 +379,122 @@ BackwardParams backward_params(const DBSCudaDecodeArgs& a) {
     return p;
 }
 
+// ---------------------------------------------------------------------------
+// Vocabulary-sharded decode (vshard.cu)
+// ---------------------------------------------------------------------------
+int vshard_lanes_log2(int world) {
+    switch (world) {
+        case 1: return 8;
+        case 2: return 7;
+        case 4: return 6;
+        case 8: return 5;
+        default: return -1;
+    }
+}
+
+// Tokens of rank `rank`: L of every full 256-token block, and its part of the last one.
+int64_t vshard_shard_vocab(int64_t V, int world, int rank) {
+    const int64_t L = kLanesPerRow / world;
+    const int64_t nfull = V / kLanesPerRow;
+    int64_t tail = V - nfull * kLanesPerRow - rank * L;
+    tail = tail < 0 ? 0 : (tail > L ? L : tail);
+    return nfull * L + tail;
+}
+
+bool vshard_plan_fill(const DBSCudaDecodeArgs* a, int from_logits, int world, int rank, int shard_list,
+                      DBSCudaVocabShardPlan& pl) {
+    std::memset(&pl, 0, sizeof pl);
+    if (!valid_args(a) || vshard_lanes_log2(world) < 0 || rank < 0 || rank >= world || shard_list < 0) return false;
+    pl.world_size = world;
+    pl.rank = rank;
+    pl.lanes = kLanesPerRow / world;
+    pl.shard_vocab = static_cast<int32_t>(vshard_shard_vocab(a->vocab_size, world, rank));
+    pl.list_len = decode_chain_list_len(a->beam_size);
+    // Up to two shards keep whole records; more keep half (their union still holds far
+    // more than a record, and a row short of entries is rescanned).
+    const int dflt = world <= 2 ? pl.list_len : pl.list_len / 2;
+    pl.shard_list_len = shard_list > 0 ? (shard_list < pl.list_len ? shard_list : pl.list_len) : dflt;
+    pl.row_words = 1 + (from_logits ? pl.lanes / 2 : 0) + pl.shard_list_len;
+    pl.rows = static_cast<int64_t>(a->batch_size) * a->steps * a->beam_size;
+    pl.workspace_bytes = make_layout(*a, false, true).total;
+    return true;
+}
+
+int vshard_setup(const DBSCudaVocabShardCall* c, VShardParams& q) {
+    if (!c || !valid_dtype(c->data_type) || c->reserved0 != 0 || !valid_args(c->args)) {
+        return DBS_CUDA_STATUS_INVALID_ARGUMENT;
+    }
+    const DBSCudaDecodeArgs& a = *c->args;
+    if (!valid_options(c->options, a)) return DBS_CUDA_STATUS_INVALID_ARGUMENT;
+    DBSCudaVocabShardPlan pl;
+    if (!vshard_plan_fill(c->args, c->from_logits, c->world_size, c->rank, c->shard_list_len, pl)) {
+        return DBS_CUDA_STATUS_INVALID_ARGUMENT;
+    }
+    const DBSCudaVocabShardBuffers& bf = c->buffers;
+    if (!bf.row_max || !bf.row_min || !bf.exchange || !bf.exchange_all || !bf.resume || !bf.stalled || !bf.workspace) {
+        return DBS_CUDA_STATUS_INVALID_ARGUMENT;
+    }
+    if (bf.workspace_bytes < pl.workspace_bytes || (pl.shard_vocab > 0 && !c->shard_inputs)) {
+        return DBS_CUDA_STATUS_INVALID_ARGUMENT;
+    }
+    if (bf.n_rescan < 0 || bf.n_rescan > static_cast<int64_t>(a.batch_size) * a.beam_size) {
+        return DBS_CUDA_STATUS_INVALID_ARGUMENT;
+    }
+    if (bf.n_rescan > 0 && (!bf.rescan_rows || !bf.rescan_slot || !bf.rescan || !bf.rescan_all)) {
+        return DBS_CUDA_STATUS_INVALID_ARGUMENT;
+    }
+    const DecodeLayout L = make_layout(a, false, true);
+    char* ws = static_cast<char*>(bf.workspace);
+    auto at = [ws](int64_t off) { return off < 0 ? nullptr : ws + off; };
+    std::memset(&q, 0, sizeof q);
+    DecodeParams& p = q.d;
+    fill_params(p, a, c->options);
+    p.inputs = nullptr;
+    p.step_api = 0;
+    p.raw = reinterpret_cast<float*>(at(L.raw));
+    p.len = reinterpret_cast<int32_t*>(at(L.len));
+    p.ended = reinterpret_cast<uint8_t*>(at(L.ended));
+    p.last = reinterpret_cast<int32_t*>(at(L.last));
+    for (int i = 0; i < 2; ++i) {
+        p.prefix[i] = reinterpret_cast<int32_t*>(at(L.prefix[i]));
+        p.prefix_len[i] = reinterpret_cast<int32_t*>(at(L.prefix_len[i]));
+    }
+    p.out = c->outputs;
+    p.row_lse = c->row_lse;
+    p.keys = reinterpret_cast<uint64_t*>(at(L.keys));
+    p.list_len = L.list_len;
+    p.arrive = reinterpret_cast<uint32_t*>(at(L.arrive));
+    p.flag = reinterpret_cast<int32_t*>(at(L.flag));
+    p.ticket = reinterpret_cast<uint32_t*>(at(L.ticket));
+    p.error = reinterpret_cast<int32_t*>(at(L.error));
+    p.chain = 1;
+    p.rkeys = reinterpret_cast<uint64_t*>(at(L.rkeys));
+    p.rlse = reinterpret_cast<float*>(at(L.rlse));
+    p.rinfo = reinterpret_cast<uint32_t*>(at(L.rinfo));
+    p.count = nullptr;
+    q.world = pl.world_size;
+    q.rank = pl.rank;
+    q.lanes = pl.lanes;
+    q.lanes_log2 = vshard_lanes_log2(pl.world_size);
+    q.shard_v = pl.shard_vocab;
+    q.shard_list = pl.shard_list_len;
+    q.row_words = pl.row_words;
+    q.key_off = pl.row_words - pl.shard_list_len;
+    q.shard = c->shard_inputs;
+    q.row_max = bf.row_max;
+    q.row_min = bf.row_min;
+    q.pack = bf.exchange;
+    q.pack_all = bf.exchange_all;
+    q.resume = bf.resume;
+    q.stalled = bf.stalled;
+    q.rescan_rows = bf.rescan_rows;
+    q.rescan_slot = bf.rescan_slot;
+    q.n_rescan = static_cast<int>(bf.n_rescan);
+    q.rescan = bf.rescan;
+    q.rescan_all = bf.rescan_all;
+    return DBS_CUDA_STATUS_OK;
+}
+
 }  // namespace
 }  // namespace dbsb
 
@@ -566,5 +690,79 @@ DBS_CUDA_EXPORT int dbs_cuda_backtrack(const DBSCudaDecodeArgs* args, const int3
 }
 
 DBS_CUDA_EXPORT int dbs_cuda_b200_abi_version(void) { return DBS_CUDA_B200_ABI_VERSION; }
+
+DBS_CUDA_EXPORT int dbs_cuda_vshard_plan(const DBSCudaDecodeArgs* args, int from_logits, int world_size, int rank,
+                                         int shard_list_len, DBSCudaVocabShardPlan* plan) {
+    if (!plan) return DBS_CUDA_STATUS_INVALID_ARGUMENT;
+    DBSCudaVocabShardPlan pl;
+    if (!vshard_plan_fill(args, from_logits, world_size, rank, shard_list_len, pl)) return DBS_CUDA_STATUS_INVALID_ARGUMENT;
+    *plan = pl;
+    return DBS_CUDA_STATUS_OK;
+}
+
+DBS_CUDA_EXPORT int dbs_cuda_vshard_scan(const DBSCudaVocabShardCall* call, void* stream_ptr) {
+    VShardParams q;
+    int rc = vshard_setup(call, q);
+    if (rc != DBS_CUDA_STATUS_OK) return rc;
+    cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+    const DBSCudaDecodeArgs& a = *call->args;
+    const DecodeLayout L = make_layout(a, false, true);
+    rc = validate_per_example(q.d, a, reinterpret_cast<int32_t*>(static_cast<char*>(call->buffers.workspace) + L.status),
+                              stream);
+    if (rc != DBS_CUDA_STATUS_OK) return rc;
+    const size_t kw = static_cast<size_t>((a.beam_size + 31) / 32);
+    if (launch_init(q.d, stream) != cudaSuccess ||
+        cudaMemsetAsync(q.resume, 0, sizeof(int32_t) * a.batch_size, stream) != cudaSuccess ||
+        cudaMemsetAsync(q.stalled, 0, sizeof(uint32_t) * kw * a.batch_size, stream) != cudaSuccess ||
+        launch_vshard_scan(q, call->data_type, stream, sm_count_of_current_device()) != cudaSuccess) {
+        return DBS_CUDA_STATUS_LAUNCH_FAILED;
+    }
+    return finish(stream, q.d.error);
+}
+
+DBS_CUDA_EXPORT int dbs_cuda_vshard_lanes(const DBSCudaVocabShardCall* call, void* stream_ptr) {
+    VShardParams q;
+    const int rc = vshard_setup(call, q);
+    if (rc != DBS_CUDA_STATUS_OK) return rc;
+    if (!call->from_logits) return DBS_CUDA_STATUS_OK;  // log-probs need no logsumexp
+    cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+    if (launch_vshard_lanes(q, call->data_type, stream, sm_count_of_current_device()) != cudaSuccess) {
+        return DBS_CUDA_STATUS_LAUNCH_FAILED;
+    }
+    return finish(stream, q.d.error);
+}
+
+DBS_CUDA_EXPORT int dbs_cuda_vshard_merge(const DBSCudaVocabShardCall* call, void* stream_ptr) {
+    VShardParams q;
+    const int rc = vshard_setup(call, q);
+    if (rc != DBS_CUDA_STATUS_OK) return rc;
+    cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+    if (launch_vshard_merge(q, call->from_logits != 0, stream, sm_count_of_current_device()) != cudaSuccess) {
+        return DBS_CUDA_STATUS_LAUNCH_FAILED;
+    }
+    return finish(stream, q.d.error);
+}
+
+DBS_CUDA_EXPORT int dbs_cuda_vshard_select(const DBSCudaVocabShardCall* call, void* stream_ptr) {
+    VShardParams q;
+    const int rc = vshard_setup(call, q);
+    if (rc != DBS_CUDA_STATUS_OK) return rc;
+    if (!call->outputs.final_scores) return DBS_CUDA_STATUS_INVALID_ARGUMENT;
+    cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+    if (launch_vshard_select(q, call->from_logits != 0, stream) != cudaSuccess) return DBS_CUDA_STATUS_LAUNCH_FAILED;
+    return finish(stream, q.d.error);
+}
+
+DBS_CUDA_EXPORT int dbs_cuda_vshard_rescan(const DBSCudaVocabShardCall* call, void* stream_ptr) {
+    VShardParams q;
+    const int rc = vshard_setup(call, q);
+    if (rc != DBS_CUDA_STATUS_OK) return rc;
+    cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+    if (launch_vshard_rescan(q, call->data_type, call->from_logits != 0, stream, sm_count_of_current_device()) !=
+        cudaSuccess) {
+        return DBS_CUDA_STATUS_LAUNCH_FAILED;
+    }
+    return finish(stream, q.d.error);
+}
 
 }  // extern "C"

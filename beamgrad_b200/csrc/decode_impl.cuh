@@ -1335,9 +1335,11 @@ __device__ __forceinline__ uint64_t load_pair(const char* row, int v) {
 
 // Pass 2 over the full 256-entry blocks for logsumexp lanes (2j, 2j + 1): thread j sums
 // exp(x - max) of both lanes in increasing v, packed. MASKED: entries with x - max below
-// -87 contribute +0 (adding +0 leaves a non-negative sum unchanged).
+// -87 contribute +0 (adding +0 leaves a non-negative sum unchanged). stride: entries per
+// block in `row` (a vocabulary shard holds stride of each block's 256 lanes).
 template <int DT, bool MASKED>
-__device__ __forceinline__ uint64_t lane_pair_sums(const Pack2& q, const char* row, int nfull, float mx, int j) {
+__device__ __forceinline__ uint64_t lane_pair_sums(const Pack2& q, const char* row, int nfull, float mx, int j,
+                                                   int stride = kLanes) {
     const uint64_t mx2 = f2_splat(mx);
     uint64_t acc = f2_pack(0.0f, 0.0f);
     auto one = [&](uint64_t x2) {
@@ -1359,14 +1361,14 @@ __device__ __forceinline__ uint64_t lane_pair_sums(const Pack2& q, const char* r
     for (; i + 4 <= nfull; i += 4) {
         uint64_t x2[4];
 #pragma unroll
-        for (int u = 0; u < 4; ++u) x2[u] = load_pair<DT>(row, (i + u) * kLanes + 2 * j);
+        for (int u = 0; u < 4; ++u) x2[u] = load_pair<DT>(row, (i + u) * stride + 2 * j);
         uint64_t e[4];
 #pragma unroll
         for (int u = 0; u < 4; ++u) e[u] = one(x2[u]);
 #pragma unroll
         for (int u = 0; u < 4; ++u) acc = f2_add(q, acc, e[u]);
     }
-    for (; i < nfull; ++i) acc = f2_add(q, acc, one(load_pair<DT>(row, i * kLanes + 2 * j)));
+    for (; i < nfull; ++i) acc = f2_add(q, acc, one(load_pair<DT>(row, i * stride + 2 * j)));
     return acc;
 }
 
@@ -2461,10 +2463,15 @@ __device__ void rescan_row_wide(const DecodeParams& p, RowShared& sh, WideShared
     block_sync();
 }
 
-// Selection of step t of example b for beams above 16 (whole CTA).
-template <int DT, bool LOGITS, int KCAP>
-__device__ void chain_select_wide(const DecodeParams& p, RowShared& sh, WideShared& ws, SelectShared<KCAP>& ss,
-                                  int t, int b, const Meta& m) {
+// Selection of step t of example b for beams above 16 (whole CTA). Rows whose record is
+// not enough are marked in ws.fb and handed to fallback() (called by every thread),
+// which fills their lists and returns true, or returns false to stop before the
+// selection (nothing of step t is then written but the read rows' lists and row_lse).
+// A record holds cnt = info >> 8 entries; when cnt reaches the list length or bit 1
+// of info is set, entries may be missing after its last one.
+template <bool LOGITS, int KCAP, class Fallback>
+__device__ bool chain_select_wide_with(const DecodeParams& p, RowShared& sh, WideShared& ws, SelectShared<KCAP>& ss,
+                                       int t, int b, const Meta& m, Fallback&& fallback) {
     const int tid = threadIdx.x;
     const int lane = tid & 31;
     const int warp = tid >> 5;
@@ -2493,11 +2500,12 @@ __device__ void chain_select_wide(const DecodeParams& p, RowShared& sh, WideShar
             const uint32_t info = ld_cg(p.rinfo + rowi);
             lse = ld_cg(p.rlse + rowi);
             const int cnt = static_cast<int>(info >> 8);
+            const bool partial = cnt >= LIST || (info & 2u) != 0;
             const uint64_t* rec = p.rkeys + rowi * LIST;
             const ConsView cv = chain_prefix(p, t, s);
             float raw_last = f_ninf();
-            if (cnt >= LIST) {
-                const float x = key_raw(ld_cg(rec + LIST - 1));
+            if (partial && cnt > 0) {
+                const float x = key_raw(ld_cg(rec + cnt - 1));
                 const float lp = LOGITS ? __fsub_rn(x, lse) : x;
                 if (lp < f_inf() && lp != f_ninf()) raw_last = __fadd_rn(pr, lp);
             }
@@ -2516,7 +2524,7 @@ __device__ void chain_select_wide(const DecodeParams& p, RowShared& sh, WideShar
                 list[i] = key;
             }
             above = warp_sum_i32(above);
-            const bool exact = plen == t && (cnt < LIST || above >= R);
+            const bool exact = plen == t && (!partial || above >= R);
             if (lane == 0) {
                 if (!exact) atomicOr(&ws.fb[k >> 5], 1u << (k & 31));
                 if (info & 1u) sh.sel.invalid = 1;
@@ -2527,14 +2535,11 @@ __device__ void chain_select_wide(const DecodeParams& p, RowShared& sh, WideShar
         if (lane == 0 && p.row_lse) p.row_lse[rowi] = (read && LOGITS) ? lse : 0.0f;
     }
     block_sync();
-    for (int w = 0; w < (K + 31) / 32; ++w) {
-        unsigned bits = ws.fb[w];
-        while (bits) {
-            const int k = w * 32 + __ffs(bits) - 1;
-            bits &= bits - 1;
-            const int64_t rowi = (static_cast<int64_t>(b) * p.T + t) * K + k;
-            rescan_row_wide<DT, LOGITS>(p, sh, ws, t, b, k, m, ld_cg(p.rlse + rowi));
-        }
+    bool any_fb = false;
+    for (int w = 0; w < (K + 31) / 32; ++w) any_fb |= ws.fb[w] != 0;
+    if (any_fb && !fallback()) {
+        block_sync();
+        return false;
     }
     if (tid == 0 && sh.sel.invalid && p.out.invalid_input) p.out.invalid_input[b] = 1;
     __threadfence_block();
@@ -2542,6 +2547,24 @@ __device__ void chain_select_wide(const DecodeParams& p, RowShared& sh, WideShar
     select_step<0, KCAP>(p, sh, ss, t, b, m);
     __threadfence();
     block_sync();
+    return true;
+}
+
+template <int DT, bool LOGITS, int KCAP>
+__device__ void chain_select_wide(const DecodeParams& p, RowShared& sh, WideShared& ws, SelectShared<KCAP>& ss,
+                                  int t, int b, const Meta& m) {
+    chain_select_wide_with<LOGITS, KCAP>(p, sh, ws, ss, t, b, m, [&]() {
+        for (int w = 0; w < (p.K + 31) / 32; ++w) {
+            unsigned bits = ws.fb[w];
+            while (bits) {
+                const int k = w * 32 + __ffs(bits) - 1;
+                bits &= bits - 1;
+                const int64_t rowi = (static_cast<int64_t>(b) * p.T + t) * p.K + k;
+                rescan_row_wide<DT, LOGITS>(p, sh, ws, t, b, k, m, ld_cg(p.rlse + rowi));
+            }
+        }
+        return true;
+    });
 }
 
 template <int DT, bool LOGITS, int KCAP>

@@ -83,6 +83,33 @@ struct DecodeParams {
 };
 
 
+// A vocabulary-sharded decode on rank `rank` of `world` (vshard.cu). Rank r holds the
+// tokens v with (v mod 256) in [r * lanes, (r + 1) * lanes): shard entry i is token
+// (i / lanes) * 256 + r * lanes + i mod lanes, so logsumexp lane j of the reference's
+// fixed order lives whole on rank j / lanes. d describes the whole problem (V is the
+// full vocabulary) and holds the decode state, the merged row records and the outputs.
+struct VShardParams {
+    DecodeParams d;
+    int world, rank;
+    int lanes, lanes_log2;     // lanes per rank (256 / world)
+    int shard_v;               // tokens of this rank
+    int shard_list;            // entries of a row record per rank
+    int row_words;             // 64-bit words per row of the exchange buffer
+    int key_off;               // word of the first record entry in an exchange row
+    const void* shard;         // [B, T, K, shard_v]
+    float* row_max;            // [B * T * K] this rank's row maxima, then (all-reduced) the rows'
+    float* row_min;            // [B * T * K]
+    uint64_t* pack;            // [rows, row_words]: info, lane sums (from logits), record
+    const uint64_t* pack_all;  // [world, rows, row_words]
+    int32_t* resume;           // [B] first step not yet selected (T: done)
+    uint32_t* stalled;         // [B, ceil(K / 32)] rows of step resume[b] waiting for a rescan
+    const int32_t* rescan_rows;  // [n_rescan] b * K + k
+    const int32_t* rescan_slot;  // [B * K] position in rescan_rows or -1
+    int n_rescan;
+    uint64_t* rescan;            // [n_rescan, K]
+    const uint64_t* rescan_all;  // [world, n_rescan, K]
+};
+
 // Everything the backward kernels need.
 struct BackwardParams {
     int B, T, K, V;

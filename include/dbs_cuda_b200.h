@@ -51,6 +51,95 @@ DBS_CUDA_EXPORT int dbs_cuda_decode_no_alloc(const void* inputs, int data_type, 
                                              const DBSCudaDecodeArgs* args, const DBSCudaSearchOptions* options,
                                              const DBSCudaDecodeOutputs* outputs, float* row_lse, void* stream);
 
+/* ------------------------------------------------------------------------
+ * Vocabulary-sharded decode (no counterpart in the reference, which decodes
+ * a whole vocabulary on one device). One process per GPU, world_size ranks
+ * (1, 2, 4 or 8); the decode has the semantics of dbs_cuda_decode_ex2 over
+ * the full [B, T, K, V] input and gives identical outputs on every rank.
+ *
+ * Rank r holds the tokens v with (v mod 256) in [r * 256 / W, (r + 1) * 256 / W)
+ * (W = world_size), in increasing v: its shard is [B, T, K, shard_vocab] with
+ * shard entry i the token (i / L) * 256 + r * L + i mod L, L = 256 / W. A
+ * vocabulary-parallel output projection produces this layout directly when its
+ * weight rows are ordered the same way. Interleaving by lane keeps each of the
+ * reference's 256 logsumexp lanes (src/kernels_scalar.cpp:48-66 of beamgrad
+ * 2.3.0) whole on one rank, so the logsumexp is bit-identical.
+ *
+ * Stages, each asynchronous on `stream`, with the caller's collectives between
+ * them (the same on every rank, in this order):
+ *   dbs_cuda_vshard_scan      row maxima, NaN/+inf flags and row records
+ *   caller:                   all-reduce MAX of buffers.row_max (from logits)
+ *   dbs_cuda_vshard_lanes     this rank's logsumexp lane sums (from logits)
+ *   caller:                   all-gather buffers.exchange into buffers.exchange_all
+ *   dbs_cuda_vshard_merge     logsumexp and merged records of every row
+ *   loop:
+ *     dbs_cuda_vshard_select  the selections of every example from resume[b] on;
+ *                             an example stops at a step whose rows need a rescan
+ *     caller:                 read resume / stalled; done when resume[b] == steps
+ *                             for every b; else list the stalled rows (b * K + k,
+ *                             examples ascending, then k) in rescan_rows, their
+ *                             positions in rescan_slot, and
+ *     dbs_cuda_vshard_rescan  this rank's best K candidates of those rows
+ *     caller:                 all-gather buffers.rescan into buffers.rescan_all
+ * The caller passes the same call (inputs, arguments, buffers, outputs) to
+ * every stage; only the rescan fields change between rounds.
+ * ------------------------------------------------------------------------ */
+#define DBS_CUDA_VSHARD_MAX_WORLD 8
+
+typedef struct DBSCudaVocabShardPlan {
+    int32_t world_size;
+    int32_t rank;
+    int32_t shard_vocab;    /* tokens held by this rank */
+    int32_t lanes;          /* 256 / world_size */
+    int32_t list_len;       /* entries of a merged row record */
+    int32_t shard_list_len; /* entries of a row record per rank */
+    int32_t row_words;      /* 64-bit words per row of the exchange buffer */
+    int32_t reserved0;
+    int64_t rows;           /* batch * steps * beam */
+    int64_t workspace_bytes;
+} DBSCudaVocabShardPlan;
+
+typedef struct DBSCudaVocabShardBuffers {
+    float* row_max;               /* [rows] */
+    float* row_min;               /* [rows] */
+    uint64_t* exchange;           /* [rows, row_words] */
+    const uint64_t* exchange_all; /* [world_size, rows, row_words] */
+    int32_t* resume;              /* [batch]: first step not yet selected, steps when done */
+    uint32_t* stalled;            /* [batch, ceil(beam / 32)]: rows of step resume[b] to rescan */
+    const int32_t* rescan_rows;   /* [n_rescan] */
+    const int32_t* rescan_slot;   /* [batch * beam]: position in rescan_rows, or -1 */
+    uint64_t* rescan;             /* [n_rescan, beam] */
+    const uint64_t* rescan_all;   /* [world_size, n_rescan, beam] */
+    int64_t n_rescan;
+    void* workspace;              /* plan.workspace_bytes; kept by the caller for the whole decode */
+    int64_t workspace_bytes;
+} DBSCudaVocabShardBuffers;
+
+typedef struct DBSCudaVocabShardCall {
+    const void* shard_inputs;     /* [batch, steps, beam, shard_vocab] of data_type */
+    int32_t data_type;
+    int32_t from_logits;
+    int32_t world_size;
+    int32_t rank;
+    int32_t shard_list_len;       /* 0: the default (half the merged record) */
+    int32_t reserved0;
+    const DBSCudaDecodeArgs* args;        /* vocab_size is the full vocabulary */
+    const DBSCudaSearchOptions* options;  /* may be NULL */
+    DBSCudaVocabShardBuffers buffers;
+    DBSCudaDecodeOutputs outputs;         /* as dbs_cuda_decode_ex2; every rank writes all of them */
+    float* row_lse;                       /* [B, T, K] or NULL */
+} DBSCudaVocabShardCall;
+
+DBS_CUDA_EXPORT int dbs_cuda_vshard_plan(const DBSCudaDecodeArgs* args, int from_logits, int world_size, int rank,
+                                         int shard_list_len, DBSCudaVocabShardPlan* plan);
+/* scan also resets the decode state and resume / stalled, and (with
+ * per-example arrays) checks their ranges, waiting for the stream once. */
+DBS_CUDA_EXPORT int dbs_cuda_vshard_scan(const DBSCudaVocabShardCall* call, void* stream);
+DBS_CUDA_EXPORT int dbs_cuda_vshard_lanes(const DBSCudaVocabShardCall* call, void* stream);
+DBS_CUDA_EXPORT int dbs_cuda_vshard_merge(const DBSCudaVocabShardCall* call, void* stream);
+DBS_CUDA_EXPORT int dbs_cuda_vshard_select(const DBSCudaVocabShardCall* call, void* stream);
+DBS_CUDA_EXPORT int dbs_cuda_vshard_rescan(const DBSCudaVocabShardCall* call, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -29,6 +29,12 @@ STRUCTS = {
     "DBSCudaBackwardInputs": A.BackwardInputs,
     "DBSCudaSearchOptions": A.SearchOptions,
 }
+# Structs of the engine's additions (include/dbs_cuda_b200.h).
+B200_STRUCTS = {
+    "DBSCudaVocabShardPlan": A.VocabShardPlan,
+    "DBSCudaVocabShardBuffers": A.VocabShardBuffers,
+    "DBSCudaVocabShardCall": A.VocabShardCall,
+}
 
 
 def declared_functions() -> list[str]:
@@ -64,8 +70,8 @@ def test_no_device_reports_unavailable_without_faulting():
     assert A.load().dbs_cuda_available() == 0
 
 
-def _c_layout(header: Path, tmp_path: Path) -> dict[str, list[int]]:
-    fields = {name: [f[0] for f in cls._fields_] for name, cls in STRUCTS.items()}
+def _c_layout(header: Path, tmp_path: Path, structs=STRUCTS) -> dict[str, list[int]]:
+    fields = {name: [f[0] for f in cls._fields_] for name, cls in structs.items()}
     lines = ["#include <stdio.h>", "#include <stddef.h>", f'#include "{header}"', "int main(void) {"]
     for name, fs in fields.items():
         parts = [f"(int)sizeof({name})"] + [f"(int)offsetof({name}, {f})" for f in fs]
@@ -75,17 +81,20 @@ def _c_layout(header: Path, tmp_path: Path) -> dict[str, list[int]]:
     src = tmp_path / "layout.c"
     src.write_text("\n".join(lines))
     exe = tmp_path / "layout"
-    subprocess.run(["gcc", "-std=c99", "-Wall", "-Werror", "-o", str(exe), str(src)], check=True)
+    subprocess.run(["gcc", "-std=c99", "-Wall", "-Werror", "-I", str(header.parent), "-o", str(exe), str(src)],
+                   check=True)
     out = subprocess.run([str(exe)], capture_output=True, text=True, check=True).stdout
     return {line.split()[0]: [int(v) for v in line.split()[1:]] for line in out.strip().splitlines()}
 
 
-def _ctypes_layout() -> dict[str, list[int]]:
-    return {name: [C.sizeof(cls)] + [getattr(cls, f[0]).offset for f in cls._fields_] for name, cls in STRUCTS.items()}
+def _ctypes_layout(structs=STRUCTS) -> dict[str, list[int]]:
+    return {name: [C.sizeof(cls)] + [getattr(cls, f[0]).offset for f in cls._fields_] for name, cls in structs.items()}
 
 
 def test_struct_layout_matches_ctypes(tmp_path):
     assert _c_layout(ROOT / "include" / "dbs_cuda.h", tmp_path) == _ctypes_layout()
+    b200 = ROOT / "include" / "dbs_cuda_b200.h"
+    assert _c_layout(b200, tmp_path, B200_STRUCTS) == _ctypes_layout(B200_STRUCTS)
 
 
 @pytest.mark.skipif(not REF_HEADER.exists(), reason="reference tree not present")
