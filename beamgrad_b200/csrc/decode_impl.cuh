@@ -111,6 +111,11 @@ __device__ __forceinline__ uint32_t smem_u32(const void* p) {
 // TMA bulk staging of one row
 // ---------------------------------------------------------------------------
 
+// Hint to bring [p, p + bytes) into L2 (p and bytes multiples of 16); no data returns.
+__device__ __forceinline__ void prefetch_l2_bulk(const void* p, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
 __device__ __forceinline__ void mbar_init(unsigned long long* mbar) {
     asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_u32(mbar)) : "memory");
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -344,14 +349,39 @@ __device__ int block_select(RowShared& sh, Gen&& gen, int n, int want, Out&& out
                 if (in && lane == __ffs(peers) - 1) atomicAdd(&sh.hist[digit], __popc(peers));
             }
             block_sync();
-            if (tid == 0) {
-                int rem = sh.remaining;
-                int d = 255;
-                while (d > 0 && sh.hist[d] < rem) rem -= sh.hist[d--];
-                sh.sel_prefix |= static_cast<unsigned long long>(d) << shift;
-                sh.sel_mask |= 255ull << shift;
-                sh.remaining = rem;
-                sh.done = sh.hist[d] == rem;
+            if (tid < 32) {
+                // The boundary bucket: the highest digit d whose count, with every digit above
+                // it, reaches `remaining`. Lane l holds digits 255 - 8l ... 248 - 8l.
+                int h[8];
+                int sum = 0;
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                    h[e] = sh.hist[255 - (lane * 8 + e)];
+                    sum += h[e];
+                }
+                int incl = sum;
+#pragma unroll
+                for (int o = 1; o < 32; o <<= 1) {
+                    const int y = __shfl_up_sync(0xffffffffu, incl, o);
+                    if (lane >= o) incl += y;
+                }
+                const int rem = sh.remaining;
+                const int excl = incl - sum;
+                const unsigned here = __ballot_sync(0xffffffffu, excl < rem && incl >= rem);
+                const int owner = here ? __ffs(here) - 1 : 31;  // no lane: digit 0 (as a full scan ends)
+                if (lane == owner) {
+                    int c = excl, d = 0, e = 0;
+                    for (; e < 8; ++e) {
+                        d = 255 - (lane * 8 + e);
+                        if (d == 0 || c + h[e] >= rem) break;
+                        c += h[e];
+                    }
+                    const int left = rem - c;
+                    sh.sel_prefix |= static_cast<unsigned long long>(d) << shift;
+                    sh.sel_mask |= 255ull << shift;
+                    sh.remaining = left;
+                    sh.done = h[e] == left;
+                }
             }
             block_sync();
             if (sh.done) break;
@@ -562,8 +592,11 @@ __device__ __forceinline__ uint64_t full_key(const DecodeParams& p, const RowSha
 // ---------------------------------------------------------------------------
 // Selection of example b at step t (run by the CTA that finished its last row).
 // ---------------------------------------------------------------------------
+// cand / n_cand (optional, KMAX == 0): the step's candidate keys gathered in shared
+// memory instead of the per-row lists in p.keys.
 template <int KMAX, int KCAP>
-__device__ void select_step(const DecodeParams& p, RowShared& sh, SelectShared<KCAP>& ss, int t, int b, const Meta& m) {
+__device__ void select_step(const DecodeParams& p, RowShared& sh, SelectShared<KCAP>& ss, int t, int b, const Meta& m,
+                            const uint64_t* cand = nullptr, int n_cand = 0) {
     const int tid = threadIdx.x;
     const int K = p.K;
     const int V = p.V;
@@ -621,14 +654,35 @@ __device__ void select_step(const DecodeParams& p, RowShared& sh, SelectShared<K
             block_sync();
             ns = sh.n_scanned;
         } else {
-            const int n = K * p.list_len;
-            ns = block_select(
-                sh, [&](int i) { return ld_cg(lists + i); }, n, m.beam, [&](int pos, uint64_t key) { ss.keys[pos] = key; });
-            int n2 = 1;
-            while (n2 < ns) n2 <<= 1;
-            for (int i = ns + tid; i < n2; i += kThreads) ss.keys[i] = 0;
-            block_sync();
-            bitonic_desc(ss.keys, n2);
+            bool ranked = false;
+            if (cand && n_cand <= 512) {
+                // Few candidates: each key's rank is the number of larger keys (unique keys).
+                for (int i = tid; i < n_cand; i += kThreads) {
+                    const uint64_t key = cand[i];
+                    int rank = 0;
+#pragma unroll 4
+                    for (int j = 0; j < n_cand; ++j) rank += cand[j] > key ? 1 : 0;
+                    if (rank < m.beam) ss.keys[rank] = key;
+                }
+                ns = n_cand < m.beam ? n_cand : m.beam;
+                ranked = true;
+            } else if (cand) {
+                ns = block_select(
+                    sh, [&](int i) { return cand[i]; }, n_cand, m.beam, [&](int pos, uint64_t key) { ss.keys[pos] = key; });
+            } else {
+                const int n = K * p.list_len;
+                ns = block_select(
+                    sh, [&](int i) { return ld_cg(lists + i); }, n, m.beam, [&](int pos, uint64_t key) { ss.keys[pos] = key; });
+            }
+            if (ranked) {
+                block_sync();
+            } else {
+                int n2 = 1;
+                while (n2 < ns) n2 <<= 1;
+                for (int i = ns + tid; i < n2; i += kThreads) ss.keys[i] = 0;
+                block_sync();
+                bitonic_desc(ss.keys, n2);
+            }
         }
         // 2. Scanned candidates' scores; carried-forward finished beams.
         for (int i = tid; i < ns; i += kThreads) {
@@ -1337,7 +1391,7 @@ __device__ __forceinline__ uint64_t load_pair(const char* row, int v) {
 // exp(x - max) of both lanes in increasing v, packed. MASKED: entries with x - max below
 // -87 contribute +0 (adding +0 leaves a non-negative sum unchanged). stride: entries per
 // block in `row` (a vocabulary shard holds stride of each block's 256 lanes).
-template <int DT, bool MASKED>
+template <int DT, bool MASKED, int UR = 4>
 __device__ __forceinline__ uint64_t lane_pair_sums(const Pack2& q, const char* row, int nfull, float mx, int j,
                                                    int stride = kLanes) {
     const uint64_t mx2 = f2_splat(mx);
@@ -1358,15 +1412,15 @@ __device__ __forceinline__ uint64_t lane_pair_sums(const Pack2& q, const char* r
         return f2_pack(lo, hi);
     };
     int i = 0;
-    for (; i + 4 <= nfull; i += 4) {
-        uint64_t x2[4];
+    for (; i + UR <= nfull; i += UR) {
+        uint64_t x2[UR];
 #pragma unroll
-        for (int u = 0; u < 4; ++u) x2[u] = load_pair<DT>(row, (i + u) * stride + 2 * j);
-        uint64_t e[4];
+        for (int u = 0; u < UR; ++u) x2[u] = load_pair<DT>(row, (i + u) * stride + 2 * j);
+        uint64_t e[UR];
 #pragma unroll
-        for (int u = 0; u < 4; ++u) e[u] = one(x2[u]);
+        for (int u = 0; u < UR; ++u) e[u] = one(x2[u]);
 #pragma unroll
-        for (int u = 0; u < 4; ++u) acc = f2_add(q, acc, e[u]);
+        for (int u = 0; u < UR; ++u) acc = f2_add(q, acc, e[u]);
     }
     for (; i < nfull; ++i) acc = f2_add(q, acc, one(load_pair<DT>(row, i * stride + 2 * j)));
     return acc;
@@ -2355,6 +2409,7 @@ struct WideShared {
     uint64_t cand[kWideCand];
     int n_cand;
     unsigned fb[DBS_CUDA_MAX_BEAM / 32];  // rows whose record is not enough
+    unsigned long long thr;               // selection: lower bound on the step's beam-th key
 };
 
 // Every eligible entry of the group's share with x >= thr, appended as an x-key to
@@ -2423,6 +2478,19 @@ __device__ __forceinline__ void collect_candidates(WideShared& ws, const char* r
 
 // Sorts ws.cand[0, n) descending (n <= kWideCand) and writes the first min(n, LIST) to out.
 __device__ __forceinline__ int sort_candidates(WideShared& ws, int n, int LIST, uint64_t* out) {
+    if (n <= 512) {
+        // Up to 512 keys: each key's rank is the number of larger keys (keys are unique),
+        // one pass without a sorting network.
+        for (int i = threadIdx.x; i < n; i += kThreads) {
+            const uint64_t key = ws.cand[i];
+            int rank = 0;
+#pragma unroll 4
+            for (int j = 0; j < n; ++j) rank += ws.cand[j] > key ? 1 : 0;
+            if (rank < LIST) out[rank] = key;
+        }
+        block_sync();
+        return n < LIST ? n : LIST;
+    }
     int n2 = 1;
     while (n2 < n) n2 <<= 1;
     for (int i = n + static_cast<int>(threadIdx.x); i < n2; i += kThreads) ws.cand[i] = 0;
@@ -2463,6 +2531,133 @@ __device__ void rescan_row_wide(const DecodeParams& p, RowShared& sh, WideShared
     block_sync();
 }
 
+// Candidates of step t for an unconstrained buffered selection (K <= 128), gathered into
+// cbuf (count in ws.n_cand). Without constraints a record's raw scores never increase
+// along it (raw = parent raw + (x - lse), x non-increasing), so a record is enough when
+// no entry may be missing after it, or when its entry R - 1 is strictly above its last
+// entry (R = beam): two entries decide it. The first two entries of every exact row
+// sample the step; the beam-th largest sample, ws.thr, bounds the step's beam-th
+// candidate from below (samples are candidates), and each exact row contributes its
+// entries down to the first whose raw score is below the bound's. Rows that are not
+// exact are marked in ws.fb.
+template <bool LOGITS>
+__device__ void gather_sampled(const DecodeParams& p, RowShared& sh, WideShared& ws, int t, int b, const Meta& m,
+                               uint64_t* cbuf) {
+    constexpr int kMaxRows = kWarps * 32 / 2;  // 128: two samples per row in sh.wkeys
+    const int tid = threadIdx.x;
+    const int lane = tid & 31;
+    const int warp = tid >> 5;
+    const int K = p.K, LIST = p.list_len;
+    const uint32_t V = static_cast<uint32_t>(p.V);
+    const bool active = t < m.steps;
+    const int R = m.beam;
+    const int64_t row0 = (static_cast<int64_t>(b) * p.T + t) * K;
+    float* s_pr = sh.lanes;              // parent raw score of row k
+    float* s_lse = sh.lanes + kMaxRows;  // logsumexp of row k
+    int* s_cnt = sh.hist;                // record entries of row k to scan (0: none)
+    // Phase A: thread k takes row k.
+    for (int k = tid; k < K; k += kThreads) {
+        const int64_t s = static_cast<int64_t>(b) * K + k;
+        const int64_t rowi = row0 + k;
+        int scan = 0;
+        float pr = 0.0f, lse = 0.0f;
+        bool read = false;
+        if (active && k < m.beam && (t > 0 || k == 0)) {
+            pr = ld_cg(p.raw + s);
+            const int plen = ld_cg(p.len + s);
+            const uint8_t ended = ld_cg(p.ended + s);
+            const uint32_t info = ld_cg(p.rinfo + rowi);
+            lse = ld_cg(p.rlse + rowi);
+            read = f_finite(pr) && !(m.eos >= 0 && ended != 0);
+            if (read) {
+                const int cnt = static_cast<int>(info >> 8);
+                const bool partial = cnt >= LIST || (info & 2u) != 0;
+                const uint64_t* rec = p.rkeys + rowi * LIST;
+                const uint64_t x0 = cnt > 0 ? ld_cg(rec) : 0;
+                const uint64_t x1 = cnt > 1 ? ld_cg(rec + 1) : 0;
+                const uint64_t xr = (partial && cnt >= R) ? ld_cg(rec + R - 1) : 0;
+                const uint64_t xl = (partial && cnt > 0) ? ld_cg(rec + cnt - 1) : 0;
+                auto raw_of = [&](uint64_t xk) {
+                    const float x = key_raw(xk);
+                    const float lp = LOGITS ? __fsub_rn(x, lse) : x;
+                    return (lp < f_inf() && lp != f_ninf()) ? __fadd_rn(pr, lp) : f_ninf();
+                };
+                auto key_of = [&](uint64_t xk) -> uint64_t {
+                    if (xk == 0) return 0;
+                    const float raw = raw_of(xk);
+                    return raw != f_ninf() ? make_key(raw, static_cast<uint32_t>(k) * V + key_index(xk)) : 0;
+                };
+                bool exact = plen == t;
+                if (partial) exact = exact && cnt >= R && raw_of(xr) > raw_of(xl);
+                if (exact) {
+                    scan = cnt;
+                    sh.wkeys[2 * k] = key_of(x0);
+                    sh.wkeys[2 * k + 1] = key_of(x1);
+                } else {
+                    atomicOr(&ws.fb[k >> 5], 1u << (k & 31));
+                }
+                if (info & 1u) sh.sel.invalid = 1;
+            }
+        }
+        s_pr[k] = pr;
+        s_lse[k] = lse;
+        s_cnt[k] = scan;
+        if (p.row_lse) p.row_lse[rowi] = (read && LOGITS) ? lse : 0.0f;
+    }
+    block_sync();
+    // The bound: the sample of rank R - 1 (keys are unique); 0 with fewer than R samples.
+    for (int i = tid; i < 2 * K; i += kThreads) {
+        const uint64_t v = sh.wkeys[i];
+        if (v == 0) continue;
+        int rank = 0;
+#pragma unroll 8
+        for (int j = 0; j < 2 * K; ++j) rank += sh.wkeys[j] > v ? 1 : 0;
+        if (rank == R - 1) ws.thr = v;
+    }
+    block_sync();
+    const uint64_t thr = ws.thr;
+    const float thr_raw = thr ? key_raw(thr) : f_ninf();
+    // Phase B: warp w takes rows w, w + kWarps, ...; the first 32 entries of all its rows
+    // are loaded before any is used.
+    constexpr int kMaxJ = kMaxRows / kWarps;
+    uint64_t first[kMaxJ];
+#pragma unroll
+    for (int j = 0; j < kMaxJ; ++j) {
+        const int k = warp + kWarps * j;
+        first[j] = (k < K && lane < s_cnt[k]) ? ld_cg(p.rkeys + (row0 + k) * LIST + lane) : 0;
+    }
+    const unsigned lt = (1u << lane) - 1u;
+#pragma unroll
+    for (int j = 0; j < kMaxJ; ++j) {
+        const int k = warp + kWarps * j;
+        if (k >= K) break;
+        const int sc = s_cnt[k];
+        if (sc == 0) continue;
+        const float pr = s_pr[k], lse = s_lse[k];
+        const uint64_t* rec = p.rkeys + (row0 + k) * LIST;
+        uint64_t xk = first[j];
+        for (int c0 = 0; c0 < sc; c0 += 32) {
+            if (c0 > 0) xk = c0 + lane < sc ? ld_cg(rec + c0 + lane) : 0;
+            float raw = f_ninf();
+            uint64_t key = 0;
+            const bool have = c0 + lane < sc && xk != 0;
+            if (have) {
+                const float x = key_raw(xk);
+                const float lp = LOGITS ? __fsub_rn(x, lse) : x;
+                if (lp < f_inf() && lp != f_ninf()) raw = __fadd_rn(pr, lp);
+                if (raw != f_ninf()) key = make_key(raw, static_cast<uint32_t>(k) * V + key_index(xk));
+            }
+            const unsigned take = __ballot_sync(0xffffffffu, key != 0 && key >= thr);
+            int base = 0;
+            if (lane == 0 && take) base = atomicAdd(&ws.n_cand, __popc(take));
+            base = __shfl_sync(0xffffffffu, base, 0);
+            if ((take >> lane) & 1u) cbuf[base + __popc(take & lt)] = key;
+            // Entries after one below the bound's raw score are below the bound.
+            if (__any_sync(0xffffffffu, have && !(raw >= thr_raw))) break;
+        }
+    }
+}
+
 // Selection of step t of example b for beams above 16 (whole CTA). Rows whose record is
 // not enough are marked in ws.fb and handed to fallback() (called by every thread),
 // which fills their lists and returns true, or returns false to stop before the
@@ -2471,7 +2666,9 @@ __device__ void rescan_row_wide(const DecodeParams& p, RowShared& sh, WideShared
 // of info is set, entries may be missing after its last one.
 template <bool LOGITS, int KCAP, class Fallback>
 __device__ bool chain_select_wide_with(const DecodeParams& p, RowShared& sh, WideShared& ws, SelectShared<KCAP>& ss,
-                                       int t, int b, const Meta& m, Fallback&& fallback) {
+                                       int t, int b, const Meta& m, Fallback&& fallback, uint64_t* cbuf = nullptr,
+                                       int cap = 0) {
+    constexpr int kRegKeys = 8;  // record entries per lane kept in registers (LIST <= 256)
     const int tid = threadIdx.x;
     const int lane = tid & 31;
     const int warp = tid >> 5;
@@ -2479,72 +2676,261 @@ __device__ bool chain_select_wide_with(const DecodeParams& p, RowShared& sh, Wid
     const uint32_t V = static_cast<uint32_t>(p.V);
     const bool active = t < m.steps;
     const int R = m.beam;
+    // With a shared-memory buffer that holds every row's record, the candidates are
+    // gathered there (non-zero keys only) and the selection reads them from it.
+    const bool use_buf = cbuf != nullptr && LIST <= 32 * kRegKeys && K * LIST <= cap;
+    // Buffered mode with up to 128 rows: the first two entries of every exact row are
+    // kept as samples; the beam-th largest sample bounds the step's beam-th candidate
+    // from below (the samples are candidates), and only candidates at or above it go on
+    // to the radix select.
+    const bool sample = use_buf && 2 * K <= kWarps * 32;
+    const bool unconstrained = !(p.ngram > 0 || p.penalise);
+    if (use_buf && tid == 0 && t + 1 < p.T) {
+        // The next step's records do not depend on this step: bring them into L2 now.
+        const int64_t row1 = (static_cast<int64_t>(b) * p.T + t + 1) * K;
+        prefetch_l2_bulk(p.rkeys + row1 * LIST, static_cast<uint32_t>(K) * static_cast<uint32_t>(LIST) * 8u);
+        const uintptr_t i0 = reinterpret_cast<uintptr_t>(p.rinfo + row1) & ~static_cast<uintptr_t>(15);
+        const uintptr_t i1 = (reinterpret_cast<uintptr_t>(p.rinfo + row1 + K) + 15) & ~static_cast<uintptr_t>(15);
+        prefetch_l2_bulk(reinterpret_cast<const void*>(i0), static_cast<uint32_t>(i1 - i0));
+        const uintptr_t l0 = reinterpret_cast<uintptr_t>(p.rlse + row1) & ~static_cast<uintptr_t>(15);
+        const uintptr_t l1 = (reinterpret_cast<uintptr_t>(p.rlse + row1 + K) + 15) & ~static_cast<uintptr_t>(15);
+        prefetch_l2_bulk(reinterpret_cast<const void*>(l0), static_cast<uint32_t>(l1 - l0));
+    }
     for (int i = tid; i < DBS_CUDA_MAX_BEAM / 32; i += kThreads) ws.fb[i] = 0;
-    if (tid == 0) sh.sel.invalid = 0;
+    if (sample)
+        for (int i = tid; i < 2 * K; i += kThreads) sh.wkeys[i] = 0;
+    if (tid == 0) {
+        sh.sel.invalid = 0;
+        ws.n_cand = 0;
+        ws.thr = 0;
+    }
     block_sync();
-    for (int k = warp; k < K; k += kWarps) {
-        const int64_t s = static_cast<int64_t>(b) * K + k;
-        const int64_t rowi = (static_cast<int64_t>(b) * p.T + t) * K + k;
-        uint64_t* list = p.keys + s * LIST;
-        bool read = false;
-        float pr = 0.0f;
-        int plen = 0;
-        if (active && k < m.beam && (t > 0 || k == 0)) {
-            pr = ld_cg(p.raw + s);
-            plen = ld_cg(p.len + s);
+    auto append = [&](uint64_t key) {
+        const unsigned mask = __ballot_sync(0xffffffffu, key != 0);
+        if (!mask) return;
+        int base = 0;
+        if (lane == 0) base = atomicAdd(&ws.n_cand, __popc(mask));
+        base = __shfl_sync(0xffffffffu, base, 0);
+        if (key != 0) cbuf[base + __popc(mask & ((1u << lane) - 1u))] = key;
+    };
+    if (sample && unconstrained) gather_sampled<LOGITS>(p, sh, ws, t, b, m, cbuf);
+    // Warp w takes rows w, w + kWarps, ...; their scalars are loaded 32 rows at a time (lane
+    // j: the warp's row j of the batch) before the rows are processed one by one.
+    for (int j0 = 0; !(sample && unconstrained) && warp + kWarps * j0 < K; j0 += 32) {
+        const int kl = warp + kWarps * (j0 + lane);
+        float pr_l = 0.0f, lse_l = 0.0f;
+        int plen_l = 0;
+        uint32_t info_l = 0;
+        bool read_l = false;
+        if (kl < K) {
+            const int64_t s = static_cast<int64_t>(b) * K + kl;
+            const int64_t rowi = (static_cast<int64_t>(b) * p.T + t) * K + kl;
+            const float r = ld_cg(p.raw + s);
+            plen_l = ld_cg(p.len + s);
             const uint8_t ended = ld_cg(p.ended + s);
-            read = f_finite(pr) && !(m.eos >= 0 && ended != 0);
+            info_l = ld_cg(p.rinfo + rowi);
+            lse_l = ld_cg(p.rlse + rowi);
+            pr_l = r;
+            read_l = active && kl < m.beam && (t > 0 || kl == 0) && f_finite(r) && !(m.eos >= 0 && ended != 0);
         }
-        float lse = 0.0f;
-        if (read) {
-            const uint32_t info = ld_cg(p.rinfo + rowi);
-            lse = ld_cg(p.rlse + rowi);
-            const int cnt = static_cast<int>(info >> 8);
-            const bool partial = cnt >= LIST || (info & 2u) != 0;
-            const uint64_t* rec = p.rkeys + rowi * LIST;
-            const ConsView cv = chain_prefix(p, t, s);
-            float raw_last = f_ninf();
-            if (partial && cnt > 0) {
-                const float x = key_raw(ld_cg(rec + cnt - 1));
-                const float lp = LOGITS ? __fsub_rn(x, lse) : x;
-                if (lp < f_inf() && lp != f_ninf()) raw_last = __fadd_rn(pr, lp);
+        const unsigned reads = __ballot_sync(0xffffffffu, read_l);
+        // Buffered mode: the next row's record entries are loaded while this row's are used.
+        auto load_rec = [&](int j, uint64_t (&xk)[kRegKeys]) {
+            const int k = warp + kWarps * (j0 + j);
+            const bool rd = ((reads >> j) & 1u) && k < K;
+            const int cnt = static_cast<int>(__shfl_sync(0xffffffffu, info_l, j) >> 8);
+            const uint64_t* rec = p.rkeys + ((static_cast<int64_t>(b) * p.T + t) * K + k) * LIST;
+#pragma unroll
+            for (int u = 0; u < kRegKeys; ++u) {
+                const int i = lane + 32 * u;
+                xk[u] = (rd && i < cnt) ? ld_cg(rec + i) : 0;
             }
-            // Exactness of the record (as in the narrow case): R entries whose constrained raw
-            // is strictly above the last entry's unconstrained raw. The record's EOS masking
-            // assumed parent length t.
-            int above = 0;
-            for (int i = lane; i < LIST; i += 32) {
-                uint64_t key = 0;
-                if (i < cnt) {
-                    const uint64_t xk = ld_cg(rec + i);
-                    const float raw = constrained_raw<LOGITS>(p, cv, pr, key_raw(xk), lse, static_cast<int>(key_index(xk)));
-                    if (raw != f_ninf()) key = make_key(raw, static_cast<uint32_t>(k) * V + key_index(xk));
-                    above += raw > raw_last ? 1 : 0;
+        };
+        int nj = 0;  // rows of this warp in the batch
+        while (nj < 32 && warp + kWarps * (j0 + nj) < K) ++nj;
+        // Row j of the batch from `use`, with row j + 1's entries loaded into `load` (the two
+        // register arrays swap roles from row to row, so no load is waited for early).
+        auto row_step = [&](int j, const uint64_t (&use)[kRegKeys], uint64_t (&load)[kRegKeys]) {
+            if (use_buf && j + 1 < nj) load_rec(j + 1, load);
+            const int k = warp + kWarps * (j0 + j);
+            const int64_t s = static_cast<int64_t>(b) * K + k;
+            const int64_t rowi = (static_cast<int64_t>(b) * p.T + t) * K + k;
+            const bool read = (reads >> j) & 1u;
+            const float pr = __shfl_sync(0xffffffffu, pr_l, j);
+            const int plen = __shfl_sync(0xffffffffu, plen_l, j);
+            const uint32_t info = __shfl_sync(0xffffffffu, info_l, j);
+            const float lse = __shfl_sync(0xffffffffu, lse_l, j);
+            uint64_t* list = p.keys + s * LIST;
+            if (read) {
+                const int cnt = static_cast<int>(info >> 8);
+                const bool partial = cnt >= LIST || (info & 2u) != 0;
+                const uint64_t* rec = p.rkeys + rowi * LIST;
+                const ConsView cv = chain_prefix(p, t, s);
+                // Exactness of the record (as in the narrow case): R entries whose constrained
+                // raw is strictly above the last entry's unconstrained raw. The record's EOS
+                // masking assumed parent length t.
+                auto entry_raw = [&](uint64_t xk, float& plain) {
+                    const float x = key_raw(xk);
+                    const float lp = LOGITS ? __fsub_rn(x, lse) : x;
+                    plain = (lp < f_inf() && lp != f_ninf()) ? __fadd_rn(pr, lp) : f_ninf();
+                    return cv.prefix ? constrained_raw<LOGITS>(p, cv, pr, x, lse, static_cast<int>(key_index(xk))) : plain;
+                };
+                if (use_buf) {
+                    const uint64_t (&xk)[kRegKeys] = use;
+                    uint64_t key[kRegKeys];
+                    float raw[kRegKeys];
+                    uint64_t last_x = 0;
+#pragma unroll
+                    for (int u = 0; u < kRegKeys; ++u) {
+                        float plain;
+                        raw[u] = xk[u] != 0 ? entry_raw(xk[u], plain) : f_ninf();
+                        key[u] = raw[u] != f_ninf() ? make_key(raw[u], static_cast<uint32_t>(k) * V + key_index(xk[u])) : 0;
+                        if (cnt > 0 && u == ((cnt - 1) >> 5)) last_x = xk[u];
+                    }
+                    float raw_last = f_ninf();
+                    if (partial && cnt > 0) {
+                        const uint64_t lx = __shfl_sync(0xffffffffu, last_x, (cnt - 1) & 31);
+                        entry_raw(lx, raw_last);
+                    }
+                    int above = 0;
+#pragma unroll
+                    for (int u = 0; u < kRegKeys; ++u) above += raw[u] > raw_last ? 1 : 0;
+                    above = warp_sum_i32(above);
+                    const bool exact = plen == t && (!partial || above >= R);
+                    if (exact) {
+                        // All of the row's keys with one shared-memory atomic.
+                        unsigned masks[kRegKeys];
+                        int tot = 0;
+#pragma unroll
+                        for (int u = 0; u < kRegKeys; ++u) {
+                            masks[u] = __ballot_sync(0xffffffffu, 32 * u < cnt && key[u] != 0);
+                            tot += __popc(masks[u]);
+                        }
+                        int base = 0;
+                        if (lane == 0 && tot) base = atomicAdd(&ws.n_cand, tot);
+                        base = __shfl_sync(0xffffffffu, base, 0);
+                        const unsigned lt = (1u << lane) - 1u;
+#pragma unroll
+                        for (int u = 0; u < kRegKeys; ++u) {
+                            if ((masks[u] >> lane) & 1u) cbuf[base + __popc(masks[u] & lt)] = key[u];
+                            base += __popc(masks[u]);
+                        }
+                        // The row's first two entries sample the step's candidates.
+                        if (sample && lane < 2) sh.wkeys[2 * k + lane] = key[0];
+                    }
+                    if (lane == 0) {
+                        if (!exact) atomicOr(&ws.fb[k >> 5], 1u << (k & 31));
+                        if (info & 1u) sh.sel.invalid = 1;
+                    }
+                } else {
+                    float raw_last = f_ninf();
+                    if (partial && cnt > 0) entry_raw(ld_cg(rec + cnt - 1), raw_last);
+                    int above = 0;
+                    for (int i = lane; i < LIST; i += 32) {
+                        uint64_t key = 0;
+                        if (i < cnt) {
+                            const uint64_t xk = ld_cg(rec + i);
+                            float plain;
+                            const float raw = entry_raw(xk, plain);
+                            if (raw != f_ninf()) key = make_key(raw, static_cast<uint32_t>(k) * V + key_index(xk));
+                            above += raw > raw_last ? 1 : 0;
+                        }
+                        list[i] = key;
+                    }
+                    above = warp_sum_i32(above);
+                    const bool exact = plen == t && (!partial || above >= R);
+                    if (lane == 0) {
+                        if (!exact) atomicOr(&ws.fb[k >> 5], 1u << (k & 31));
+                        if (info & 1u) sh.sel.invalid = 1;
+                    }
                 }
-                list[i] = key;
+            } else if (!use_buf) {
+                for (int i = lane; i < LIST; i += 32) list[i] = 0;
             }
-            above = warp_sum_i32(above);
-            const bool exact = plen == t && (!partial || above >= R);
-            if (lane == 0) {
-                if (!exact) atomicOr(&ws.fb[k >> 5], 1u << (k & 31));
-                if (info & 1u) sh.sel.invalid = 1;
-            }
-        } else {
-            for (int i = lane; i < LIST; i += 32) list[i] = 0;
+            if (lane == 0 && p.row_lse) p.row_lse[rowi] = (read && LOGITS) ? lse : 0.0f;
+        };
+        uint64_t cur[kRegKeys], nxt[kRegKeys];
+        if (use_buf) load_rec(0, cur);
+        for (int j = 0; j < nj; j += 2) {
+            row_step(j, cur, nxt);
+            if (j + 1 < nj) row_step(j + 1, nxt, cur);
         }
-        if (lane == 0 && p.row_lse) p.row_lse[rowi] = (read && LOGITS) ? lse : 0.0f;
     }
     block_sync();
     bool any_fb = false;
     for (int w = 0; w < (K + 31) / 32; ++w) any_fb |= ws.fb[w] != 0;
-    if (any_fb && !fallback()) {
-        block_sync();
-        return false;
+    if (any_fb) {
+        if (!fallback()) {
+            block_sync();
+            return false;
+        }
+        if (use_buf) {
+            // The rescanned rows' lists join the buffer.
+            for (int w = 0; w < (K + 31) / 32; ++w) {
+                unsigned bits = ws.fb[w];
+                while (bits) {
+                    const int k = w * 32 + __ffs(bits) - 1;
+                    bits &= bits - 1;
+                    if (warp == 0) {
+                        const uint64_t* list = p.keys + (static_cast<int64_t>(b) * K + k) * LIST;
+                        for (int i0 = 0; i0 < LIST; i0 += 32) append(i0 + lane < LIST ? ld_cg(list + i0 + lane) : 0);
+                    }
+                }
+            }
+            block_sync();
+        }
     }
     if (tid == 0 && sh.sel.invalid && p.out.invalid_input) p.out.invalid_input[b] = 1;
+    int n_cand = ws.n_cand;
+    if (sample && !unconstrained) {
+        for (int i = tid; i < 2 * K; i += kThreads) {
+            const uint64_t v = sh.wkeys[i];
+            if (v == 0) continue;
+            int rank = 0;
+#pragma unroll 8
+            for (int j = 0; j < 2 * K; ++j) rank += sh.wkeys[j] > v ? 1 : 0;
+            if (rank == R - 1) ws.thr = v;  // keys are unique: one sample has rank R - 1
+        }
+        block_sync();
+        const uint64_t thr = ws.thr;
+        if (thr != 0) {
+            // In-place compaction of the keys >= thr, 8 per thread per round: a round's keys
+            // are all read before any is written, and writes never pass the round's end.
+            if (tid == 0) ws.n_cand = 0;
+            block_sync();
+            for (int r0 = 0; r0 < n_cand; r0 += 8 * kThreads) {
+                uint64_t v[8];
+#pragma unroll
+                for (int u = 0; u < 8; ++u) {
+                    const int i = r0 + u * kThreads + tid;
+                    v[u] = i < n_cand ? cbuf[i] : 0;
+                }
+                block_sync();
+                unsigned masks[8];
+                int tot = 0;
+#pragma unroll
+                for (int u = 0; u < 8; ++u) {
+                    masks[u] = __ballot_sync(0xffffffffu, v[u] != 0 && v[u] >= thr);
+                    tot += __popc(masks[u]);
+                }
+                int base = 0;
+                if (lane == 0 && tot) base = atomicAdd(&ws.n_cand, tot);
+                base = __shfl_sync(0xffffffffu, base, 0);
+                const unsigned lt = (1u << lane) - 1u;
+#pragma unroll
+                for (int u = 0; u < 8; ++u) {
+                    if ((masks[u] >> lane) & 1u) cbuf[base + __popc(masks[u] & lt)] = v[u];
+                    base += __popc(masks[u]);
+                }
+                block_sync();
+            }
+            n_cand = ws.n_cand;
+        }
+    }
     __threadfence_block();
     block_sync();
-    select_step<0, KCAP>(p, sh, ss, t, b, m);
+    if (use_buf) select_step<0, KCAP>(p, sh, ss, t, b, m, cbuf, n_cand);
+    else select_step<0, KCAP>(p, sh, ss, t, b, m);
     __threadfence();
     block_sync();
     return true;
@@ -2564,7 +2950,7 @@ __device__ void chain_select_wide(const DecodeParams& p, RowShared& sh, WideShar
             }
         }
         return true;
-    });
+    }, ws.cand, kWideCand);
 }
 
 template <int DT, bool LOGITS, int KCAP>

@@ -108,6 +108,7 @@ struct VShardParams {
     int n_rescan;
     uint64_t* rescan;            // [n_rescan, K]
     const uint64_t* rescan_all;  // [world, n_rescan, K]
+    int cand_cap;                // select: candidate keys its shared-memory buffer holds (0: none)
 };
 
 // Everything the backward kernels need.

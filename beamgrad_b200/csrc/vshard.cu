@@ -59,6 +59,61 @@ __device__ __forceinline__ bool vs_row_read(const Meta& m, int t, int k) {
     return t < m.steps && k < m.beam && (t > 0 || k == 0);
 }
 
+// Pass 1 over a row in global memory with eight 16-byte loads in flight per thread:
+// NaN-propagating maximum and minimum of the entries the thread owns (chunk c on thread
+// c mod kThreads, ragged ends on threads 0 .. n_ends - 1).
+template <int DT>
+__device__ __forceinline__ void pass1_deep(const char* row, const RowSplit& rs, int tid, float& mxn, float& mn) {
+    using E = Elem<DT>;
+    constexpr int UR = 8;
+    const char* body = row + static_cast<size_t>(rs.head) * E::kBytes;
+    mxn = f_ninf();
+    mn = f_inf();
+    if constexpr (E::kBytes == 2) {
+        uint32_t mx2 = h2_ninf<DT>(), mn2 = h2_inf<DT>();
+        for (int c0 = tid; c0 < rs.nvec; c0 += UR * kThreads) {
+            uint4 q[UR];
+#pragma unroll
+            for (int u = 0; u < UR; ++u) {
+                const int c = c0 + u * kThreads;
+                if (c < rs.nvec) q[u] = ld_stream_v4(body + static_cast<size_t>(c) * 16);
+            }
+#pragma unroll
+            for (int u = 0; u < UR; ++u) {
+                if (c0 + u * kThreads < rs.nvec) {
+                    mx2 = h2_max_nan<DT>(mx2, h2_max_nan<DT>(h2_max_nan<DT>(q[u].x, q[u].y), h2_max_nan<DT>(q[u].z, q[u].w)));
+                    mn2 = h2_min<DT>(mn2, h2_min<DT>(h2_min<DT>(q[u].x, q[u].y), h2_min<DT>(q[u].z, q[u].w)));
+                }
+            }
+        }
+        mxn = max_nan(h2_lo<DT>(mx2), h2_hi<DT>(mx2));
+        mn = fminf(h2_lo<DT>(mn2), h2_hi<DT>(mn2));
+    } else {
+        for (int c0 = tid; c0 < rs.nvec; c0 += UR * kThreads) {
+            uint4 q[UR];
+#pragma unroll
+            for (int u = 0; u < UR; ++u) {
+                const int c = c0 + u * kThreads;
+                if (c < rs.nvec) q[u] = ld_stream_v4(body + static_cast<size_t>(c) * 16);
+            }
+#pragma unroll
+            for (int u = 0; u < UR; ++u) {
+                if (c0 + u * kThreads < rs.nvec) {
+                    const float a = __uint_as_float(q[u].x), b = __uint_as_float(q[u].y);
+                    const float c = __uint_as_float(q[u].z), d = __uint_as_float(q[u].w);
+                    mxn = max_nan(mxn, max_nan(max_nan(a, b), max_nan(c, d)));
+                    mn = fminf(mn, fminf(fminf(a, b), fminf(c, d)));
+                }
+            }
+        }
+    }
+    if (tid < rs.n_ends()) {
+        const float x = load_elem<DT>(row, rs.end_entry(tid));
+        mxn = max_nan(mxn, x);
+        mn = fminf(mn, x);
+    }
+}
+
 // ---------------------------------------------------------------------------
 // scan: one CTA per row (grid-stride).
 // ---------------------------------------------------------------------------
@@ -98,7 +153,7 @@ __global__ void __launch_bounds__(kThreads, 2) vs_scan_kernel(const __grid_const
         // Maximum (NaN-propagating: one test flags NaN/+inf), minimum, and the per-thread
         // maxima behind the filter bound, as in the single-GPU record scan.
         float mxn, mn;
-        group_pass1<DT, kThreads>(row, rs, tid, mxn, mn);
+        pass1_deep<DT>(row, rs, tid, mxn, mn);
         const bool bad = !(mxn < f_inf());
         if (want_bound) {
             float me = bad ? f_ninf() : mxn;
@@ -212,8 +267,8 @@ __global__ void __launch_bounds__(kThreads) vs_lanes_kernel(const __grid_constan
                 const bool fast = __fsub_rn(q.row_min[rowi], mx) >= cephes::kMin;  // every x - max >= -87
                 const bool paired = (reinterpret_cast<uintptr_t>(row) & (2 * EB - 1)) == 0;
                 if (paired) {
-                    const uint64_t acc = fast ? lane_pair_sums<DT, false>(pk, row, nfull, mx, j, L)
-                                              : lane_pair_sums<DT, true>(pk, row, nfull, mx, j, L);
+                    const uint64_t acc = fast ? lane_pair_sums<DT, false, 8>(pk, row, nfull, mx, j, L)
+                                              : lane_pair_sums<DT, true, 8>(pk, row, nfull, mx, j, L);
                     f2_unpack(acc, acc_a, acc_c);
                 } else {
                     for (int i = 0; i < nfull; ++i) {
@@ -241,88 +296,119 @@ __global__ void __launch_bounds__(kThreads) vs_lanes_kernel(const __grid_constan
 }
 
 // ---------------------------------------------------------------------------
-// merge: one warp per row.
+// merge: one warp per four rows. The logsumexp of each row takes the whole warp; the
+// records are merged by a tournament in eight-lane groups (group g: row g, lane r of
+// the group: the head of shard r's record).
 // ---------------------------------------------------------------------------
+constexpr int kMergeRows = 4;
+
+__device__ __forceinline__ uint64_t group8_max_u64(uint64_t v) {
+#pragma unroll
+    for (int o = 4; o >= 1; o >>= 1) {
+        const uint64_t w = __shfl_xor_sync(0xffffffffu, v, o);
+        v = w > v ? w : v;
+    }
+    return v;
+}
+
 template <bool LOGITS>
 __global__ void __launch_bounds__(kThreads) vs_merge_kernel(const __grid_constant__ VShardParams q) {
     const DecodeParams& p = q.d;
     const int lane = threadIdx.x & 31;
     const int W = q.world, LIST = p.list_len;
     const int64_t rows = static_cast<int64_t>(p.B) * p.T * p.K;
-    for (int64_t rowi = static_cast<int64_t>(blockIdx.x) * kWarps + (threadIdx.x >> 5); rowi < rows;
-         rowi += static_cast<int64_t>(gridDim.x) * kWarps) {
-        int b, t, k;
-        vs_row_coords(p, rowi, b, t, k);
-        const Meta m = load_meta(p, b);
-        if (!vs_row_read(m, t, k)) continue;
-        auto part = [&](int r) { return q.pack_all + (static_cast<int64_t>(r) * rows + rowi) * q.row_words; };
-        float lse = 0.0f;
+    const int g = lane >> 3, li = lane & 7;
+    const unsigned gmask = 0xffu << (8 * g);
+    const int64_t step = static_cast<int64_t>(gridDim.x) * kWarps * kMergeRows;
+    for (int64_t row0 = (static_cast<int64_t>(blockIdx.x) * kWarps + (threadIdx.x >> 5)) * kMergeRows; row0 < rows;
+         row0 += step) {
+        auto part = [&](int r, int64_t rowi) {
+            return q.pack_all + (static_cast<int64_t>(r) * rows + rowi) * q.row_words;
+        };
+        auto row_read = [&](int64_t rowi) {
+            if (rowi >= rows) return false;
+            int b, t, k;
+            vs_row_coords(p, rowi, b, t, k);
+            return vs_row_read(load_meta(p, b), t, k);
+        };
         if constexpr (LOGITS) {
-            const float mx = q.row_max[rowi];
-            lse = f_ninf();
-            if (mx != f_ninf()) {
-                // Lane i = lane + 32u; the tree lanes[i] += lanes[i + s], s = 128 ... 1
-                // (src/kernels.hpp:197-202), the first three levels in registers.
-                float v[8];
+#pragma unroll 1
+            for (int j = 0; j < kMergeRows; ++j) {
+                const int64_t rowi = row0 + j;
+                if (!row_read(rowi)) continue;
+                const float mx = q.row_max[rowi];
+                float lse = f_ninf();
+                if (mx != f_ninf()) {
+                    // Lane i = lane + 32u; the tree lanes[i] += lanes[i + s], s = 128 ... 1
+                    // (src/kernels.hpp:197-202), the first three levels in registers.
+                    float v[8];
 #pragma unroll
-                for (int u = 0; u < 8; ++u) {
-                    const int jg = lane + 32 * u;
-                    const int r = jg >> q.lanes_log2;
-                    v[u] = reinterpret_cast<const float*>(part(r) + 1)[jg - (r << q.lanes_log2)];
-                }
-#pragma unroll
-                for (int u = 0; u < 4; ++u) v[u] = __fadd_rn(v[u], v[u + 4]);
-#pragma unroll
-                for (int u = 0; u < 2; ++u) v[u] = __fadd_rn(v[u], v[u + 2]);
-                float x = __fadd_rn(v[0], v[1]);
-#pragma unroll
-                for (int st = 16; st >= 1; st >>= 1) {
-                    const float y = __shfl_down_sync(0xffffffffu, x, st);
-                    if (lane < st) x = __fadd_rn(x, y);
-                }
-                lse = logsumexp_from(mx, __shfl_sync(0xffffffffu, x, 0));
-            }
-        }
-        // The shards' records: counts, NaN/+inf flags, and the bound (largest last entry
-        // of a full record; 0 when none is full).
-        const uint32_t info = lane < W ? static_cast<uint32_t>(part(lane)[0]) : 0u;
-        const int cnt_l = static_cast<int>(info >> 8);
-        const bool full_l = (info & 2u) != 0;
-        const uint64_t last_l = (full_l && cnt_l > 0) ? part(lane)[q.key_off + cnt_l - 1] : 0;
-        const uint64_t bound = warp_max_u64(last_l);
-        const bool invalid = __any_sync(0xffffffffu, (info & 1u) != 0);
-        const bool any_full = __any_sync(0xffffffffu, full_l);
-        int cnts[DBS_CUDA_VSHARD_MAX_WORLD];
-#pragma unroll
-        for (int r = 0; r < DBS_CUDA_VSHARD_MAX_WORLD; ++r) cnts[r] = __shfl_sync(0xffffffffu, cnt_l, r);
-        uint64_t* rec = p.rkeys + rowi * LIST;
-        int n = 0;
-        for (int r = 0; r < W; ++r) {
-            const uint64_t* lr = part(r) + q.key_off;
-            for (int i = lane; i < cnts[r]; i += 32) {
-                const uint64_t key = lr[i];
-                if (key < bound) break;
-                ++n;
-                int rank = i;
-                for (int r2 = 0; r2 < W; ++r2) {
-                    if (r2 == r) continue;
-                    const uint64_t* l2 = part(r2) + q.key_off;
-                    int lo = 0, hi = cnts[r2];  // entries of r2 above key form a prefix
-                    while (lo < hi) {
-                        const int mid = (lo + hi) >> 1;
-                        if (l2[mid] > key) lo = mid + 1;
-                        else hi = mid;
+                    for (int u = 0; u < 8; ++u) {
+                        const int jg = lane + 32 * u;
+                        const int r = jg >> q.lanes_log2;
+                        v[u] = reinterpret_cast<const float*>(part(r, rowi) + 1)[jg - (r << q.lanes_log2)];
                     }
-                    rank += lo;
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) v[u] = __fadd_rn(v[u], v[u + 4]);
+#pragma unroll
+                    for (int u = 0; u < 2; ++u) v[u] = __fadd_rn(v[u], v[u + 2]);
+                    float x = __fadd_rn(v[0], v[1]);
+#pragma unroll
+                    for (int st = 16; st >= 1; st >>= 1) {
+                        const float y = __shfl_down_sync(0xffffffffu, x, st);
+                        if (lane < st) x = __fadd_rn(x, y);
+                    }
+                    lse = logsumexp_from(mx, __shfl_sync(0xffffffffu, x, 0));
                 }
-                if (rank < LIST) rec[rank] = key;
+                if (lane == 0) p.rlse[rowi] = lse;
             }
         }
-        n = warp_sum_i32(n);
-        if (lane == 0) {
-            const int cnt = n < LIST ? n : LIST;
-            p.rlse[rowi] = lse;
-            p.rinfo[rowi] = (invalid ? 1u : 0u) | (any_full ? 2u : 0u) | (static_cast<uint32_t>(cnt) << 8);
+        const int64_t rowi = row0 + g;
+        const bool read = row_read(rowi);
+        // Shard li's record of row g: count, NaN/+inf flag, full (entries may be missing).
+        const uint64_t* mine = nullptr;
+        uint32_t info = 0;
+        if (read && li < W) {
+            mine = part(li, rowi);
+            info = static_cast<uint32_t>(mine[0]);
+            mine += q.key_off;
+        }
+        const int cnt = static_cast<int>(info >> 8);
+        const bool full = (info & 2u) != 0;
+        // Every entry at or above the largest last entry of a full record is in the union.
+        const uint64_t bound = group8_max_u64((full && cnt > 0) ? mine[cnt - 1] : 0);
+        const unsigned flags = __ballot_sync(0xffffffffu, (info & 1u) != 0) & gmask;
+        const unsigned fulls = __ballot_sync(0xffffffffu, full) & gmask;
+        uint64_t head = cnt > 0 ? mine[0] : 0;
+        uint64_t next = cnt > 1 ? mine[1] : 0;
+        if (head < bound) head = 0;
+        int pos = 0;
+        uint64_t* rec = read ? p.rkeys + rowi * LIST : nullptr;
+        uint64_t held = 0;  // entry n of the record with n mod 8 == li, stored eight at a time
+        int n = 0;
+        for (; n < LIST; ++n) {
+            const uint64_t best = group8_max_u64(head);
+            if (!__any_sync(0xffffffffu, best != 0)) break;
+            if (best != 0) {
+                if ((n & 7) == li) held = best;
+                if ((n & 7) == 7) rec[n - 7 + li] = held;
+                if (head == best) {
+                    ++pos;
+                    head = next < bound ? 0 : next;
+                    next = pos + 1 < cnt ? mine[pos + 1] : 0;
+                }
+            }
+        }
+        // The group's count: every entry it emitted advanced one of its lanes.
+        int taken = pos;
+#pragma unroll
+        for (int o = 4; o >= 1; o >>= 1) taken += __shfl_xor_sync(0xffffffffu, taken, o);
+        if (read) {
+            const int c = taken < LIST ? taken : LIST;
+            if (li < (c & 7)) rec[(c & ~7) + li] = held;
+            if (li == 0) {
+                p.rinfo[rowi] = (flags ? 1u : 0u) | (fulls ? 2u : 0u) | (static_cast<uint32_t>(c) << 8);
+            }
         }
     }
 }
@@ -337,6 +423,7 @@ __global__ void __launch_bounds__(kThreads, 1) vs_select_kernel(const __grid_con
     auto& ss = *reinterpret_cast<SelectShared<KCAP>*>(dyn);
     constexpr size_t kSelBytes = (sizeof(SelectShared<KCAP>) + 127) & ~static_cast<size_t>(127);
     auto& ws = *reinterpret_cast<WideShared*>(dyn + kSelBytes);
+    uint64_t* cbuf = reinterpret_cast<uint64_t*>(dyn + wide_dyn_smem<KCAP>());
     const DecodeParams& p = q.d;
     const int b = blockIdx.x;
     const int T = p.T, K = p.K, LIST = p.list_len;
@@ -373,7 +460,7 @@ __global__ void __launch_bounds__(kThreads, 1) vs_select_kernel(const __grid_con
                 }
             }
             return true;
-        });
+        }, q.cand_cap > 0 ? cbuf : nullptr, q.cand_cap);
         if (!ok) {
             if (threadIdx.x == 0) q.resume[b] = t;
             return;
@@ -460,9 +547,15 @@ cudaError_t rescan_as(const VShardParams& q, cudaStream_t stream, int sm_count) 
     return cudaGetLastError();
 }
 
+// Candidate keys of one step held in the select kernel's shared memory (128 KB).
+constexpr int kSelectCandCap = 16384;
+
 template <bool LOGITS, int KCAP>
-cudaError_t select_as(const VShardParams& q, cudaStream_t stream) {
-    const size_t dyn = wide_dyn_smem<KCAP>();
+cudaError_t select_as(const VShardParams& q0, cudaStream_t stream) {
+    VShardParams q = q0;
+    const int64_t all = static_cast<int64_t>(q.d.K) * q.d.list_len;
+    q.cand_cap = all <= kSelectCandCap ? static_cast<int>(all) : 0;
+    const size_t dyn = wide_dyn_smem<KCAP>() + static_cast<size_t>(q.cand_cap) * sizeof(uint64_t);
     auto kernel = vs_select_kernel<LOGITS, KCAP>;
     cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(dyn));
     if (e != cudaSuccess) return e;
