@@ -59,16 +59,60 @@ __device__ __forceinline__ bool vs_row_read(const Meta& m, int t, int k) {
     return t < m.steps && k < m.beam && (t > 0 || k == 0);
 }
 
-// Pass 1 over a row in global memory with eight 16-byte loads in flight per thread:
-// NaN-propagating maximum and minimum of the entries the thread owns (chunk c on thread
-// c mod kThreads, ragged ends on threads 0 .. n_ends - 1).
+// A thread's four largest entries (values, shard indices), v[0] >= ... >= v[3].
+__device__ __forceinline__ void top4_insert(float (&v)[4], int (&ix)[4], float x, int i) {
+    if (!(x > v[3])) return;
+    if (x > v[1]) {
+        v[3] = v[2];
+        ix[3] = ix[2];
+        v[2] = v[1];
+        ix[2] = ix[1];
+        if (x > v[0]) {
+            v[1] = v[0];
+            ix[1] = ix[0];
+            v[0] = x;
+            ix[0] = i;
+        } else {
+            v[1] = x;
+            ix[1] = i;
+        }
+    } else if (x > v[2]) {
+        v[3] = v[2];
+        ix[3] = ix[2];
+        v[2] = x;
+        ix[2] = i;
+    } else {
+        v[3] = x;
+        ix[3] = i;
+    }
+}
+
+// Pass 1 over a row in global memory, eight 16-byte loads in flight per thread: the
+// NaN-propagating maximum and the minimum of the entries the thread owns (chunk c on
+// thread c mod kThreads, ragged ends on threads 0 .. n_ends - 1), and its four largest
+// entries (NaN never enters; +inf may, and then the row takes the slow path), leaving out
+// entry `skip` (a masked EOS token; -1: none).
 template <int DT>
-__device__ __forceinline__ void pass1_deep(const char* row, const RowSplit& rs, int tid, float& mxn, float& mn) {
+__device__ __forceinline__ void pass1_top4(const char* row, const RowSplit& rs, int tid, int skip, float& mxn,
+                                           float& mn, float (&tv)[4], int (&ti)[4]) {
     using E = Elem<DT>;
     constexpr int UR = 8;
+    constexpr int PER = 16 / E::kBytes;
     const char* body = row + static_cast<size_t>(rs.head) * E::kBytes;
     mxn = f_ninf();
     mn = f_inf();
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+        tv[u] = f_ninf();
+        ti[u] = 0;
+    }
+    auto single = [&](int v) {
+        const float x = load_elem<DT>(row, v);
+        mxn = max_nan(mxn, x);
+        mn = fminf(mn, x);
+        if (v != skip) top4_insert(tv, ti, x, v);
+    };
+    if (tid < rs.head && tid < rs.n_ends()) single(rs.end_entry(tid));  // entries before the body
     if constexpr (E::kBytes == 2) {
         uint32_t mx2 = h2_ninf<DT>(), mn2 = h2_inf<DT>();
         for (int c0 = tid; c0 < rs.nvec; c0 += UR * kThreads) {
@@ -80,14 +124,23 @@ __device__ __forceinline__ void pass1_deep(const char* row, const RowSplit& rs, 
             }
 #pragma unroll
             for (int u = 0; u < UR; ++u) {
-                if (c0 + u * kThreads < rs.nvec) {
+                const int c = c0 + u * kThreads;
+                if (c < rs.nvec) {
                     mx2 = h2_max_nan<DT>(mx2, h2_max_nan<DT>(h2_max_nan<DT>(q[u].x, q[u].y), h2_max_nan<DT>(q[u].z, q[u].w)));
                     mn2 = h2_min<DT>(mn2, h2_min<DT>(h2_min<DT>(q[u].x, q[u].y), h2_min<DT>(q[u].z, q[u].w)));
+                    const uint32_t m2 = h2_max<DT>(h2_max<DT>(q[u].x, q[u].y), h2_max<DT>(q[u].z, q[u].w));
+                    if (fmaxf(h2_lo<DT>(m2), h2_hi<DT>(m2)) > tv[3]) {
+                        float x[PER];
+                        unpack16<DT>(q[u], x);
+#pragma unroll
+                        for (int e = 0; e < PER; ++e)
+                            if (rs.head + c * PER + e != skip) top4_insert(tv, ti, x[e], rs.head + c * PER + e);
+                    }
                 }
             }
         }
-        mxn = max_nan(h2_lo<DT>(mx2), h2_hi<DT>(mx2));
-        mn = fminf(h2_lo<DT>(mn2), h2_hi<DT>(mn2));
+        mxn = max_nan(mxn, max_nan(h2_lo<DT>(mx2), h2_hi<DT>(mx2)));
+        mn = fminf(mn, fminf(h2_lo<DT>(mn2), h2_hi<DT>(mn2)));
     } else {
         for (int c0 = tid; c0 < rs.nvec; c0 += UR * kThreads) {
             uint4 q[UR];
@@ -98,28 +151,39 @@ __device__ __forceinline__ void pass1_deep(const char* row, const RowSplit& rs, 
             }
 #pragma unroll
             for (int u = 0; u < UR; ++u) {
-                if (c0 + u * kThreads < rs.nvec) {
+                const int c = c0 + u * kThreads;
+                if (c < rs.nvec) {
                     const float a = __uint_as_float(q[u].x), b = __uint_as_float(q[u].y);
-                    const float c = __uint_as_float(q[u].z), d = __uint_as_float(q[u].w);
-                    mxn = max_nan(mxn, max_nan(max_nan(a, b), max_nan(c, d)));
-                    mn = fminf(mn, fminf(fminf(a, b), fminf(c, d)));
+                    const float d = __uint_as_float(q[u].z), e = __uint_as_float(q[u].w);
+                    mxn = max_nan(mxn, max_nan(max_nan(a, b), max_nan(d, e)));
+                    mn = fminf(mn, fminf(fminf(a, b), fminf(d, e)));
+                    if (fmaxf(fmaxf(a, b), fmaxf(d, e)) > tv[3]) {
+                        const int base = rs.head + c * 4;
+                        if (base != skip) top4_insert(tv, ti, a, base);
+                        if (base + 1 != skip) top4_insert(tv, ti, b, base + 1);
+                        if (base + 2 != skip) top4_insert(tv, ti, d, base + 2);
+                        if (base + 3 != skip) top4_insert(tv, ti, e, base + 3);
+                    }
                 }
             }
         }
     }
-    if (tid < rs.n_ends()) {
-        const float x = load_elem<DT>(row, rs.end_entry(tid));
-        mxn = max_nan(mxn, x);
-        mn = fminf(mn, x);
-    }
+    if (tid >= rs.head && tid < rs.n_ends()) single(rs.end_entry(tid));  // entries after the body
 }
 
 // ---------------------------------------------------------------------------
-// scan: one CTA per row (grid-stride).
+// scan: one CTA per row (grid-stride). Pass 1 streams the row once and keeps each
+// thread's four largest entries; the bound B = the smallest of the warps' q-th largest
+// thread maxima (8q >= LS) has at least LS eligible entries at or above it, so the
+// record lies among the entries >= B. A thread whose fourth entry is below B holds all
+// of its entries >= B among its four; the others (and a thread owning an EOS token)
+// read their own entries again. Rows with NaN/+inf, banned tokens, or records above
+// 256 entries take a block radix select over the row.
 // ---------------------------------------------------------------------------
 template <int DT>
-__global__ void __launch_bounds__(kThreads, 2) vs_scan_kernel(const __grid_constant__ VShardParams q) {
+__global__ void __launch_bounds__(kThreads, 3) vs_scan_kernel(const __grid_constant__ VShardParams q) {
     using E = Elem<DT>;
+    constexpr int PER = 16 / E::kBytes;
     __shared__ RowShared sh;
     __shared__ WideShared ws;
     const DecodeParams& p = q.d;
@@ -130,6 +194,7 @@ __global__ void __launch_bounds__(kThreads, 2) vs_scan_kernel(const __grid_const
     const int64_t rows = static_cast<int64_t>(p.B) * p.T * p.K;
     const bool exclusions = p.banned != nullptr;
     const bool want_bound = !exclusions && LS <= kWarps * 32;
+    const int qw = (LS + kWarps - 1) / kWarps;  // thread maxima each warp contributes to the bound
     for (int64_t rowi = blockIdx.x; rowi < rows; rowi += gridDim.x) {
         int b, t, k;
         vs_row_coords(p, rowi, b, t, k);
@@ -150,21 +215,40 @@ __global__ void __launch_bounds__(kThreads, 2) vs_scan_kernel(const __grid_const
             const int v = vs_global(q, i);
             return !(exclusions && p.banned[v]) && !(mask_eos && is_eos(p, m, v));
         };
-        // Maximum (NaN-propagating: one test flags NaN/+inf), minimum, and the per-thread
-        // maxima behind the filter bound, as in the single-GPU record scan.
-        float mxn, mn;
-        pass1_deep<DT>(row, rs, tid, mxn, mn);
-        const bool bad = !(mxn < f_inf());
-        if (want_bound) {
-            float me = bad ? f_ninf() : mxn;
-            if (m.eos >= 0) {
-                if (rs.owns(vs_local(q, m.eos))) me = f_ninf();
-                for (int i = 0; i < p.n_extra; ++i)
-                    if (rs.owns(vs_local(q, p.extra[i]))) me = f_ninf();
-            }
-            sh.wtop[warp * 32 + lane] = warp_sort_desc(me);
+        auto push = [&](bool cond, float x, int i) {
+            const unsigned mask = __ballot_sync(0xffffffffu, cond);
+            if (!mask) return;
+            int base = 0;
+            if (lane == 0) base = atomicAdd(&ws.n_cand, __popc(mask));
+            base = __shfl_sync(0xffffffffu, base, 0);
+            const int pos = base + __popc(mask & ((1u << lane) - 1u));
+            if (cond && pos < kWideCand) ws.cand[pos] = make_key(x, static_cast<uint32_t>(vs_global(q, i)));
+        };
+        // EOS tokens of this thread: their entries never count toward the bound; a masked one
+        // is left out of the four, and a thread owning two masked ones reads its entries again.
+        bool dirty = false;
+        int skip = -1, n_masked = 0;
+        if (m.eos >= 0) {
+            auto own = [&](int v) {
+                const int i = vs_local(q, v);
+                if (!rs.owns(i)) return;
+                dirty = true;
+                if (mask_eos && i != skip) {
+                    skip = i;
+                    ++n_masked;
+                }
+            };
+            own(m.eos);
+            for (int i = 0; i < p.n_extra; ++i) own(p.extra[i]);
         }
+        float mxn, mn;
+        float tv[4];
+        int ti[4];
+        pass1_top4<DT>(row, rs, tid, skip, mxn, mn, tv, ti);
+        const bool bad = !(mxn < f_inf());
         {
+            const float srt = warp_sort_desc((bad || dirty) ? f_ninf() : mxn);
+            if (lane == qw - 1) sh.wtop[warp] = srt;
             const float wmx = warp_max_f32(bad ? f_ninf() : mxn);
             const float wmn = -warp_max_f32(-mn);
             const unsigned wbad = __ballot_sync(0xffffffffu, bad);
@@ -179,11 +263,13 @@ __global__ void __launch_bounds__(kThreads, 2) vs_scan_kernel(const __grid_const
         float mx = sh.wred[0];
         mn = sh.wred2[0];
         bool any_bad = sh.ired[0] != 0;
+        float bound = sh.wtop[0];
 #pragma unroll
         for (int w = 1; w < kWarps; ++w) {
             mx = fmaxf(mx, sh.wred[w]);
             mn = fminf(mn, sh.wred2[w]);
             any_bad |= sh.ired[w] != 0;
+            bound = fminf(bound, sh.wtop[w]);
         }
         if (any_bad) {
             // Rare: the maximum over entries below +inf (NaN never raises fmaxf).
@@ -194,31 +280,51 @@ __global__ void __launch_bounds__(kThreads, 2) vs_scan_kernel(const __grid_const
             });
             mx = block_max(sh, mx);
         }
-        const bool make_bound = want_bound && !any_bad;
-        if (make_bound && warp >= kWarps / 2) bound_rank<32>(sh, LS, tid - kThreads / 2);
-        block_sync();
-        const float xthr = make_bound ? sh.xbound : f_ninf();
-        if (xthr != f_ninf()) collect_candidates<DT, kThreads>(ws, row, rs, tid, xthr, eligible);
-        block_sync();
-        const int n = ws.n_cand;
         uint64_t* keys = out + q.key_off;
-        int cnt;
-        if (xthr != f_ninf() && n <= kWideCand) {
-            cnt = sort_candidates(ws, n, LS, keys);
-        } else {
+        int cnt = -1;
+        if (want_bound && !any_bad && bound != f_ninf()) {
+            const bool reread = n_masked > 1 || tv[3] >= bound;
+#pragma unroll
+            for (int u = 0; u < 4; ++u) push(!reread && tv[u] >= bound, tv[u], ti[u]);
+            // Threads that may own more entries >= bound than they kept: their whole share,
+            // read by their warp (lane r takes the thread's chunks r, r + 32, ...).
+            unsigned todo = __ballot_sync(0xffffffffu, reread);
+            while (todo) {
+                const int src = __ffs(todo) - 1;
+                todo &= todo - 1;
+                const int owner = warp * 32 + src;
+                if (owner < rs.n_ends()) {
+                    const int i = rs.end_entry(owner);
+                    const float x = lane == 0 ? load_elem<DT>(row, i) : f_ninf();
+                    push(lane == 0 && x >= bound && x < f_inf() && eligible(i), x, i);
+                }
+                const int nch = owner < rs.nvec ? (rs.nvec - owner + kThreads - 1) / kThreads : 0;
+                for (int r0 = 0; r0 < nch; r0 += 32) {
+                    const int c = owner + (r0 + lane) * kThreads;
+                    const bool have = r0 + lane < nch;
+                    float x[PER];
+                    if (have) unpack16<DT>(ld_stream_v4(row + static_cast<size_t>(rs.head) * E::kBytes +
+                                                        static_cast<size_t>(c) * 16), x);
+#pragma unroll
+                    for (int e = 0; e < PER; ++e) {
+                        const int i = rs.head + c * PER + e;
+                        push(have && x[e] >= bound && x[e] < f_inf() && eligible(i), x[e], i);
+                    }
+                }
+            }
+            block_sync();
+            const int n = ws.n_cand;
+            if (n <= kWideCand) cnt = sort_candidates(ws, n, LS, keys);
+        }
+        if (cnt < 0) {
+            block_sync();
             auto gen = [&](int i) -> uint64_t {
                 const float x = load_elem<DT>(row, i);
-                return (x < f_inf() && x != f_ninf() && eligible(i)) ? make_key(x, static_cast<uint32_t>(i)) : 0;
+                return (x < f_inf() && x != f_ninf() && eligible(i)) ? make_key(x, static_cast<uint32_t>(vs_global(q, i)))
+                                                                    : 0;
             };
             const int got = block_select(sh, gen, Vr, LS, [&](int pos, uint64_t key) { ws.cand[pos] = key; });
             cnt = sort_candidates(ws, got, LS, keys);
-        }
-        // Shard entries to tokens. The map is increasing, so the order of equal x (lower
-        // index first) is kept; each thread rewrites the keys it wrote.
-        for (int i = tid; i < cnt; i += kThreads) {
-            const uint64_t key = keys[i];
-            const uint32_t v = static_cast<uint32_t>(vs_global(q, static_cast<int>(key_index(key))));
-            keys[i] = (key & 0xffffffff00000000ull) | static_cast<uint64_t>(0xffffffffu - v);
         }
         if (tid == 0) {
             // Bit 1: the record is full, so the shard may hold more eligible entries.
