@@ -156,6 +156,7 @@ class ShardDecode:
         }
         self.rescan_rows = self.rescan_slot = self.rescan = self.rescan_all = None
         self.rounds = 0
+        self.timings = None  # {stage: [(start, end) CUDA events]} when set to a dict
         c = A.VocabShardCall()
         c.shard_inputs = _ptr(self.shard)
         c.data_type = _DTYPES[shard.dtype]
@@ -177,8 +178,27 @@ class ShardDecode:
         c.row_lse = _ptr(self.out["row_lse"])
         self.call = c
 
+    def begin(self) -> None:
+        """Starts a decode: no rescanned lists yet (buffers of an earlier decode are reused), then scan."""
+        self.call.buffers.n_rescan = 0
+        self.rounds = 0
+        self.stage("scan")
+
     def stage(self, name: str) -> None:
+        if self.timings is None:
+            self.engine.run(name, self)
+            return
+        s = torch.cuda.current_stream(self.device)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(s)
         self.engine.run(name, self)
+        e1.record(s)
+        self.timings.setdefault(name, []).append((e0, e1))
+
+    def stage_ms(self) -> dict[str, float]:
+        """Device milliseconds per stage summed over the recorded calls (timings enabled)."""
+        torch.cuda.synchronize(self.device)
+        return {k: sum(a.elapsed_time(b) for a, b in v) for k, v in (self.timings or {}).items()}
 
     def stalled_rows(self) -> list[int]:
         """Rows b * K + k the last select stopped at (examples ascending, then k); waits for the GPU."""
@@ -235,21 +255,26 @@ def _agree(n: int, device, group) -> None:
         raise RuntimeError(f"vocab-sharded decode: ranks disagree on the rows to rescan ({lo}..{hi})")
 
 
-def decode_vocab_sharded(shard: torch.Tensor, vocab_size: int, from_logits: bool, steps: torch.Tensor | None = None, *,
-                         group=None, validate: bool = False, engine=None, **settings) -> dict[str, torch.Tensor]:
+def decode_vocab_sharded(shard: torch.Tensor | ShardDecode, vocab_size: int | None = None, from_logits: bool = False,
+                         steps: torch.Tensor | None = None, *, group=None, validate: bool = False, engine=None,
+                         **settings) -> dict[str, torch.Tensor]:
     """The decode of the full vocabulary from this rank's shard; all ranks call it together.
 
-    shard: [B, T, K, shard_vocab_size(vocab_size, W, rank)] (see :func:`shard_inputs`);
+    shard: [B, T, K, shard_vocab_size(vocab_size, W, rank)] (see :func:`shard_inputs`), or a
+    ShardDecode built for this rank (its buffers are reused; the other arguments are ignored);
     settings: eos_token, min_length, length_penalty_alpha, banned_tokens ([V]),
     no_repeat_ngram_size, repetition_penalty, extra_eos, shard_list_len (0: default).
     Returns decode_ex's outputs (and ``invalid``) for the whole batch, on every rank.
     """
     world = dist.get_world_size(group) if dist.is_initialized() else 1
     rank = dist.get_rank(group) if dist.is_initialized() else 0
-    d = ShardDecode(shard, vocab_size, from_logits, world, rank, steps=steps, engine=engine, **settings)
+    if isinstance(shard, ShardDecode):
+        d = shard  # a prepared decode (buffers reused; its inputs may have been refilled)
+    else:
+        d = ShardDecode(shard, vocab_size, from_logits, world, rank, steps=steps, engine=engine, **settings)
     if world == 1:
         return decode_vocab_shards([d], validate=validate)
-    d.stage("scan")
+    d.begin()
     if d.from_logits:
         dist.all_reduce(d.row_max, op=dist.ReduceOp.MAX, group=group)
         d.stage("lanes")
@@ -282,7 +307,7 @@ def decode_vocab_shards(shards: Sequence[torch.Tensor] | Sequence[ShardDecode], 
         ds = [ShardDecode(s, vocab_size, from_logits, world, r, steps=steps, engine=engine, **settings)
               for r, s in enumerate(shards)]
     for d in ds:
-        d.stage("scan")
+        d.begin()
     if ds[0].from_logits:
         m = ds[0].row_max.clone()
         for d in ds[1:]:

@@ -3,7 +3,7 @@
 bf16 logits [B=64, T=128, K=8, V=32000] = N(0, 2) + Zipf(s=1.1) per-token bias, from_logits,
 eos=2, length-penalty alpha=1.0 -- decoded through the engine's C ABI (dbs_cuda_decode_ex2).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload c2|c5]
 
 One JSON line on rank 0. `value` is whole-job candidates/s (B*T*K*V per decode, all ranks)
 with inputs resident in HBM; `e2e` is the same metric through the same C-ABI call with the
@@ -11,6 +11,10 @@ inputs in pinned host memory, copied in and the outputs copied out inside the ti
 Under torchrun each rank decodes its own batch of the config (weak scaling, no collective on
 the data path). `--impl reference` times the reference's own CPU implementation (libdbs,
 oracle/_ref/libdbs.so) with every host thread on the same config.
+
+`--workload c5` benchmarks BASELINE configs C5 instead: fp32 logits [16,32,64,256000] of the
+same recipe, eos=1, alpha=0.6, the vocabulary lane-interleaved over the N ranks
+(beamgrad_b200.vocab_sharding; strong scaling: N GPUs decode the same problem).
 """
 
 from __future__ import annotations
@@ -51,7 +55,10 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--batch", type=int, default=64, help="examples per GPU (C2: 64); smaller only for profiling")
     ap.add_argument("--seq", type=int, default=128, help="decode steps T (C2: 128); smaller only for profiling")
+    ap.add_argument("--workload", default="c2", choices=["c2", "c5"])
     args = ap.parse_args()
+    if args.workload == "c5":
+        return args
     global B, T
     B, T = args.batch, args.seq
     return args
@@ -211,11 +218,229 @@ def run_reference_arm(args, rank: int, world: int):
     }), flush=True)
 
 
+# ---------------------------------------------------------------------------- C5
+C5 = (16, 32, 64, 256000)
+C5_EOS, C5_ALPHA = 1, 0.6
+
+
+def c5_workload() -> str:
+    B5, T5, K5, V5 = C5
+    return (f"C5: fp32 logits [{B5},{T5},{K5},{V5}] N(0,2)+Zipf(1.1) bias, from_logits, eos={C5_EOS}, "
+            f"alpha={C5_ALPHA}, vocabulary lane-interleaved over the ranks")
+
+
+def c5_example(torch, device, b: int):
+    """Example b of the C5 input, full vocabulary [T, K, V] float32 (the same on every rank)."""
+    B5, T5, K5, V5 = C5
+    g = torch.Generator(device=device).manual_seed(5000)
+    bias = -1.1 * torch.log(torch.randperm(V5, generator=g, device=device).float() + 1.0)
+    g.manual_seed(5001 + b)
+    return torch.randn((T5, K5, V5), generator=g, device=device) * 2.0 + bias
+
+
+def c5_shard(torch, world: int, rank: int, device):
+    from beamgrad_b200 import vocab_sharding as vs
+
+    B5, T5, K5, V5 = C5
+    cols = vs.shard_tokens(V5, world, rank, device)
+    x = torch.empty((B5, T5, K5, cols.numel()), dtype=torch.float32, device=device)
+    for b in range(B5):
+        x[b] = c5_example(torch, device, b).index_select(-1, cols)
+    return x
+
+
+def c5_cpu_reference(torch, device, threads: int, n_examples: int = 1):
+    """The reference CPU decoder on the first n_examples of C5 (full vocabulary); candidates/s."""
+    from oracle import oracle
+    from beamgrad_b200 import _abi as A
+
+    B5, T5, K5, V5 = C5
+    x = np.stack([c5_example(torch, device, b).cpu().numpy() for b in range(n_examples)])
+    pb = oracle.Problem(x, dtype=A.DTYPE_F32, from_logits=True, eos=C5_EOS, alpha=C5_ALPHA)
+    times = []
+    with oracle.RefDecoder(pb) as d:
+        for _ in range(3):
+            t0 = time.perf_counter()
+            d.decode(threads=threads)
+            times.append(time.perf_counter() - t0)
+    sec = statistics.median(times)
+    return n_examples * T5 * K5 * V5 / sec, f"{n_examples} example(s) of C5 (full vocabulary), median of 3 runs"
+
+
+def run_c5(args, rank: int, world: int, local: int):
+    import torch
+
+    from oracle import oracle
+
+    B5, T5, K5, V5 = C5
+    cand = B5 * T5 * K5 * V5
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        if not oracle.ref_available():
+            print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/libdbs.so was not built"}))
+            return
+        threads = oracle.cpu_count()
+        dev = "cuda" if torch.cuda.is_available() else "cpu"
+        per = []
+        for i in range(args.warmup + args.steps):
+            value, sample = c5_cpu_reference(torch, dev, threads)
+            if i >= args.warmup:
+                per.append(value)
+        value = statistics.median(per)
+        print(json.dumps({
+            "impl": "reference", "metric": METRIC, "value": value, "unit": "candidates/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": cand / value * 1e3, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": c5_workload(), "global_batch": B5, "seq_len": T5, "beam": K5, "vocab": V5,
+                       "parallelism": "host threads"},
+            "cpu_baseline": {"value": value, "unit": "candidates/s", "cores": threads, "kind": "reference",
+                             "sample": sample},
+            "e2e": {"value": value, "unit": "candidates/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        }), flush=True)
+        return
+
+    from beamgrad_b200 import vocab_sharding as vs
+
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+    dev = torch.device("cuda", local)
+    x = c5_shard(torch, world, rank, dev)
+    d = vs.ShardDecode(x, V5, True, world, rank, eos_token=C5_EOS, length_penalty_alpha=C5_ALPHA)
+    stream = torch.cuda.current_stream(dev)
+
+    def decode():
+        vs.decode_vocab_sharded(d)
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+
+    for _ in range(args.warmup):
+        decode()
+    barrier()
+    try:
+        gpu_id = f"GPU-{torch.cuda.get_device_properties(dev).uuid}"
+    except (AttributeError, RuntimeError):
+        gpu_id = str(local)
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(gpu_id) as clocks:
+        barrier()
+        clocks.start()
+        start.record(stream)
+        for _ in range(args.steps):
+            decode()
+        stop.record(stream)
+        barrier()
+        clocks.stop()
+        if clocks.proc is not None and not clocks.in_window():
+            clocks.extended = True
+            deadline = time.monotonic() + 2.0
+            while not clocks.in_window() and time.monotonic() < deadline:
+                decode()
+                torch.cuda.synchronize(dev)
+                clocks.stop()
+    elapsed = start.elapsed_time(stop) / 1e3
+    t_all = torch.tensor([elapsed], device=dev, dtype=torch.float64)
+    if dist is not None:
+        dist.all_reduce(t_all, op=dist.ReduceOp.MAX)
+    elapsed = float(t_all.item())
+
+    # Stage times of one more (untimed) decode; the scan is the dominant kernel.
+    d.timings = {}
+    decode()
+    stage = d.stage_ms()
+    d.timings = None
+    Vr = d.plan.shard_vocab
+    scan_rows = B5 * (1 + (T5 - 1) * K5)  # rows the search may read: the scan's
+    scan_bytes = scan_rows * Vr * 4 + scan_rows * d.plan.row_words * 8
+    peak, peak_kind = peaks()
+    achieved = scan_bytes / (stage["scan"] / 1e3) / 1e9
+
+    # End to end: this rank's shard from pinned host memory, the decode, the outputs back.
+    e2e = None
+    shard_bytes = x.numel() * x.element_size()
+    if not args.no_e2e and shard_bytes <= (8 << 30):
+        xh = torch.empty(x.shape, dtype=x.dtype, pin_memory=True)
+        xh.copy_(x)
+        outs_h = {k: torch.empty(v.shape, dtype=v.dtype, pin_memory=True) for k, v in d.out.items()}
+        d2h = sum(v.numel() * v.element_size() for v in outs_h.values())
+        n_e2e = max(2, min(args.steps, 3))
+
+        def e2e_step():
+            d.shard.copy_(xh, non_blocking=True)
+            vs.decode_vocab_sharded(d)
+            for k, v in d.out.items():
+                outs_h[k].copy_(v, non_blocking=True)
+
+        e2e_step()
+        barrier()
+        s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s0.record(stream)
+        for _ in range(n_e2e):
+            e2e_step()
+        s1.record(stream)
+        barrier()
+        e2e_t = torch.tensor([s0.elapsed_time(s1) / 1e3 / n_e2e], device=dev, dtype=torch.float64)
+        if dist is not None:
+            dist.all_reduce(e2e_t, op=dist.ReduceOp.MAX)
+        e2e = {"value": cand / float(e2e_t.item()), "unit": "candidates/s", "h2d_bytes_per_step": shard_bytes,
+               "d2h_bytes_per_step": d2h}
+        del xh
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and oracle.ref_available():
+        threads = oracle.cpu_count()
+        value, sample = c5_cpu_reference(torch, dev, threads)
+        cpu = {"value": value, "unit": "candidates/s", "cores": threads, "kind": "reference", "sample": sample}
+
+    if dist is not None:
+        dist.barrier()
+    if rank == 0:
+        line = {
+            "metric": METRIC,
+            "value": cand / elapsed * args.steps,
+            "unit": "candidates/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": elapsed / args.steps * 1e3,
+            "higher_is_better": True,
+            "scaling": "strong",
+            "vs_baseline": None,
+            "dtype": "f32",
+            "data": "synthetic",
+            "config": {"workload": c5_workload(), "global_batch": B5, "seq_len": T5, "beam": K5, "vocab": V5,
+                       "parallelism": f"vocab x{world}" if world > 1 else "single GPU (vocab-shard path, one shard)",
+                       "l2": f"inputs ({shard_bytes / 1e9:.2f} GB per GPU) larger than L2 (126 MB)",
+                       "stage_ms": {k: round(v, 4) for k, v in stage.items()}, "rescan_rounds": d.rounds},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                         "traffic": None, "peak_kind": peak_kind, "kernel": "vs_scan_kernel",
+                         "alg_bytes_per_launch": scan_bytes},
+            "cpu_baseline": cpu,
+            "e2e": e2e,
+            "gpu_launches": args.steps * (5 + d.rounds * 2),
+            "clocks": clocks.summary(),
+        }
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.destroy_process_group()
+
+
 def main():
     args = parse()
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.workload == "c5":
+        return run_c5(args, rank, world, local)
     if args.impl == "reference":
         return run_reference_arm(args, rank, world)
 

@@ -161,6 +161,31 @@ float oracle_row_lse(const float* row, int V, int* invalid) {
     return mx + (float)log_ge1((double)lanes[0]);
 }
 
+/* The row lse split by lane (a vocabulary shard's view of oracle_row_lse): rank
+ * `rank` of `world` holds the tokens v with (v mod 256) in [rank * L, rank * L + L),
+ * L = 256 / world, shard entry i being token (i / L) * 256 + rank * L + i mod L.
+ * lanes_out[l] = the reference's lane rank * L + l of the full row, given the full
+ * row's maximum mx (src/kernels_scalar.cpp:48-66). */
+void oracle_shard_lanes(const float* shard_row, int shard_vocab, int world, float mx, float* lanes_out) {
+    const int L = LANES / world;
+    for (int l = 0; l < L; ++l) lanes_out[l] = 0.0f;
+    if (mx == NEG_INF) return;
+    for (int i = 0; i < shard_vocab; ++i) {
+        const float x = shard_row[i];
+        if (x < INFINITY && x != NEG_INF) lanes_out[i % L] = lanes_out[i % L] + oracle_exp_nonpositive(x - mx);
+    }
+}
+
+/* lse from the 256 lane sums (src/kernels.hpp:197-202, src/logits.hpp:241-243). */
+float oracle_lse_from_lanes(const float* lanes256, float mx) {
+    if (mx == NEG_INF) return NEG_INF;
+    float lanes[LANES];
+    for (int j = 0; j < LANES; ++j) lanes[j] = lanes256[j];
+    for (int s = LANES / 2; s > 0; s >>= 1)
+        for (int j = 0; j < s; ++j) lanes[j] = lanes[j] + lanes[j + s];
+    return mx + (float)log_ge1((double)lanes[0]);
+}
+
 static float softmax_probability(float x, float lse) {
     const int finite = x < INFINITY && x > NEG_INF;
     return finite ? oracle_exp_nonpositive(x - lse) : 0.0f;

@@ -45,6 +45,10 @@ void oracle_length_penalty(const int32_t* lengths, int64_t count, float alpha, f
 float oracle_gnmt_penalty(int length, float alpha);
 float oracle_exp_nonpositive(float x);
 float oracle_row_lse(const float* row, int vocab_size, int* invalid);
+/* Vocabulary shards (lane-interleaved, world = 1, 2, 4 or 8): the shard's lane sums of
+ * a row with maximum mx, and the lse from all 256 lanes. */
+void oracle_shard_lanes(const float* shard_row, int shard_vocab, int world, float mx, float* lanes_out);
+float oracle_lse_from_lanes(const float* lanes256, float mx);
 float oracle_half_to_float(uint16_t bits, int data_type);
 
 #ifdef __cplusplus

@@ -158,6 +158,10 @@ def oracle_lib() -> C.CDLL:
         lib.oracle_exp_nonpositive.argtypes = [C.c_float]
         lib.oracle_row_lse.restype = C.c_float
         lib.oracle_row_lse.argtypes = [_p, C.c_int, C.POINTER(C.c_int)]
+        lib.oracle_shard_lanes.restype = None
+        lib.oracle_shard_lanes.argtypes = [_p, C.c_int, C.c_int, C.c_float, _p]
+        lib.oracle_lse_from_lanes.restype = C.c_float
+        lib.oracle_lse_from_lanes.argtypes = [_p, C.c_float]
         lib.oracle_half_to_float.restype = C.c_float
         lib.oracle_half_to_float.argtypes = [C.c_uint16, C.c_int]
         _olib = lib

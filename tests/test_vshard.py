@@ -152,3 +152,136 @@ def test_validate_raises_on_nan_rows():
     shards = [vs.shard_inputs(x, 2, r) for r in range(2)]
     with pytest.raises(ValueError, match="NaN"):
         vs.decode_vocab_shards(shards, 600, True, eos_token=1, validate=True)
+
+
+# ---------------------------------------------------------------------------- gloo ranks (CPU)
+
+
+def _free_port() -> int:
+    import socket
+
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _gloo_problem():
+    return make_problem(3, 5, 3, 600, from_logits=True, seed=77, eos=2, min_length=2, alpha=0.6,
+                        variable_steps=True)
+
+
+def _gloo_rank(rank: int, world: int, port: int, result_path: str, shard_list_len: int):
+    import os
+    from pathlib import Path
+
+    import torch.distributed as dist
+
+    from _vshard_emu import EmuEngine
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        pb = _gloo_problem()
+        V = pb.shape[3]
+        x = torch.from_numpy(np.ascontiguousarray(pb.x))
+        shard = vs.shard_inputs(x, world, rank)
+        d = vs.ShardDecode(shard, V, True, world, rank, steps=torch.from_numpy(pb.steps), eos_token=pb.eos,
+                           min_length=pb.min_length, length_penalty_alpha=pb.alpha, shard_list_len=shard_list_len,
+                           engine=EmuEngine())
+        out = vs.decode_vocab_sharded(d)
+        ref = oracle.oracle_decode(pb)
+        bad = [n for n in OUT if out[n].numpy().tobytes() != np.ascontiguousarray(ref[n]).tobytes()]
+        Path(f"{result_path}.{rank}").write_text(f"rounds={d.rounds} " + ("ok" if not bad else "mismatch " + ",".join(bad)))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("shard_list_len", [0, 1])
+def test_vocab_sharded_protocol_on_gloo_ranks(tmp_path, shard_list_len):
+    """Two gloo ranks run decode_vocab_sharded with a CPU model of the stages; the result is
+    the oracle's full decode. One-entry shard records force the stalled-row rescans."""
+    import torch.multiprocessing as mp
+    from pathlib import Path
+
+    world = 2
+    result = str(tmp_path / "result")
+    mp.start_processes(_gloo_rank, args=(world, _free_port(), result, shard_list_len), nprocs=world,
+                       start_method="spawn", join=True)
+    texts = [Path(f"{result}.{r}").read_text() for r in range(world)]
+    for t in texts:
+        assert t.endswith("ok"), texts
+    if shard_list_len == 1:
+        assert int(texts[0].split()[0].split("=")[1]) > 0, texts
+
+
+def test_shard_lanes_rebuild_the_row_logsumexp():
+    """The oracle's per-shard lane sums, put together lane by lane, give its full-row lse."""
+    rng = np.random.default_rng(4)
+    lib = oracle.oracle_lib()
+    for V in (1, 200, 256, 1000, 1537):
+        row = (rng.standard_normal(V) * 3).astype(np.float32)
+        row[rng.random(V) < 0.05] = -np.inf
+        inv = C.c_int(0)
+        ref = lib.oracle_row_lse(row.ctypes.data_as(C.c_void_p), V, C.byref(inv))
+        mx = np.float32(row[row < np.inf].max())
+        for W in (1, 2, 4, 8):
+            lanes = []
+            for r in range(W):
+                sh = np.ascontiguousarray(row[vs.shard_tokens(V, W, r).numpy()])
+                out = np.zeros(256 // W, np.float32)
+                lib.oracle_shard_lanes(sh.ctypes.data_as(C.c_void_p), sh.size, W, float(mx),
+                                       out.ctypes.data_as(C.c_void_p))
+                lanes.append(out)
+            lanes = np.ascontiguousarray(np.concatenate(lanes))
+            got = lib.oracle_lse_from_lanes(lanes.ctypes.data_as(C.c_void_p), float(mx))
+            assert np.float32(got).tobytes() == np.float32(ref).tobytes(), (V, W)
+
+
+# ---------------------------------------------------------------------------- NCCL ranks (2 GPUs)
+
+
+def _nccl_rank(rank: int, world: int, port: int, result_path: str, case: int, shard_list_len: int):
+    import datetime
+    import os
+    from pathlib import Path
+
+    import torch.distributed as dist
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+    try:
+        B, T, K, V, dtype, logits, extra = CASES[case]
+        pb = make_problem(B, T, K, V, dtype=dtype, from_logits=logits, seed=1300 + case, **extra)
+        x = full_inputs(pb)
+        steps = torch.from_numpy(pb.steps).cuda() if pb.steps is not None else None
+        banned = torch.from_numpy(pb.banned).cuda() if pb.banned is not None else None
+        out = vs.decode_vocab_sharded(vs.shard_inputs(x, world, rank), V, logits, steps, eos_token=pb.eos,
+                                      min_length=pb.min_length, length_penalty_alpha=pb.alpha, banned_tokens=banned,
+                                      no_repeat_ngram_size=pb.ngram, repetition_penalty=pb.rep_penalty,
+                                      extra_eos=pb.extra_eos, shard_list_len=shard_list_len)
+        ref = oracle.oracle_decode(pb)
+        bad = [n for n in OUT if out[n].cpu().numpy().tobytes() != np.ascontiguousarray(ref[n]).tobytes()]
+        Path(f"{result_path}.{rank}").write_text("ok" if not bad else "mismatch " + ",".join(bad))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("case,shard_list_len", [(0, 0), (5, 0), (6, 0), (2, 1)])
+def test_vocab_sharded_decode_on_two_nccl_ranks(tmp_path, case, shard_list_len):
+    """One process per GPU over NCCL: every rank's outputs are the oracle's full decode."""
+    import torch.multiprocessing as mp
+    from pathlib import Path
+
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    world = 2
+    result = str(tmp_path / "result")
+    mp.start_processes(_nccl_rank, args=(world, _free_port(), result, case, shard_list_len), nprocs=world,
+                       start_method="spawn", join=True)
+    for r in range(world):
+        assert Path(f"{result}.{r}").read_text() == "ok", r
