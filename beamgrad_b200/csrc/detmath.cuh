@@ -218,7 +218,11 @@ __device__ __forceinline__ void exp_nonpositive_fast2(const Pack2& q, uint64_t d
     f2_unpack(f2_add(q, f2_mul(q, d, f2_splat(kLog2e)), f2_splat(0.5f)), y_lo, y_hi);
     const float z_lo = __fadd_rd(y_lo, kMagic), z_hi = __fadd_rd(y_hi, kMagic);
     const uint64_t k = f2_sub(q, f2_pack(z_lo, z_hi), f2_splat(kMagic));
-    const uint64_t r = f2_sub(q, f2_sub(q, d, f2_mul(q, k, f2_splat(kLn2Hi))), f2_mul(q, k, f2_splat(kLn2Lo)));
+    // d - round(k ln2hi) is d - k ln2hi rounded once, a single fma: k ln2hi is exact
+    // (k an integer in [-126, 0], ln2hi = 355/512 needs 9 significant bits).
+    const uint64_t r1 = f2_fma(k, f2_splat(-kLn2Hi), d);
+    // r1 - round(k ln2lo) = r1 + round(k (-ln2lo)): rounding to nearest is sign-symmetric.
+    const uint64_t r = f2_add(q, r1, f2_mul(q, k, f2_splat(-kLn2Lo)));
     const uint64_t r2 = f2_mul(q, r, r);
     uint64_t p = f2_splat(kP0);
     p = f2_add(q, f2_mul(q, p, r), f2_splat(kP1));
