@@ -1588,8 +1588,14 @@ __device__ __forceinline__ void prepare_row(const DecodeParams& p, RowShared& sh
 // step's best keys, the carried-forward finished beams, their merge in the
 // full candidate order, and the new trace / state / prefixes / finals.
 // ---------------------------------------------------------------------------
-template <int KMAX, int LIST = KMAX>
-__device__ void select_fast(const DecodeParams& p, int t, int b, const Meta& m) {
+// The selection proper, from the step's row lists in registers (mine[j]: entry lane + 32j
+// of the K rows' LIST-entry lists, zeros for no candidate) and the state before the step
+// (lane k < beam holds slot k).
+template <int KMAX, int LIST>
+__device__ void select_fast_core(const DecodeParams& p, int t, int b, const Meta& m,
+                                 uint64_t (&mine)[(KMAX * LIST + 31) / 32], float s_raw, int s_len, int s_end,
+                                 int s_last) {
+    constexpr int kPer = (KMAX * LIST + 31) / 32;
     const int lane = threadIdx.x & 31;
     const int K = p.K;
     const uint32_t V = static_cast<uint32_t>(p.V);
@@ -1598,32 +1604,6 @@ __device__ void select_fast(const DecodeParams& p, int t, int b, const Meta& m) 
     const bool active = t < m.steps;
     const bool last_step = p.step_api ? true : (t == p.T - 1);
     const int beam = m.beam;
-
-    // State before the step (lane k holds slot k) and the step's candidate keys.
-    float s_raw = f_ninf();
-    int s_len = 0, s_last = -1;
-    int s_end = 0;
-    if (lane < beam) {
-        s_raw = ld_cg(p.raw + sbase + lane);
-        s_len = ld_cg(p.len + sbase + lane);
-        s_end = ld_cg(p.ended + sbase + lane);
-        if (p.step_api) {
-            if (p.caller_prefix && s_len >= 1 && s_len <= p.prefix_stride)
-                s_last = ld_cg(p.caller_prefix + (sbase + lane) * p.prefix_stride + s_len - 1);
-        } else {
-            s_last = ld_cg(p.last + sbase + lane);
-        }
-    }
-    // Row lists of LIST keys each (unsorted; zeros for no candidate).
-    constexpr int kPer = (KMAX * LIST + 31) / 32;
-    const uint64_t* lists = p.keys + sbase * LIST;
-    const int n = K * LIST;
-    uint64_t mine[kPer];
-#pragma unroll
-    for (int j = 0; j < kPer; ++j) {
-        const int i = lane + 32 * j;
-        mine[j] = (active && i < n) ? ld_cg(lists + i) : 0;
-    }
 
     int filled = 0;
     // This lane's candidate (scanned: lanes [0, ns); carried: lanes [ns, ns + nc)).
@@ -1795,8 +1775,40 @@ __device__ void select_fast(const DecodeParams& p, int t, int b, const Meta& m) 
         if (p.out.final_raw_scores) p.out.final_raw_scores[sl] = raw;
         if (p.out.final_lengths) p.out.final_lengths[sl] = len;
     }
-    __threadfence();
-    __syncwarp();
+    __syncwarp();  // callers order the writes for other CTAs (fence or release) before publishing
+}
+
+// select_fast_core with the state and the row lists (p.keys) read from global memory.
+template <int KMAX, int LIST = KMAX>
+__device__ void select_fast(const DecodeParams& p, int t, int b, const Meta& m) {
+    const int lane = threadIdx.x & 31;
+    const int K = p.K;
+    const int64_t sbase = static_cast<int64_t>(b) * K;
+    const bool active = t < m.steps;
+    float s_raw = f_ninf();
+    int s_len = 0, s_last = -1;
+    int s_end = 0;
+    if (lane < m.beam) {
+        s_raw = ld_cg(p.raw + sbase + lane);
+        s_len = ld_cg(p.len + sbase + lane);
+        s_end = ld_cg(p.ended + sbase + lane);
+        if (p.step_api) {
+            if (p.caller_prefix && s_len >= 1 && s_len <= p.prefix_stride)
+                s_last = ld_cg(p.caller_prefix + (sbase + lane) * p.prefix_stride + s_len - 1);
+        } else {
+            s_last = ld_cg(p.last + sbase + lane);
+        }
+    }
+    constexpr int kPer = (KMAX * LIST + 31) / 32;
+    const uint64_t* lists = p.keys + sbase * LIST;
+    const int n = K * LIST;
+    uint64_t mine[kPer];
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) {
+        const int i = lane + 32 * j;
+        mine[j] = (active && i < n) ? ld_cg(lists + i) : 0;
+    }
+    select_fast_core<KMAX, LIST>(p, t, b, m, mine, s_raw, s_len, s_end, s_last);
 }
 
 // ---------------------------------------------------------------------------
@@ -2129,9 +2141,10 @@ __device__ void rescan_row(const DecodeParams& p, SelScratch& ss, int t, int b, 
     group_sync<NT>(bar);
 }
 
-// Selection of step t of example b from the row records, by a group of NT threads.
+// Selection of step t of example b with n-gram blocking or a repetition penalty: warp w of
+// the group takes rows w, w + NW, ..., whose constraint checks read the parent's prefix.
 template <int DT, bool LOGITS, int KMAX, int LIST, int NT>
-__device__ void chain_select(const DecodeParams& p, SelScratch& ss, int t, int b, const Meta& m, int ltid, int bar) {
+__device__ void chain_select_constrained(const DecodeParams& p, SelScratch& ss, int t, int b, const Meta& m, int ltid, int bar) {
     constexpr int NW = NT / 32;
     const int lane = ltid & 31;
     const int lw = ltid >> 5;
@@ -2205,32 +2218,153 @@ __device__ void chain_select(const DecodeParams& p, SelScratch& ss, int t, int b
     group_sync<NT>(bar);
 }
 
+// Selection of step t of example b from the row records (no n-gram blocking or repetition
+// penalty), by a group of NT threads: warp 0 of the group loads every row's parent state, record info and record entries in one
+// batch (entry f = lane + 32u of the K rows' LIST-entry lists, so each register holds whole
+// rows in aligned LIST-lane segments), decides each record's exactness with segmented
+// shuffles, and hands the lists and the state to the selection in registers; rows whose
+// record is not enough are rescanned by the whole group first.
+template <int DT, bool LOGITS, int KMAX, int LIST, int NT>
+__device__ void chain_select(const DecodeParams& p, SelScratch& ss, int t, int b, const Meta& m, int ltid, int bar) {
+    if (p.ngram > 0 || p.penalise) {
+        chain_select_constrained<DT, LOGITS, KMAX, LIST, NT>(p, ss, t, b, m, ltid, bar);
+        return;
+    }
+    constexpr int kPer = (KMAX * LIST + 31) / 32;
+    static_assert(32 % LIST == 0 || LIST % 32 == 0, "rows must fill whole lane segments");
+    const int lane = ltid & 31;
+    const int lw = ltid >> 5;
+    const int K = p.K;
+    const uint32_t V = static_cast<uint32_t>(p.V);
+    const bool active = t < m.steps;
+    const int R = m.beam < KMAX ? m.beam : KMAX;
+    const int64_t sbase = static_cast<int64_t>(b) * K;
+    const int64_t row0 = (static_cast<int64_t>(b) * p.T + t) * K;
+    float s_raw = f_ninf();
+    int s_len = 0, s_end = 0, s_last = -1;
+    uint64_t mine[kPer];
+    if (lw == 0) {
+        // One batch of loads: lane k < K the state of slot k and row k's info / lse; every
+        // lane its record entries.
+        float lse_l = 0.0f;
+        uint32_t info_l = 0;
+        if (lane < K) {
+            s_raw = ld_cg(p.raw + sbase + lane);
+            s_len = ld_cg(p.len + sbase + lane);
+            s_end = ld_cg(p.ended + sbase + lane);
+            s_last = ld_cg(p.last + sbase + lane);
+            info_l = ld_cg(p.rinfo + row0 + lane);
+            lse_l = ld_cg(p.rlse + row0 + lane);
+        }
+        uint64_t xk[kPer];
+#pragma unroll
+        for (int u = 0; u < kPer; ++u) {
+            const int f = lane + 32 * u;
+            xk[u] = f < K * LIST ? ld_cg(p.rkeys + row0 * LIST + f) : 0;
+        }
+        const bool read_l = active && lane < m.beam && (t > 0 || lane == 0) && f_finite(s_raw) &&
+                            !(m.eos >= 0 && s_end != 0);
+        const unsigned reads = __ballot_sync(0xffffffffu, read_l);
+        unsigned inexact = 0;
+#pragma unroll
+        for (int u = 0; u < kPer; ++u) {
+            const int f = lane + 32 * u;
+            const int k = f / LIST;       // row of this entry
+            const int e = f - k * LIST;   // its position in the record
+            const int src = k < K ? k : 0;
+            const float pr = __shfl_sync(0xffffffffu, s_raw, src);
+            const int plen = __shfl_sync(0xffffffffu, s_len, src);
+            const uint32_t info = __shfl_sync(0xffffffffu, info_l, src);
+            const float lse = __shfl_sync(0xffffffffu, lse_l, src);
+            const bool read = k < K && ((reads >> k) & 1u);
+            const int cnt = static_cast<int>(info >> 8);
+            float raw_plain = f_ninf(), raw = f_ninf();
+            uint64_t key = 0;
+            if (read && e < cnt && xk[u] != 0) {
+                const float x = key_raw(xk[u]);
+                const float lp = LOGITS ? __fsub_rn(x, lse) : x;
+                if (lp < f_inf() && lp != f_ninf()) {
+                    raw_plain = __fadd_rn(pr, lp);
+                    raw = raw_plain;
+                    key = make_key(raw, static_cast<uint32_t>(k) * V + key_index(xk[u]));
+                }
+            }
+            // Exactness of the record: R entries whose raw is strictly above the last
+            // entry's, or every eligible entry recorded. The record's EOS masking assumed
+            // parent length t.
+            constexpr int SEG = LIST < 32 ? LIST : 32;
+            const int seg0 = lane & ~(SEG - 1);
+            const float raw_last = __shfl_sync(0xffffffffu, raw_plain, seg0 + SEG - 1);
+            int above = raw > raw_last ? 1 : 0;
+#pragma unroll
+            for (int o = SEG / 2; o >= 1; o >>= 1) above += __shfl_xor_sync(0xffffffffu, above, o);
+            const bool exact = plen == t && (cnt < LIST || above >= R);
+            if (read && e == 0 && !exact) inexact |= 1u << k;
+            mine[u] = (read && exact) ? key : 0;
+        }
+        inexact = __reduce_or_sync(0xffffffffu, inexact);
+        const bool any_bad = __any_sync(0xffffffffu, read_l && (info_l & 1u));
+        if (lane == 0) {
+            ss.fallback = inexact;
+            ss.invalid = any_bad ? 1 : 0;
+        }
+        if (lane < K && p.row_lse) p.row_lse[row0 + lane] = (read_l && LOGITS) ? lse_l : 0.0f;
+    }
+    group_sync<NT>(bar);
+    const unsigned fb_all = ss.fallback;
+    unsigned fb = fb_all;
+    while (fb) {
+        const int k = __ffs(fb) - 1;
+        fb &= fb - 1;
+        rescan_row<DT, LOGITS, KMAX, LIST, NT>(p, ss, t, b, k, m, ld_cg(p.rlse + row0 + k), ltid, bar);
+    }
+    if (ltid == 0 && ss.invalid && p.out.invalid_input) p.out.invalid_input[b] = 1;
+    if (fb_all) group_sync<NT>(bar);
+    if (lw == 0) {
+        if (fb_all) {
+            // The rescanned rows' lists (p.keys) replace their entries.
+#pragma unroll
+            for (int u = 0; u < kPer; ++u) {
+                const int f = lane + 32 * u;
+                const int k = f / LIST;
+                if (k < K && ((fb_all >> k) & 1u)) mine[u] = ld_cg(p.keys + sbase * LIST + f);
+            }
+        }
+        select_fast_core<KMAX, LIST>(p, t, b, m, mine, lane < m.beam ? s_raw : f_ninf(), lane < m.beam ? s_len : 0,
+                                     lane < m.beam ? s_end : 0, lane < m.beam ? s_last : -1);
+    }
+    group_sync<NT>(bar);
+}
+
 // Arrival of one finished row (or of the selection of step t - 1) on example b's step-t
 // count; while the group completes counts it selects those steps (select(step)) and
 // arrives for the next. Called by all NT threads of the group after their writes.
+// Arrival counter increment with release (the group's writes, ordered before it by the
+// group barrier, become visible first) and acquire (when this arrival completes the
+// count, the other arrivals' writes are visible to the group after the next barrier).
+__device__ __forceinline__ uint32_t arrive_acq_rel(uint32_t* counter) {
+    uint32_t old;
+    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(old) : "l"(counter) : "memory");
+    return old;
+}
+
 template <int NT, class Select>
 __device__ __forceinline__ void chain_arrive_with(const DecodeParams& p, SelScratch& ss, int t, int b, int ltid,
                                                   int bar, Select&& select) {
-    // The group's writes are ordered before the arrival by the barrier and the arriving
-    // thread's (cumulative) fence.
     group_sync<NT>(bar);
     if (ltid == 0) {
-        __threadfence();
         const uint32_t target = static_cast<uint32_t>(p.K) + (t > 0 ? 1u : 0u);
-        ss.next = atomicAdd(p.count + static_cast<int64_t>(b) * p.T + t, 1u) == target - 1u ? t : -1;
+        ss.next = arrive_acq_rel(p.count + static_cast<int64_t>(b) * p.T + t) == target - 1u ? t : -1;
     }
     group_sync<NT>(bar);
     int ct = ss.next;
     while (ct >= 0) {
-        if (ltid == 0) __threadfence();
-        group_sync<NT>(bar);
         select(ct);
         if (ltid == 0) {
             int nxt = -1;
-            if (ct + 1 < p.T) {
-                __threadfence();
-                if (atomicAdd(p.count + static_cast<int64_t>(b) * p.T + ct + 1, 1u) == static_cast<uint32_t>(p.K)) nxt = ct + 1;
-            }
+            if (ct + 1 < p.T &&
+                arrive_acq_rel(p.count + static_cast<int64_t>(b) * p.T + ct + 1) == static_cast<uint32_t>(p.K))
+                nxt = ct + 1;
             ss.next = nxt;
         }
         group_sync<NT>(bar);
@@ -2355,6 +2489,268 @@ __global__ void __launch_bounds__(kThreads, 3) decode_chain_kernel(const __grid_
         // Arrive: the K rows of (t, b), prepared or not, and for t > 0 the selection of t - 1.
         chain_arrive<DT, LOGITS, KMAX, LIST, kThreads>(p, sh.sel, t, b, m, tid, 0);
     }
+}
+
+// ---------------------------------------------------------------------------
+// Chained decode of log-probability rows by single warps (beams up to 16, no banned
+// tokens). Each warp takes row tickets on its own: it streams the row once (eight
+// 16-byte loads in flight per lane) keeping the lane's maximum (NaN-propagating) and
+// its four largest entries; the LIST-th largest lane maximum bounds the record from
+// below (LIST eligible entries reach it), so the record is the best LIST of the kept
+// entries at or above it -- a lane whose fourth entry reaches the bound reads its share
+// again, with the whole warp. Rows with NaN/+inf, without a bound, or with too many
+// candidates fall back to a full scan with the register top-k. Arrival and selection
+// are the chained protocol at group width 32; no barrier spans more than one warp.
+// ---------------------------------------------------------------------------
+constexpr int kWarpCand = 64;  // record candidates per warp
+
+struct WarpRowShared {
+    SelScratch sel;
+    uint64_t cand[kWarpCand];
+};
+
+// Top four (value, index) of a lane, v[0] >= ... >= v[3]; strict comparisons, so NaN
+// never enters.
+__device__ __forceinline__ void lane_top4(float (&v)[4], int (&ix)[4], float x, int i) {
+    if (!(x > v[3])) return;
+    if (x > v[1]) {
+        v[3] = v[2];
+        ix[3] = ix[2];
+        v[2] = v[1];
+        ix[2] = ix[1];
+        if (x > v[0]) {
+            v[1] = v[0];
+            ix[1] = ix[0];
+            v[0] = x;
+            ix[0] = i;
+        } else {
+            v[1] = x;
+            ix[1] = i;
+        }
+    } else if (x > v[2]) {
+        v[3] = v[2];
+        ix[3] = ix[2];
+        v[2] = x;
+        ix[2] = i;
+    } else {
+        v[3] = x;
+        ix[3] = i;
+    }
+}
+
+// The lane owning entry v of a row split rs among 32 lanes (chunk c on lane c mod 32,
+// ragged ends on lanes 0 .. n_ends - 1); -1 outside the row.
+__device__ __forceinline__ int warp_owner(const RowSplit& rs, int v) {
+    if (v < 0 || v >= rs.V) return -1;
+    if (v < rs.head) return v;
+    if (v >= rs.tail0) return rs.head + (v - rs.tail0);
+    return ((v - rs.head) / rs.per) & 31;
+}
+
+// The record of one log-probability row (best LIST eligible entries by x-key), written
+// to rec by the calling warp; returns the row's info word (bit 0: NaN/+inf; count << 8).
+template <int DT, int LIST>
+__device__ uint32_t warp_row_record(const DecodeParams& p, WarpRowShared& ws, const char* row, const Meta& m, int t,
+                                    uint64_t* rec) {
+    using E = Elem<DT>;
+    constexpr int PER = 16 / E::kBytes;
+    constexpr int UR = 4;
+    const int lane = threadIdx.x & 31;
+    const unsigned lt = (1u << lane) - 1u;
+    const int V = p.V;
+    const RowSplit rs = RowSplit::of<E::kBytes>(row, V);
+    const char* body = row + static_cast<size_t>(rs.head) * E::kBytes;
+    const bool mask_eos = m.eos >= 0 && t + 1 < m.min_length;
+    // EOS tokens of this lane: they never bound the record; a masked one is left out of the
+    // four, and a lane owning two masked ones reads its share again.
+    bool dirty = false;
+    int skip = -1, n_masked = 0;
+    if (m.eos >= 0) {
+        auto own = [&](int v) {
+            if (warp_owner(rs, v) != lane) return;
+            dirty = true;
+            if (mask_eos && v != skip) {
+                skip = v;
+                ++n_masked;
+            }
+        };
+        own(m.eos);
+        for (int i = 0; i < p.n_extra; ++i) own(p.extra[i]);
+    }
+    float mxn = f_ninf();
+    float tv[4] = {f_ninf(), f_ninf(), f_ninf(), f_ninf()};
+    int ti[4] = {0, 0, 0, 0};
+    auto single = [&](int v) {
+        const float x = load_elem<DT>(row, v);
+        mxn = max_nan(mxn, x);
+        if (v != skip) lane_top4(tv, ti, x, v);
+    };
+    if (lane < rs.head && lane < rs.n_ends()) single(rs.end_entry(lane));
+    if constexpr (E::kBytes == 2) {
+        uint32_t mx2 = h2_ninf<DT>();
+        for (int c0 = lane; c0 < rs.nvec; c0 += UR * 32) {
+            uint4 q[UR];
+#pragma unroll
+            for (int u = 0; u < UR; ++u) {
+                const int c = c0 + u * 32;
+                if (c < rs.nvec) q[u] = ld_stream_v4(body + static_cast<size_t>(c) * 16);
+            }
+#pragma unroll
+            for (int u = 0; u < UR; ++u) {
+                const int c = c0 + u * 32;
+                if (c < rs.nvec) {
+                    mx2 = h2_max_nan<DT>(mx2, h2_max_nan<DT>(h2_max_nan<DT>(q[u].x, q[u].y), h2_max_nan<DT>(q[u].z, q[u].w)));
+                    const uint32_t m2 = h2_max<DT>(h2_max<DT>(q[u].x, q[u].y), h2_max<DT>(q[u].z, q[u].w));
+                    if (fmaxf(h2_lo<DT>(m2), h2_hi<DT>(m2)) > tv[3]) {
+                        float x[PER];
+                        unpack16<DT>(q[u], x);
+#pragma unroll
+                        for (int e = 0; e < PER; ++e)
+                            if (rs.head + c * PER + e != skip) lane_top4(tv, ti, x[e], rs.head + c * PER + e);
+                    }
+                }
+            }
+        }
+        mxn = max_nan(mxn, max_nan(h2_lo<DT>(mx2), h2_hi<DT>(mx2)));
+    } else {
+        for (int c0 = lane; c0 < rs.nvec; c0 += UR * 32) {
+            uint4 q[UR];
+#pragma unroll
+            for (int u = 0; u < UR; ++u) {
+                const int c = c0 + u * 32;
+                if (c < rs.nvec) q[u] = ld_stream_v4(body + static_cast<size_t>(c) * 16);
+            }
+#pragma unroll
+            for (int u = 0; u < UR; ++u) {
+                const int c = c0 + u * 32;
+                if (c < rs.nvec) {
+                    const float a = __uint_as_float(q[u].x), b = __uint_as_float(q[u].y);
+                    const float d = __uint_as_float(q[u].z), e = __uint_as_float(q[u].w);
+                    mxn = max_nan(mxn, max_nan(max_nan(a, b), max_nan(d, e)));
+                    if (fmaxf(fmaxf(a, b), fmaxf(d, e)) > tv[3]) {
+                        const int base = rs.head + c * 4;
+                        if (base != skip) lane_top4(tv, ti, a, base);
+                        if (base + 1 != skip) lane_top4(tv, ti, b, base + 1);
+                        if (base + 2 != skip) lane_top4(tv, ti, d, base + 2);
+                        if (base + 3 != skip) lane_top4(tv, ti, e, base + 3);
+                    }
+                }
+            }
+        }
+    }
+    if (lane >= rs.head && lane < rs.n_ends()) single(rs.end_entry(lane));
+    const bool bad = !(mxn < f_inf());
+    const bool any_bad = __any_sync(0xffffffffu, bad);
+    auto eligible = [&](int v) { return !(mask_eos && is_eos(p, m, v)); };
+    const float bound = __shfl_sync(0xffffffffu, warp_sort_desc((bad || dirty) ? f_ninf() : mxn), LIST - 1);
+    int n = 0;
+    if (!any_bad && bound != f_ninf()) {
+        auto push = [&](bool cond, float x, int v) {
+            const unsigned mask = __ballot_sync(0xffffffffu, cond);
+            const int pos = n + __popc(mask & lt);
+            if (cond && pos < kWarpCand) ws.cand[pos] = make_key(x, static_cast<uint32_t>(v));
+            n += __popc(mask);
+        };
+        const bool reread = n_masked > 1 || tv[3] >= bound;
+#pragma unroll
+        for (int u = 0; u < 4; ++u) push(!reread && tv[u] >= bound, tv[u], ti[u]);
+        unsigned todo = __ballot_sync(0xffffffffu, reread);
+        while (todo) {
+            const int src = __ffs(todo) - 1;
+            todo &= todo - 1;
+            if (src < rs.n_ends()) {
+                const int v = rs.end_entry(src);
+                const float x = lane == 0 ? load_elem<DT>(row, v) : f_ninf();
+                push(lane == 0 && x >= bound && x < f_inf() && eligible(v), x, v);
+            }
+            const int nch = src < rs.nvec ? (rs.nvec - src + 31) / 32 : 0;
+            for (int r0 = 0; r0 < nch; r0 += 32) {
+                const int c = src + (r0 + lane) * 32;
+                const bool have = r0 + lane < nch;
+                float x[PER];
+                if (have) unpack16<DT>(ld_stream_v4(body + static_cast<size_t>(c) * 16), x);
+#pragma unroll
+                for (int e = 0; e < PER; ++e) {
+                    const int v = rs.head + c * PER + e;
+                    push(have && x[e] >= bound && x[e] < f_inf() && eligible(v), x[e], v);
+                }
+            }
+        }
+        __syncwarp();
+        if (n <= kWarpCand) {
+            // Rank by counting (keys are unique).
+            for (int i = lane; i < n; i += 32) {
+                const uint64_t key = ws.cand[i];
+                int rank = 0;
+                for (int j = 0; j < n; ++j) rank += ws.cand[j] > key ? 1 : 0;
+                if (rank < LIST) rec[rank] = key;
+            }
+            __syncwarp();
+            return (any_bad ? 1u : 0u) | (static_cast<uint32_t>(n < LIST ? n : LIST) << 8);
+        }
+    }
+    // Fallback: the whole row through the register top-k.
+    WarpTopK<LIST> wt;
+    wt.init(f_ninf());
+    scan_chunks_ballot_n<DT, 32>(row, rs, false, lane, [&](float x) { return x >= wt.thr; },
+                                 [&](float x, int v, bool valid) {
+                                     uint64_t key = 0;
+                                     if (valid && x >= wt.thr && x < f_inf() && x != f_ninf() && eligible(v))
+                                         key = make_key(x, static_cast<uint32_t>(v));
+                                     wt.offer(key, lane);
+                                 });
+    if (lane < LIST) rec[lane] = wt.wl;
+    const int cnt = __popc(__ballot_sync(0xffffffffu, lane < LIST && wt.wl != 0));
+    __syncwarp();
+    return (any_bad ? 1u : 0u) | (static_cast<uint32_t>(cnt) << 8);
+}
+
+template <int DT, int KMAX>
+__global__ void __launch_bounds__(kThreads, 3) decode_chain_warp_kernel(const __grid_constant__ DecodeParams p) {
+    constexpr int LIST = chain_list_len<KMAX>();
+    using E = Elem<DT>;
+    __shared__ WarpRowShared wsh[kWarps];
+    const int lane = threadIdx.x & 31;
+    const int warp = threadIdx.x >> 5;
+    WarpRowShared& ws = wsh[warp];
+    const int bar = 1 + warp;  // the warp's named barrier (0 is the CTA's)
+    const int K = p.K, V = p.V, T = p.T;
+    const uint32_t rows_per_step = static_cast<uint32_t>(p.B) * static_cast<uint32_t>(K);
+    const uint32_t total = rows_per_step * static_cast<uint32_t>(T);
+    // Tickets are fetched one row ahead, so the atomic's round trip overlaps a row.
+    uint32_t next = 0;
+    if (lane == 0) next = atomicAdd(p.ticket, 1u);
+    for (;;) {
+        const uint32_t tk = __shfl_sync(0xffffffffu, next, 0);
+        if (tk >= total) break;
+        if (lane == 0) next = atomicAdd(p.ticket, 1u);
+        const int t = static_cast<int>(tk / rows_per_step);
+        const uint32_t rem = tk - static_cast<uint32_t>(t) * rows_per_step;
+        const int b = static_cast<int>(rem / static_cast<uint32_t>(K));
+        const int k = static_cast<int>(rem - static_cast<uint32_t>(b) * static_cast<uint32_t>(K));
+        const Meta m = load_meta(p, b);
+        const int64_t rowi = (static_cast<int64_t>(b) * T + t) * K + k;
+        if (t < m.steps && k < m.beam && (t > 0 || k == 0)) {
+            const char* row = static_cast<const char*>(p.inputs) + rowi * static_cast<int64_t>(V) * E::kBytes;
+            const uint32_t info = warp_row_record<DT, LIST>(p, ws, row, m, t, p.rkeys + rowi * LIST);
+            if (lane == 0) p.rinfo[rowi] = info;
+        }
+        chain_arrive<DT, false, KMAX, LIST, 32>(p, ws.sel, t, b, m, lane, bar);
+    }
+}
+
+template <int DT, int KMAX>
+static cudaError_t launch_chain_warp_as(const DecodeParams& p, cudaStream_t stream, int sm_count) {
+    auto kernel = decode_chain_warp_kernel<DT, KMAX>;
+    int per_sm = 0;
+    cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kThreads, 0);
+    if (e != cudaSuccess) return e;
+    if (per_sm < 1) per_sm = 1;
+    const int64_t warps = static_cast<int64_t>(p.B) * p.K * p.T;
+    int64_t grid = static_cast<int64_t>(sm_count) * per_sm;
+    if (grid * kWarps > warps) grid = (warps + kWarps - 1) / kWarps;
+    kernel<<<static_cast<unsigned>(grid), kThreads, 0, stream>>>(p);
+    return cudaGetLastError();
 }
 
 template <int DT, bool LOGITS, int KMAX>
@@ -3070,6 +3466,13 @@ static cudaError_t launch_chain_wide_as(const DecodeParams& p, cudaStream_t stre
 template <int DT, bool LOGITS>
 static cudaError_t launch_decode_k(const DecodeParams& p, cudaStream_t stream, int sm_count) {
     const int K = p.K;
+    if (p.chain && !LOGITS && !p.banned && K <= kFastBeam) {
+        if (K <= 1) return launch_chain_warp_as<DT, 1>(p, stream, sm_count);
+        if (K <= 2) return launch_chain_warp_as<DT, 2>(p, stream, sm_count);
+        if (K <= 4) return launch_chain_warp_as<DT, 4>(p, stream, sm_count);
+        if (K <= 8) return launch_chain_warp_as<DT, 8>(p, stream, sm_count);
+        return launch_chain_warp_as<DT, 16>(p, stream, sm_count);
+    }
     if (p.chain) {
         if (K <= 1) return launch_chain_as<DT, LOGITS, 1>(p, stream, sm_count);
         if (K <= 2) return launch_chain_as<DT, LOGITS, 2>(p, stream, sm_count);
