@@ -213,6 +213,14 @@ SIGNATURES = {
     # additions (include/dbs_cuda_b200.h)
     "dbs_cuda_b200_abi_version": (C.c_int, []),
     "dbs_cuda_backtrack": (C.c_int, [C.POINTER(DecodeArgs), _p, _p, _p, _p]),
+    "dbs_cuda_advance_prefixes": (
+        C.c_int,
+        [C.c_int, C.c_int, C.c_int, C.c_int, _p, _p, _p, _p, _p, _p, _p, _p, _p],
+    ),
+    "dbs_cuda_backward_dense": (
+        C.c_int,
+        [C.POINTER(DecodeArgs), C.POINTER(BackwardInputs), _p, C.c_int, _p, C.c_int64, _p],
+    ),
     "dbs_cuda_decode_no_alloc": (
         C.c_int,
         [_p, C.c_int, C.c_int, C.POINTER(DecodeArgs), C.POINTER(SearchOptions), C.POINTER(DecodeOutputs), _p, _p],
@@ -228,7 +236,8 @@ SIGNATURES = {
 
 VSHARD_SYMBOLS = ("dbs_cuda_vshard_plan", "dbs_cuda_vshard_scan", "dbs_cuda_vshard_lanes", "dbs_cuda_vshard_merge",
                   "dbs_cuda_vshard_select", "dbs_cuda_vshard_rescan")
-ADDED_SYMBOLS = ("dbs_cuda_b200_abi_version", "dbs_cuda_backtrack", "dbs_cuda_decode_no_alloc") + VSHARD_SYMBOLS
+ADDED_SYMBOLS = ("dbs_cuda_b200_abi_version", "dbs_cuda_backtrack", "dbs_cuda_backward_dense", "dbs_cuda_advance_prefixes",
+                 "dbs_cuda_decode_no_alloc") + VSHARD_SYMBOLS
 REFERENCE_SYMBOLS = [n for n in SIGNATURES if n not in ADDED_SYMBOLS]
 
 # Size of the fixed device array behind dbs_cuda_decode_no_alloc (DBS_CUDA_B200_NO_ALLOC_SCRATCH_BYTES).

@@ -40,7 +40,7 @@ NVCC_FLAGS = [
     "-fPIC,-ffp-contract=off,-fvisibility=hidden",
 ]
 LIB_SOURCES = ["decode.cu", "decode_f32.cu", "decode_f16.cu", "decode_bf16.cu", "backward.cu", "api.cu", "static_scratch.cu",
-               "vshard.cu"]
+               "vshard.cu", "search.cu"]
 
 
 def _nvcc() -> str:
@@ -75,8 +75,12 @@ def build_lib(force: bool = False, verbose: bool = False, ptxas_info: bool = Fal
     nvcc = _nvcc()
     from concurrent.futures import ThreadPoolExecutor
 
+    headers = list(CSRC.glob("*.cuh")) + list(INCLUDE.glob("*.h"))
+
     def compile_one(src: str) -> tuple[str, str]:
         obj = build_dir / (Path(src).stem + ".o")
+        if not force and not ptxas_info and not _stale(obj, [CSRC / src, *headers]):
+            return str(obj), ""
         cmd = [nvcc, *ARCH, *NVCC_FLAGS, "-I", str(INCLUDE), "-I", str(CSRC), "-c", str(CSRC / src), "-o", str(obj)]
         if ptxas_info:
             cmd += ["-Xptxas", "-v"]

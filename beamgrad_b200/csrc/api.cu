@@ -29,7 +29,13 @@ size_t decode_select_smem(int K);
 cudaError_t launch_backward(const BackwardParams& p, cudaStream_t stream);
 cudaError_t launch_logit_correction(const BackwardParams& p, int dtype, const void* logits, const float* row_lse,
                                     cudaStream_t stream);
+cudaError_t launch_dense_grad(const BackwardParams& p, int in_type, const void* logits, const float* row_lse,
+                              int out_type, void* grad, int vec, unsigned grid, cudaStream_t stream);
 cudaError_t launch_length_penalty(const int32_t* lengths, int64_t count, float alpha, float* out, cudaStream_t stream);
+// search.cu
+cudaError_t launch_advance_prefixes(int B, int K, int step, int stride, const int32_t* parents, const int32_t* tokens,
+                                    const uint8_t* from_logprob, const int32_t* in, int32_t* out, const float* raw,
+                                    const uint8_t* finished, uint8_t* any_live, int sm_count, cudaStream_t stream);
 cudaError_t launch_backtrack(int B, int T, int K, const int32_t* tokens, const int32_t* parents,
                              const int32_t* steps_pe, int64_t* out, cudaStream_t stream);
 
@@ -619,6 +625,65 @@ DBS_CUDA_EXPORT int dbs_cuda_backward_ex(const DBSCudaDecodeArgs* args, const DB
     if (launch_backward(p, stream) != cudaSuccess) return DBS_CUDA_STATUS_LAUNCH_FAILED;
     p.grad = grad_inputs;
     if (launch_logit_correction(p, in->logits_type, in->logits, in->row_lse, stream) != cudaSuccess) {
+        return DBS_CUDA_STATUS_LAUNCH_FAILED;
+    }
+    return finish(stream, nullptr);
+}
+
+DBS_CUDA_EXPORT int dbs_cuda_backward_dense(const DBSCudaDecodeArgs* args, const DBSCudaBackwardInputs* in,
+                                            void* grad_inputs, int grad_type, void* workspace, int64_t workspace_bytes,
+                                            void* stream_ptr) {
+    if (!valid_args(args) || !in || !grad_inputs || !valid_dtype(grad_type)) return DBS_CUDA_STATUS_INVALID_ARGUMENT;
+    if (!in->parents || !in->tokens || !in->lengths || !in->from_logprob) return DBS_CUDA_STATUS_INVALID_ARGUMENT;
+    if (in->reserved0 != 0 || in->reserved[0] || in->reserved[1] || in->reserved[2] || in->reserved[3]) {
+        return DBS_CUDA_STATUS_INVALID_ARGUMENT;
+    }
+    if (in->logits && (!in->row_lse || !valid_dtype(in->logits_type))) return DBS_CUDA_STATUS_INVALID_ARGUMENT;
+    cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+    const DBSCudaDecodeArgs& a = *args;
+    BackwardParams p = backward_params(a);
+    p.parents = in->parents;
+    p.tokens = in->tokens;
+    p.lengths = in->lengths;
+    p.from_logprob = in->from_logprob;
+    p.g_final = in->grad_final_scores;
+    p.g_final_raw = in->grad_final_raw_scores;
+    p.g_scores = in->grad_scores;
+    p.g_raw = in->grad_raw_scores;
+    Scratch ws(workspace, workspace_bytes, backward_ws_bytes(a), stream);
+    if (ws.status() != DBS_CUDA_STATUS_OK) return ws.status();
+    p.draws = ws.at<float>(0);
+    const size_t slots = static_cast<size_t>(a.batch_size) * a.steps * a.beam_size;
+    if (cudaMemsetAsync(p.draws, 0, slots * sizeof(float), stream) != cudaSuccess) return DBS_CUDA_STATUS_LAUNCH_FAILED;
+    if (launch_backward(p, stream) != cudaSuccess) return DBS_CUDA_STATUS_LAUNCH_FAILED;
+    const int vec = (reinterpret_cast<uintptr_t>(grad_inputs) % 16 == 0) &&
+                    (!in->logits || reinterpret_cast<uintptr_t>(in->logits) % 16 == 0);
+    const int64_t rows = static_cast<int64_t>(slots);
+    const int64_t grid = std::min<int64_t>(rows, static_cast<int64_t>(sm_count_of_current_device()) * 8);
+    if (grid > 0 && launch_dense_grad(p, in->logits_type, in->logits, in->row_lse, grad_type, grad_inputs, vec,
+                                      static_cast<unsigned>(grid), stream) != cudaSuccess) {
+        return DBS_CUDA_STATUS_LAUNCH_FAILED;
+    }
+    return finish(stream, nullptr);
+}
+
+DBS_CUDA_EXPORT int dbs_cuda_advance_prefixes(int batch_size, int beam_size, int step, int prefix_stride,
+                                              const int32_t* parents, const int32_t* tokens,
+                                              const uint8_t* from_logprob, const int32_t* prefixes_in,
+                                              int32_t* prefixes_out, const float* raw_scores, const uint8_t* finished,
+                                              uint8_t* any_live, void* stream_ptr) {
+    if (batch_size < 1 || beam_size < 1 || beam_size > DBS_CUDA_MAX_BEAM || step < 0 || prefix_stride <= step) {
+        return DBS_CUDA_STATUS_INVALID_ARGUMENT;
+    }
+    if (!parents || !tokens || !from_logprob || !prefixes_out || (step > 0 && !prefixes_in)) {
+        return DBS_CUDA_STATUS_INVALID_ARGUMENT;
+    }
+    if (any_live && (!raw_scores || !finished)) return DBS_CUDA_STATUS_INVALID_ARGUMENT;
+    if (prefixes_in == prefixes_out && step > 0) return DBS_CUDA_STATUS_INVALID_ARGUMENT;
+    cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+    if (launch_advance_prefixes(batch_size, beam_size, step, prefix_stride, parents, tokens, from_logprob, prefixes_in,
+                                prefixes_out, raw_scores, finished, any_live, sm_count_of_current_device(),
+                                stream) != cudaSuccess) {
         return DBS_CUDA_STATUS_LAUNCH_FAILED;
     }
     return finish(stream, nullptr);

@@ -15,6 +15,8 @@
 // starting from 0) and, when the slot consumed an input entry, to entry
 // (t, q, token). Every slot of a step has a distinct entry, so the dense
 // update needs no atomics and the result is deterministic.
+#include <cuda_bf16.h>
+
 #include "engine.cuh"
 
 namespace dbsb {
@@ -157,6 +159,177 @@ __global__ void __launch_bounds__(kThreads) logit_correction_kernel(const __grid
     }
 }
 
+// ---------------------------------------------------------------------------
+// Dense gradient in one write pass. Every element of grad[B, T, K, V] (element
+// type OT) is written exactly once with the value the reference produces by
+// zero-filling a float32 gradient, accumulating the backward into it and
+// casting it to the input dtype (python/beamgrad/_torch.py:270-289:
+// decode_backward(...).to(input_dtype)):
+//   log-prob rows: 0 + draw at the token of each child slot with a nonzero
+//                  draw, 0 elsewhere (src/decoder.cpp:546-663 scatter);
+//   logit rows:    0 + (g_v - softmax(x_v, lse) * S) for rows with a path
+//                  gradient (src/decoder.hpp:212-242), 0 for the others;
+// then rounded to nearest-even into OT. This replaces the zero-fill, the
+// read-modify-write of the correction and the cast pass: the gradient is
+// streamed to HBM once (16-byte stores that bypass L2 retention), and logit
+// rows are read once.
+//
+// A CTA takes rows r = (b*T + t)*K + q in a grid-stride loop. The children of
+// row r are the slots of step t whose parent is q and whose draw is nonzero
+// (draws are written only for slots that consumed an input entry); they are
+// sorted by token (slot breaks ties) so the logit sum S runs in token order.
+// ---------------------------------------------------------------------------
+template <int OT>
+struct OutElem;
+template <>
+struct OutElem<0> {
+    using T = float;
+    __device__ static __forceinline__ float cvt(float v) { return v; }
+};
+template <>
+struct OutElem<1> {
+    using T = __half;
+    __device__ static __forceinline__ __half cvt(float v) { return __float2half_rn(v); }
+};
+template <>
+struct OutElem<2> {
+    using T = __nv_bfloat16;
+    __device__ static __forceinline__ __nv_bfloat16 cvt(float v) { return __float2bfloat16_rn(v); }
+};
+
+template <int IT, int OT, bool LOGITS>
+__global__ void __launch_bounds__(kThreads) dense_grad_kernel(const __grid_constant__ BackwardParams p,
+                                                              const void* __restrict__ logits,
+                                                              const float* __restrict__ row_lse, void* __restrict__ out,
+                                                              int vec) {
+    using OutT = typename OutElem<OT>::T;
+    constexpr int kChunk = 16 / static_cast<int>(sizeof(OutT));  // elements per 16-byte store
+    __shared__ int32_t tok_s[DBS_CUDA_MAX_BEAM];
+    __shared__ float val_s[DBS_CUDA_MAX_BEAM];
+    __shared__ int32_t slot_s[DBS_CUDA_MAX_BEAM];
+    __shared__ int32_t stok_s[DBS_CUDA_MAX_BEAM];
+    __shared__ float sval_s[DBS_CUDA_MAX_BEAM];
+    __shared__ int n_s;
+    __shared__ float sum_s;
+    const int tid = threadIdx.x;
+    const int K = p.K;
+    const int64_t V = p.V;
+    const int64_t rows = static_cast<int64_t>(p.B) * p.T * K;
+    OutT* grad = static_cast<OutT*>(out);
+    for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
+        const int q = static_cast<int>(r % K);
+        const int64_t bt = r / K;
+        const int b = static_cast<int>(bt / p.T);
+        const int t = static_cast<int>(bt - static_cast<int64_t>(b) * p.T);
+        int steps = p.steps_pe ? p.steps_pe[b] : p.T;
+        int Kb = p.beams_pe ? p.beams_pe[b] : K;
+        steps = steps < 0 ? 0 : (steps > p.T ? p.T : steps);
+        Kb = Kb < 0 ? 0 : (Kb > K ? K : Kb);
+        const bool active = t < steps && q < Kb;
+        if (tid == 0) n_s = 0;
+        block_sync();
+        if (active) {
+            const int64_t base = bt * K;
+            for (int k = tid; k < Kb; k += kThreads) {
+                const float d = p.draws[base + k];
+                if (d != 0.0f && p.parents[base + k] == q) {
+                    const int i = atomicAdd(&n_s, 1);
+                    tok_s[i] = p.tokens[base + k];
+                    val_s[i] = d;
+                    slot_s[i] = k;
+                }
+            }
+        }
+        block_sync();
+        const int n = n_s;
+        if (n > 0) {
+            // Rank sort by (token, slot): the keys are distinct.
+            for (int i = tid; i < n; i += kThreads) {
+                const int32_t ti = tok_s[i], si = slot_s[i];
+                int rank = 0;
+                for (int j = 0; j < n; ++j) rank += (tok_s[j] < ti) || (tok_s[j] == ti && slot_s[j] < si);
+                stok_s[rank] = ti;
+                sval_s[rank] = val_s[i];
+            }
+            block_sync();
+            if (LOGITS && tid == 0) {
+                float s = 0.0f;
+                for (int i = 0; i < n; ++i) s = __fadd_rn(s, sval_s[i]);
+                sum_s = s;
+            }
+            block_sync();
+        }
+        const float S = LOGITS && n > 0 ? sum_s : 0.0f;
+        const float lse = LOGITS && n > 0 ? row_lse[r] : 0.0f;
+        const int64_t off = r * V;
+        // Value of element v of this row (before the cast).
+        auto value = [&](int64_t v, float x, int& e) -> float {
+            // e: index of the first sorted entry with token >= v (advanced by the caller's scan).
+            float gv = 0.0f;
+            while (e < n && stok_s[e] < v) ++e;
+            bool hit = false;
+            while (e < n && stok_s[e] == v) {
+                gv = __fadd_rn(gv, sval_s[e]);
+                hit = true;
+                ++e;
+            }
+            if (LOGITS) {
+                if (n == 0) return 0.0f;
+                return __fadd_rn(0.0f, __fsub_rn(gv, __fmul_rn(softmax_probability(x, lse), S)));
+            }
+            return hit ? __fadd_rn(0.0f, gv) : 0.0f;
+        };
+        auto lower = [&](int64_t v) -> int {
+            int lo = 0, hi = n;
+            while (lo < hi) {
+                const int mid = (lo + hi) >> 1;
+                if (stok_s[mid] < v) lo = mid + 1;
+                else hi = mid;
+            }
+            return lo;
+        };
+        const bool need_x = LOGITS && n > 0;
+        int64_t head = V;
+        if (vec) {
+            const int64_t mis = off % kChunk;
+            head = mis == 0 ? 0 : kChunk - mis;
+            if (head > V) head = V;
+        }
+        const int64_t nchunks = (V - head) / kChunk;
+        const int64_t body_end = head + nchunks * kChunk;
+        // Scalar head [0, head) and tail [body_end, V).
+        const int64_t scalar_count = head + (V - body_end);
+        for (int64_t i = tid; i < scalar_count; i += kThreads) {
+            const int64_t v = i < head ? i : body_end + (i - head);
+            int e = n > 0 ? lower(v) : 0;
+            const float x = need_x ? load_elem<IT>(logits, off + v) : 0.0f;
+            grad[off + v] = OutElem<OT>::cvt(value(v, x, e));
+        }
+        // 16-byte body.
+        for (int64_t c = tid; c < nchunks; c += kThreads) {
+            const int64_t v0 = head + c * kChunk;
+            float xs[kChunk];
+            if (need_x) {
+#pragma unroll
+                for (int j = 0; j < kChunk; ++j) xs[j] = load_elem<IT>(logits, off + v0 + j);
+            }
+            int e = n > 0 ? lower(v0) : 0;
+            union {
+                uint4 u;
+                OutT h[kChunk];
+            } pk;
+            if (n == 0) {
+                pk.u = make_uint4(0u, 0u, 0u, 0u);
+            } else {
+#pragma unroll
+                for (int j = 0; j < kChunk; ++j) pk.h[j] = OutElem<OT>::cvt(value(v0 + j, need_x ? xs[j] : 0.0f, e));
+            }
+            __stcs(reinterpret_cast<uint4*>(grad + off + v0), pk.u);
+        }
+        block_sync();  // the row's shared lists are rewritten by the next row
+    }
+}
+
 __global__ void length_penalty_kernel(const int32_t* __restrict__ lengths, int64_t count, float alpha,
                                       float* __restrict__ out) {
     const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
@@ -205,6 +378,33 @@ cudaError_t launch_logit_correction(const BackwardParams& p, int dtype, const vo
         default: logit_correction_kernel<0><<<grid, kThreads, 0, stream>>>(p, logits, row_lse); break;
     }
     return cudaGetLastError();
+}
+
+template <int IT, bool LOGITS>
+cudaError_t launch_dense_out(const BackwardParams& p, int out_type, const void* logits, const float* row_lse,
+                             void* grad, int vec, unsigned grid, cudaStream_t stream) {
+    switch (out_type) {
+        case DBS_CUDA_DTYPE_F16:
+            dense_grad_kernel<IT, 1, LOGITS><<<grid, kThreads, 0, stream>>>(p, logits, row_lse, grad, vec);
+            break;
+        case DBS_CUDA_DTYPE_BF16:
+            dense_grad_kernel<IT, 2, LOGITS><<<grid, kThreads, 0, stream>>>(p, logits, row_lse, grad, vec);
+            break;
+        default: dense_grad_kernel<IT, 0, LOGITS><<<grid, kThreads, 0, stream>>>(p, logits, row_lse, grad, vec); break;
+    }
+    return cudaGetLastError();
+}
+
+// grid: CTAs of the row loop (the caller sizes it to the SM count); vec: 1 when
+// grad and logits start on 16-byte boundaries (16-byte body stores and loads).
+cudaError_t launch_dense_grad(const BackwardParams& p, int in_type, const void* logits, const float* row_lse,
+                              int out_type, void* grad, int vec, unsigned grid, cudaStream_t stream) {
+    if (!logits) return launch_dense_out<0, false>(p, out_type, nullptr, nullptr, grad, vec, grid, stream);
+    switch (in_type) {
+        case DBS_CUDA_DTYPE_F16: return launch_dense_out<1, true>(p, out_type, logits, row_lse, grad, vec, grid, stream);
+        case DBS_CUDA_DTYPE_BF16: return launch_dense_out<2, true>(p, out_type, logits, row_lse, grad, vec, grid, stream);
+        default: return launch_dense_out<0, true>(p, out_type, logits, row_lse, grad, vec, grid, stream);
+    }
 }
 
 cudaError_t launch_length_penalty(const int32_t* lengths, int64_t count, float alpha, float* out, cudaStream_t stream) {

@@ -27,6 +27,7 @@
 #include <vector>
 
 #include "dbs_cuda.h"
+#include "dbs_cuda_b200.h"
 
 namespace {
 
@@ -340,10 +341,18 @@ Tensor op_final_scores_backward(const Tensor& grad_final, const Tensor& parents,
     const Tensor g = final_grad_checked(grad_final, tr);
     const OptTensor steps_i32 = steps_on_device(steps, tr.parents.device(), tr.B, tr.T);
     const DBSCudaDecodeArgs args = problem(tr.B, tr.T, tr.K, vocab_size, -1, 0, length_penalty_alpha, steps_i32);
-    Tensor grad = torch::zeros({tr.B, tr.T, tr.K, vocab_size}, g.options());
-    raise_on(dbs_cuda_backward(&args, tr.parents.data_ptr<int32_t>(), tr.tokens.data_ptr<int32_t>(),
-                               tr.lengths.data_ptr<int32_t>(), tr.from_logprob.data_ptr<uint8_t>(), g.data_ptr<float>(),
-                               grad.data_ptr<float>(), nullptr, 0, current_stream()),
+    // One write pass (dbs_cuda_backward_dense) instead of a zero-fill plus the scatter.
+    DBSCudaBackwardInputs in{};
+    in.parents = tr.parents.data_ptr<int32_t>();
+    in.tokens = tr.tokens.data_ptr<int32_t>();
+    in.lengths = tr.lengths.data_ptr<int32_t>();
+    in.from_logprob = tr.from_logprob.data_ptr<uint8_t>();
+    in.grad_final_scores = g.data_ptr<float>();
+    Tensor grad = torch::empty({tr.B, tr.T, tr.K, vocab_size}, g.options());
+    const int64_t ws_bytes = dbs_cuda_backward_workspace_size(&args);
+    const Tensor ws = scratch(ws_bytes, tr.parents);
+    raise_on(dbs_cuda_backward_dense(&args, &in, grad.data_ptr(), DBS_CUDA_DTYPE_F32, ws.data_ptr(), ws_bytes,
+                                     current_stream()),
              "backward");
     return grad;
 }
@@ -374,11 +383,14 @@ const float* score_grad(const OptTensor& g, c10::IntArrayRef shape, const c10::D
     return keep.data_ptr<float>();
 }
 
-Tensor op_decode_backward(const OptTensor& grad_final_scores, const OptTensor& grad_final_raw_scores,
-                          const OptTensor& grad_scores, const OptTensor& grad_raw_scores, const Tensor& parents,
-                          const Tensor& tokens, const Tensor& lengths, const Tensor& from_logprob,
-                          const OptTensor& steps, int64_t vocab_size, double length_penalty_alpha,
-                          const OptTensor& logits, const OptTensor& row_lse) {
+// The dense input gradient of a decode in `out_type`, written in one pass by
+// dbs_cuda_backward_dense: identical to zero-filling a float32 gradient,
+// accumulating the backward into it and casting the result to out_type.
+Tensor decode_backward_impl(const OptTensor& grad_final_scores, const OptTensor& grad_final_raw_scores,
+                            const OptTensor& grad_scores, const OptTensor& grad_raw_scores, const Tensor& parents,
+                            const Tensor& tokens, const Tensor& lengths, const Tensor& from_logprob,
+                            const OptTensor& steps, int64_t vocab_size, double length_penalty_alpha,
+                            const OptTensor& logits, const OptTensor& row_lse, c10::ScalarType out_type) {
     const TraceIn tr(parents, tokens, lengths, from_logprob, "decode_backward");
     const c10::cuda::CUDAGuard guard(tr.parents.device());
     const c10::Device device = tr.parents.device();
@@ -410,17 +422,38 @@ Tensor op_decode_backward(const OptTensor& grad_final_scores, const OptTensor& g
     }
     const OptTensor steps_i32 = steps_on_device(steps, device, tr.B, tr.T);
     const DBSCudaDecodeArgs args = problem(tr.B, tr.T, tr.K, vocab_size, -1, 0, length_penalty_alpha, steps_i32);
-    Tensor grad = torch::zeros({tr.B, tr.T, tr.K, vocab_size}, tr.parents.options().dtype(torch::kFloat32));
-    Tensor ws;
-    int64_t ws_bytes = 0;
-    if (in.logits) {
-        ws_bytes = dbs_cuda_backward_workspace_size(&args);
-        ws = scratch(ws_bytes, tr.parents);
-    }
-    raise_on(dbs_cuda_backward_ex(&args, &in, grad.data_ptr<float>(), in.logits ? ws.data_ptr() : nullptr, ws_bytes,
-                                  current_stream()),
+    int grad_type = DBS_CUDA_DTYPE_F32;
+    if (out_type == torch::kFloat16) grad_type = DBS_CUDA_DTYPE_F16;
+    else if (out_type == torch::kBFloat16) grad_type = DBS_CUDA_DTYPE_BF16;
+    else TORCH_CHECK_VALUE(out_type == torch::kFloat32, "the gradient dtype must be float32, float16 or bfloat16");
+    Tensor grad = torch::empty({tr.B, tr.T, tr.K, vocab_size}, tr.parents.options().dtype(out_type));
+    const int64_t ws_bytes = dbs_cuda_backward_workspace_size(&args);
+    const Tensor ws = scratch(ws_bytes, tr.parents);
+    raise_on(dbs_cuda_backward_dense(&args, &in, grad.data_ptr(), grad_type, ws.data_ptr(), ws_bytes, current_stream()),
              "backward");
     return grad;
+}
+
+Tensor op_decode_backward(const OptTensor& grad_final_scores, const OptTensor& grad_final_raw_scores,
+                          const OptTensor& grad_scores, const OptTensor& grad_raw_scores, const Tensor& parents,
+                          const Tensor& tokens, const Tensor& lengths, const Tensor& from_logprob,
+                          const OptTensor& steps, int64_t vocab_size, double length_penalty_alpha,
+                          const OptTensor& logits, const OptTensor& row_lse) {
+    return decode_backward_impl(grad_final_scores, grad_final_raw_scores, grad_scores, grad_raw_scores, parents, tokens,
+                                lengths, from_logprob, steps, vocab_size, length_penalty_alpha, logits, row_lse,
+                                torch::kFloat32);
+}
+
+// beamgrad_b200::decode_backward_as: decode_backward with the gradient written
+// directly in `dtype` (the input's dtype in autograd), replacing
+// decode_backward(...).to(dtype) (python/beamgrad/_torch.py:289 of beamgrad 2.3.0).
+Tensor op_decode_backward_as(const OptTensor& grad_final_scores, const OptTensor& grad_final_raw_scores,
+                             const OptTensor& grad_scores, const OptTensor& grad_raw_scores, const Tensor& parents,
+                             const Tensor& tokens, const Tensor& lengths, const Tensor& from_logprob,
+                             const OptTensor& steps, int64_t vocab_size, double length_penalty_alpha,
+                             const OptTensor& logits, const OptTensor& row_lse, c10::ScalarType dtype) {
+    return decode_backward_impl(grad_final_scores, grad_final_raw_scores, grad_scores, grad_raw_scores, parents, tokens,
+                                lengths, from_logprob, steps, vocab_size, length_penalty_alpha, logits, row_lse, dtype);
 }
 
 Tensor op_length_penalty(const Tensor& lengths, double alpha) {
@@ -447,6 +480,15 @@ TORCH_LIBRARY_IMPL(beamgrad, CUDA, m) {
     m.impl("decode_backward", &op_decode_backward);
     m.impl("length_penalty", &op_length_penalty);
 }
+
+// Operators this engine adds (no counterpart in beamgrad).
+TORCH_LIBRARY(beamgrad_b200, m) {
+    m.def("decode_backward_as(Tensor? grad_final_scores, Tensor? grad_final_raw_scores, Tensor? grad_scores, "
+          "Tensor? grad_raw_scores, Tensor parents, Tensor tokens, Tensor lengths, Tensor from_logprob, Tensor? steps, "
+          "int vocab_size, float length_penalty_alpha, Tensor? logits, Tensor? row_lse, ScalarType dtype) -> Tensor");
+}
+
+TORCH_LIBRARY_IMPL(beamgrad_b200, CUDA, m) { m.impl("decode_backward_as", &op_decode_backward_as); }
 
 namespace {
 

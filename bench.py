@@ -3,7 +3,7 @@
 bf16 logits [B=64, T=128, K=8, V=32000] = N(0, 2) + Zipf(s=1.1) per-token bias, from_logits,
 eos=2, length-penalty alpha=1.0 -- decoded through the engine's C ABI (dbs_cuda_decode_ex2).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload c2|c5]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload c2|c4|c5]
 
 One JSON line on rank 0. `value` is whole-job candidates/s (B*T*K*V per decode, all ranks)
 with inputs resident in HBM; `e2e` is the same metric through the same C-ABI call with the
@@ -11,6 +11,10 @@ inputs in pinned host memory, copied in and the outputs copied out inside the ti
 Under torchrun each rank decodes its own batch of the config (weak scaling, no collective on
 the data path). `--impl reference` times the reference's own CPU implementation (libdbs,
 oracle/_ref/libdbs.so) with every host thread on the same config.
+
+`--workload c4` benchmarks BASELINE configs C4: bf16 log-probs [256,256,4,50257] with variable steps,
+the decode plus the dense bf16 input gradient of a minimum-risk loss (dbs_cuda_backward_dense), per GPU
+(weak scaling under torchrun).
 
 `--workload c5` benchmarks BASELINE configs C5 instead: fp32 logits [16,32,64,256000] of the
 same recipe, eos=1, alpha=0.6, the vocabulary lane-interleaved over the N ranks
@@ -55,9 +59,9 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--batch", type=int, default=64, help="examples per GPU (C2: 64); smaller only for profiling")
     ap.add_argument("--seq", type=int, default=128, help="decode steps T (C2: 128); smaller only for profiling")
-    ap.add_argument("--workload", default="c2", choices=["c2", "c5"])
+    ap.add_argument("--workload", default="c2", choices=["c2", "c4", "c5"])
     args = ap.parse_args()
-    if args.workload == "c5":
+    if args.workload in ("c4", "c5"):
         return args
     global B, T
     B, T = args.batch, args.seq
@@ -216,6 +220,289 @@ def run_reference_arm(args, rank: int, world: int):
                          "sample": f"full workload ({B} examples) per step, libdbs dbs_decode_batch_into_ex"},
         "e2e": {"value": value, "unit": "candidates/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }), flush=True)
+
+
+# ---------------------------------------------------------------------------- C4
+C4 = (256, 256, 4, 50257)
+C4_EOS, C4_ALPHA = 50256, 0.0
+
+
+def c4_workload() -> str:
+    B4, T4, K4, V4 = C4
+    return (f"C4: bf16 log-probs [{B4},{T4},{K4},{V4}] = log_softmax(N(0,2)+Zipf(1.1) bias), steps per example "
+            f"U{{16..{T4}}}, eos={C4_EOS}, alpha={C4_ALPHA}; decode + dense input gradient (bf16) of the mean "
+            f"minimum-risk loss, costs U[0,1]")
+
+
+def c4_inputs(torch, seed: int, device, n: int | None = None):
+    """The first n examples (all by default) of the C4 input: bf16 [n, T, K, V], steps [n] int32,
+    costs [n, K] float32."""
+    B4, T4, K4, V4 = C4
+    n = B4 if n is None else n
+    g = torch.Generator(device=device).manual_seed(seed)
+    bias = -1.1 * torch.log(torch.randperm(V4, generator=g, device=device).float() + 1.0)
+    steps = torch.randint(16, T4 + 1, (B4,), generator=g, device=device, dtype=torch.int32)[:n].contiguous()
+    costs = torch.rand((B4, K4), generator=g, device=device)[:n].contiguous()
+    x = torch.empty((n, T4, K4, V4), dtype=torch.bfloat16, device=device)
+    for b in range(n):
+        x[b] = torch.log_softmax(torch.randn((T4, K4, V4), generator=g, device=device) * 2.0 + bias, -1).to(x.dtype)
+    return x, steps, costs
+
+
+def minimum_risk_grad(torch, final_scores, costs):
+    """d/d final_scores of mean_b sum_k softmax(final_scores[b])_k * costs[b, k] over live beams
+    (python/beamgrad/losses.py:139-169 of beamgrad 2.3.0, temperature 1), and the loss."""
+    live = torch.isfinite(final_scores)
+    any_live = live.any(-1, keepdim=True)
+    logits = torch.where(live, final_scores, float("-inf"))
+    logits = torch.where(any_live, logits, torch.zeros_like(logits))
+    p = torch.softmax(logits, -1)
+    c = torch.where(live, costs, 0.0)
+    expected = (p * c).sum(-1, keepdim=True)
+    B = final_scores.shape[0]
+    g = torch.where(any_live, p * (c - expected) / B, 0.0)
+    return g.contiguous(), (expected[:, 0] * any_live[:, 0]).mean()
+
+
+def c4_cpu_reference(torch, threads: int, n_examples: int = 8):
+    """The reference CPU library (libdbs: dbs_decode_batch_into_ex, then dbs_backward_batch_into_ex into a
+    zeroed float32 gradient) on the first n_examples of C4; candidates/s and the sample."""
+    from oracle import oracle
+    from beamgrad_b200 import _abi as A
+
+    B4, T4, K4, V4 = C4
+    x, steps, costs = c4_inputs(torch, 4000, "cuda" if torch.cuda.is_available() else "cpu", n_examples)
+    bits = x.view(torch.int16).cpu().numpy().view(np.uint16)
+    steps_h = steps.cpu().numpy()
+    costs_t = costs.cpu()
+    del x
+    pb = oracle.Problem(bits, dtype=A.DTYPE_BF16, from_logits=False, eos=C4_EOS, alpha=C4_ALPHA, steps=steps_h)
+    times = []
+    with oracle.RefDecoder(pb) as d:
+        for _ in range(3):
+            t0 = time.perf_counter()
+            trace = d.decode(threads=threads)
+            g, _ = minimum_risk_grad(torch, torch.from_numpy(trace["final_scores"]), costs_t)
+            d.backward(trace, {"final_scores": g.numpy()}, threads=threads)
+            times.append(time.perf_counter() - t0)
+    sec = statistics.median(times)
+    return (n_examples * T4 * K4 * V4 / sec,
+            f"{n_examples} of the {B4} examples of C4 (decode + dense float32 backward), median of 3 runs")
+
+
+def run_c4(args, rank: int, world: int, local: int):
+    import torch
+
+    from oracle import oracle
+
+    B4, T4, K4, V4 = C4
+    cand = B4 * T4 * K4 * V4
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        if not oracle.ref_available():
+            print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/libdbs.so was not built"}))
+            return
+        threads = oracle.cpu_count()
+        per = []
+        for i in range(args.warmup + args.steps):
+            value, sample = c4_cpu_reference(torch, threads, n_examples=2)
+            if i >= args.warmup:
+                per.append(value)
+        value = statistics.median(per)
+        print(json.dumps({
+            "impl": "reference", "metric": METRIC, "value": value, "unit": "candidates/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": cand / value * 1e3, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": c4_workload(), "global_batch": B4, "seq_len": T4, "beam": K4, "vocab": V4,
+                       "parallelism": "host threads"},
+            "cpu_baseline": {"value": value, "unit": "candidates/s", "cores": threads, "kind": "reference",
+                             "sample": sample},
+            "e2e": {"value": value, "unit": "candidates/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        }), flush=True)
+        return
+
+    from beamgrad_b200 import _abi as A
+
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+    lib = A.load()
+    dev = torch.device("cuda", local)
+    x, steps, costs = c4_inputs(torch, 4000 + rank, dev)
+    f32, i32, u8 = torch.float32, torch.int32, torch.uint8
+    out = {
+        "final_scores": torch.empty((B4, K4), dtype=f32, device=dev),
+        "final_raw_scores": torch.empty((B4, K4), dtype=f32, device=dev),
+        "final_lengths": torch.empty((B4, K4), dtype=i32, device=dev),
+        "tokens": torch.empty((B4, T4, K4), dtype=i32, device=dev),
+        "parents": torch.empty((B4, T4, K4), dtype=i32, device=dev),
+        "lengths": torch.empty((B4, T4, K4), dtype=i32, device=dev),
+        "scores": torch.empty((B4, T4, K4), dtype=f32, device=dev),
+        "raw_scores": torch.empty((B4, T4, K4), dtype=f32, device=dev),
+        "from_logprob": torch.empty((B4, T4, K4), dtype=u8, device=dev),
+        "invalid_input": torch.empty((B4,), dtype=u8, device=dev),
+    }
+    o = A.DecodeOutputs()
+    for k, v in out.items():
+        setattr(o, k, v.data_ptr())
+    a = A.DecodeArgs()
+    a.batch_size, a.steps, a.beam_size, a.vocab_size = B4, T4, K4, V4
+    a.eos_token, a.length_penalty_alpha, a.repetition_penalty = C4_EOS, C4_ALPHA, 1.0
+    a.steps_per_example = steps.data_ptr()
+    ws_bytes = max(lib.dbs_cuda_decode_workspace_size(C.byref(a)), lib.dbs_cuda_backward_workspace_size(C.byref(a)))
+    ws = torch.empty(ws_bytes, dtype=u8, device=dev)
+    grad = torch.empty((B4, T4, K4, V4), dtype=torch.bfloat16, device=dev)
+    bi = A.BackwardInputs()
+    bi.parents, bi.tokens = out["parents"].data_ptr(), out["tokens"].data_ptr()
+    bi.lengths, bi.from_logprob = out["lengths"].data_ptr(), out["from_logprob"].data_ptr()
+    stream = torch.cuda.current_stream(dev)
+    sp = C.c_void_p(stream.cuda_stream)
+    loss_h = torch.empty((), dtype=f32, pin_memory=True)
+
+    def step(inp, ev=None):
+        if ev:
+            ev[0].record(stream)
+        A.check(lib.dbs_cuda_decode_ex2(C.c_void_p(inp.data_ptr()), A.DTYPE_BF16, 0, C.byref(a), None, C.byref(o),
+                                        None, C.c_void_p(ws.data_ptr()), ws_bytes, sp), "decode")
+        g, loss = minimum_risk_grad(torch, out["final_scores"], costs)
+        bi.grad_final_scores = g.data_ptr()
+        if ev:
+            ev[1].record(stream)
+        A.check(lib.dbs_cuda_backward_dense(C.byref(a), C.byref(bi), C.c_void_p(grad.data_ptr()), A.DTYPE_BF16,
+                                            C.c_void_p(ws.data_ptr()), ws_bytes, sp), "backward")
+        if ev:
+            ev[2].record(stream)
+        return g, loss
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+
+    for _ in range(args.warmup):
+        step(x)
+    barrier()
+    try:
+        gpu_id = f"GPU-{torch.cuda.get_device_properties(dev).uuid}"
+    except (AttributeError, RuntimeError):
+        gpu_id = str(local)
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    evs = []
+    with ClockSampler(gpu_id) as clocks:
+        barrier()
+        clocks.start()
+        start.record(stream)
+        for _ in range(args.steps):
+            ev = tuple(torch.cuda.Event(enable_timing=True) for _ in range(3))
+            step(x, ev)
+            evs.append(ev)
+        stop.record(stream)
+        barrier()
+        clocks.stop()
+        if clocks.proc is not None and not clocks.in_window():
+            clocks.extended = True
+            deadline = time.monotonic() + 2.0
+            while not clocks.in_window() and time.monotonic() < deadline:
+                step(x)
+                torch.cuda.synchronize(dev)
+                clocks.stop()
+    elapsed = start.elapsed_time(stop) / 1e3
+    t_all = torch.tensor([elapsed], device=dev, dtype=torch.float64)
+    if dist is not None:
+        dist.all_reduce(t_all, op=dist.ReduceOp.MAX)
+    elapsed = float(t_all.item())
+    fwd_s = statistics.mean(e[0].elapsed_time(e[1]) for e in evs) / 1e3
+    bwd_s = statistics.mean(e[1].elapsed_time(e[2]) for e in evs) / 1e3
+
+    host = {k: v.cpu().numpy() for k, v in out.items()}
+    live = ((host["parents"][:, :-1] >= 0) & (host["from_logprob"][:, :-1] == 1) &
+            (host["tokens"][:, :-1] != C4_EOS) & np.isfinite(host["raw_scores"][:, :-1]))
+    n_rows = int(B4 + live.sum())
+    slots = B4 * T4 * K4
+    fwd_bytes = n_rows * V4 * 2 + slots * (4 * 5 + 1) + B4 * K4 * 12
+    bwd_bytes = slots * V4 * 2 + slots * (4 * 4 + 1)  # gradient written once; trace + draws read
+    peak, peak_kind = peaks()
+    fwd_gbs, bwd_gbs = fwd_bytes / fwd_s / 1e9, bwd_bytes / bwd_s / 1e9
+    dominant = ("dbs_cuda_backward_dense (backward_kernel + dense_grad_kernel)", bwd_bytes, bwd_gbs) \
+        if bwd_s >= fwd_s else ("dbs_cuda_decode_ex2 (decode_chain_kernel)", fwd_bytes, fwd_gbs)
+
+    # End to end: the input from pinned host memory, the decode + backward, the loss back to the host
+    # (the gradient stays on the device, where the model's backward consumes it).
+    e2e = None
+    if not args.no_e2e:
+        xh = torch.empty(x.shape, dtype=x.dtype, pin_memory=True)
+        xh.copy_(x)
+        xd = torch.empty_like(x)
+        n_e2e = max(2, min(args.steps, 3))
+
+        def e2e_step():
+            xd.copy_(xh, non_blocking=True)
+            _, loss = step(xd)
+            loss_h.copy_(loss, non_blocking=True)
+
+        e2e_step()
+        barrier()
+        s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s0.record(stream)
+        for _ in range(n_e2e):
+            e2e_step()
+        s1.record(stream)
+        barrier()
+        e2e_t = torch.tensor([s0.elapsed_time(s1) / 1e3 / n_e2e], device=dev, dtype=torch.float64)
+        if dist is not None:
+            dist.all_reduce(e2e_t, op=dist.ReduceOp.MAX)
+        e2e = {"value": world * cand / float(e2e_t.item()), "unit": "candidates/s",
+               "h2d_bytes_per_step": xh.numel() * xh.element_size(), "d2h_bytes_per_step": 4}
+        del xh, xd
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and oracle.ref_available():
+        threads = oracle.cpu_count()
+        value, sample = c4_cpu_reference(torch, threads)
+        cpu = {"value": value, "unit": "candidates/s", "cores": threads, "kind": "reference", "sample": sample}
+
+    if dist is not None:
+        dist.barrier()
+    if rank == 0:
+        line = {
+            "metric": METRIC,
+            "value": world * cand / elapsed * args.steps,
+            "unit": "candidates/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": elapsed / args.steps * 1e3,
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "bf16",
+            "data": "synthetic",
+            "config": {"workload": c4_workload(), "global_batch": world * B4, "seq_len": T4, "beam": K4,
+                       "vocab": V4, "parallelism": f"batch x{world}" if world > 1 else "single GPU",
+                       "candidates": "nominal B*T_max*K*V per step",
+                       "l2": f"inputs ({x.numel() * 2 / 1e9:.1f} GB per GPU) larger than L2 (126 MB)",
+                       "stage_ms": {"decode_and_loss": round(fwd_s * 1e3, 4), "backward_dense": round(bwd_s * 1e3, 4)},
+                       "rows_read": n_rows},
+            "roofline": {"bound": "hbm", "achieved": dominant[2], "peak": peak, "unit": "GB/s",
+                         "frac": dominant[2] / peak, "traffic": None, "peak_kind": peak_kind, "kernel": dominant[0],
+                         "alg_bytes_per_launch": dominant[1]},
+            "roofline_stages": {"decode": {"achieved": fwd_gbs, "frac": fwd_gbs / peak, "alg_bytes": fwd_bytes},
+                                "backward_dense": {"achieved": bwd_gbs, "frac": bwd_gbs / peak,
+                                                   "alg_bytes": bwd_bytes}},
+            "cpu_baseline": cpu,
+            "e2e": e2e,
+            "gpu_launches": args.steps * 4,
+            "clocks": clocks.summary(),
+        }
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.destroy_process_group()
 
 
 # ---------------------------------------------------------------------------- C5
@@ -441,6 +728,8 @@ def main():
     local = int(os.environ.get("LOCAL_RANK", "0"))
     if args.workload == "c5":
         return run_c5(args, rank, world, local)
+    if args.workload == "c4":
+        return run_c4(args, rank, world, local)
     if args.impl == "reference":
         return run_reference_arm(args, rank, world)
 

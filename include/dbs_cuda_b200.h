@@ -27,6 +27,44 @@ DBS_CUDA_EXPORT int dbs_cuda_b200_abi_version(void);
 DBS_CUDA_EXPORT int dbs_cuda_backtrack(const DBSCudaDecodeArgs* args, const int32_t* tokens, const int32_t* parents,
                                        int64_t* sequences, void* stream);
 
+/* The dense input gradient of a decode in one pass, overwriting grad_inputs
+ * [B, T, K, V] (element type grad_type: DBS_CUDA_DTYPE_F32 / F16 / BF16). Its
+ * value is what beamgrad's autograd produces from dbs_cuda_backward_ex into a
+ * zero-filled float32 buffer followed by a cast to grad_type
+ * (python/beamgrad/_torch.py:270-289 of beamgrad 2.3.0: decode_backward(...)
+ * .to(input_dtype); python/csrc/cuda_ops.cpp:455 zero-fills), bit for bit:
+ * rows of log-probabilities get their slots' path gradients at the chosen
+ * tokens and zeros elsewhere; rows decoded from logits (in->logits and
+ * in->row_lse set) get g_v - softmax(x_v) * S where a path gradient reaches
+ * them, zeros elsewhere; rows past an example's steps or beams are zero.
+ * Arguments and errors as dbs_cuda_backward_ex, plus grad_type; workspace as
+ * dbs_cuda_backward_workspace_size(args) (NULL: stream-ordered allocation).
+ * Every element is written once: no caller zero-fill, no accumulation. */
+DBS_CUDA_EXPORT int dbs_cuda_backward_dense(const DBSCudaDecodeArgs* args, const DBSCudaBackwardInputs* in,
+                                            void* grad_inputs, int grad_type, void* workspace, int64_t workspace_bytes,
+                                            void* stream);
+
+/* One step of the token prefixes of a caller-driven search, on the device.
+ * After dbs_cuda_decode_step* wrote step `step`'s [B, K] parents, tokens and
+ * from_logprob, writes prefixes_out [B, K, prefix_stride] int32:
+ *   entries j < step: prefixes_in[b, parents[b, k], j]; entry step: the
+ *   token when from_logprob[b, k], else -1; the row is -1 for parent < 0
+ *   (or >= K). Entries past `step` are left as they are.
+ * This is beamgrad's per-step torch gather + cat + where of the sequences
+ * (python/beamgrad/_search.py:450-455 of beamgrad 2.3.0) as one kernel, so the
+ * prefixes the next step reads (DBSCudaBeamState.prefixes) never leave the
+ * device. prefixes_in and prefixes_out must not overlap (ping-pong two
+ * buffers); prefixes_in may be NULL at step 0. When any_live is set, the
+ * kernel also stores 1 there if some beam of the state after the step
+ * (raw_scores, finished: the DBSCudaBeamState arrays) has a finite raw score
+ * and is not finished (python/beamgrad/_search.py:366-368); it never stores 0,
+ * so the caller zeroes the byte beforehand. No host synchronisation. */
+DBS_CUDA_EXPORT int dbs_cuda_advance_prefixes(int batch_size, int beam_size, int step, int prefix_stride,
+                                              const int32_t* parents, const int32_t* tokens,
+                                              const uint8_t* from_logprob, const int32_t* prefixes_in,
+                                              int32_t* prefixes_out, const float* raw_scores, const uint8_t* finished,
+                                              uint8_t* any_live, void* stream);
+
 /* Bytes of the fixed device array behind dbs_cuda_decode_no_alloc (4 MiB). */
 #define DBS_CUDA_B200_NO_ALLOC_SCRATCH_BYTES (4 * 1024 * 1024)
 

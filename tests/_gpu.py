@@ -126,7 +126,9 @@ def engine_step(pb: Problem, raw, lengths, finished, prefixes) -> dict[str, np.n
 
 
 def engine_backward(pb: Problem, trace: dict[str, np.ndarray], grads: dict, logits=None, row_lse=None,
-                    use_workspace: bool = True) -> np.ndarray:
+                    use_workspace: bool = True, dense: int | None = None, misalign: int = 0):
+    """dbs_cuda_backward_ex into a zeroed float32 gradient, or (dense = a DTYPE_*)
+    dbs_cuda_backward_dense writing the gradient in that type (a torch tensor for 16-bit types)."""
     lib = A.load()
     dp = DeviceProblem(pb)
     B, T, K, V = pb.shape
@@ -142,17 +144,25 @@ def engine_backward(pb: Problem, trace: dict[str, np.ndarray], grads: dict, logi
     if logits is not None:
         lg, lse = dev(logits), dev(row_lse)
         bi.logits, bi.logits_type, bi.row_lse = ptr(lg), pb.dtype, ptr(lse)
-    grad = torch.zeros((B, T, K, V), dtype=torch.float32, device="cuda")
     args = dp.args()
     ws = None
     ws_bytes = 0
     if use_workspace:
         ws_bytes = lib.dbs_cuda_backward_workspace_size(C.byref(args))
         ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device="cuda")
-    rc = lib.dbs_cuda_backward_ex(C.byref(args), C.byref(bi), ptr(grad), ptr(ws), ws_bytes, stream_ptr())
+    if dense is None:
+        grad = torch.zeros((B, T, K, V), dtype=torch.float32, device="cuda")
+        rc = lib.dbs_cuda_backward_ex(C.byref(args), C.byref(bi), ptr(grad), ptr(ws), ws_bytes, stream_ptr())
+    else:
+        # dbs_cuda_backward_dense overwrites every element: start from a sentinel, optionally
+        # at an offset that is not 16-byte aligned (the scalar path).
+        tdt = {A.DTYPE_F32: torch.float32, A.DTYPE_F16: torch.float16, A.DTYPE_BF16: torch.bfloat16}[dense]
+        store = torch.full((B * T * K * V + misalign,), 77.0, dtype=tdt, device="cuda")
+        grad = store[misalign:].view(B, T, K, V)
+        rc = lib.dbs_cuda_backward_dense(C.byref(args), C.byref(bi), ptr(grad), dense, ptr(ws), ws_bytes, stream_ptr())
     A.check(rc, "backward")
     torch.cuda.synchronize()
-    return grad.cpu().numpy()
+    return grad.cpu().numpy() if dense in (None, A.DTYPE_F32) else grad.cpu()
 
 
 def engine_path_gradient(pb: Problem, trace, g_final) -> np.ndarray:

@@ -214,6 +214,56 @@ def test_backward_parity(seed):
     assert ours.tobytes() == ref.tobytes()
 
 
+@pytest.mark.parametrize("seed", range(12))
+def test_backward_dense_parity(seed):
+    """dbs_cuda_backward_dense == zero-filled float32 backward, cast to the output type, bit for bit."""
+    pb = random_case(2100 + seed, max_kv=40_000)
+    B, T, K, V = pb.shape
+    trace = oracle.oracle_decode(pb)
+    rng = np.random.default_rng(100 + seed)
+    grads = {"final_scores": rng.uniform(-1, 1, (B, K)).astype(np.float32)}
+    if seed % 2:
+        grads["scores"] = rng.uniform(-1, 1, (B, T, K)).astype(np.float32)
+        grads["final_raw_scores"] = rng.uniform(-1, 1, (B, K)).astype(np.float32)
+    logits = pb.x if pb.from_logits else None
+    lse = trace["row_lse"] if pb.from_logits else None
+    ref = oracle.oracle_backward(pb, trace, grads, logits=logits, row_lse=lse)
+    out_type = (A.DTYPE_F32, A.DTYPE_BF16, A.DTYPE_F16)[seed % 3]
+    misalign = (0, 1, 3)[(seed // 3) % 3]
+    ours = G.engine_backward(pb, trace, grads, logits=logits, row_lse=lse, use_workspace=seed % 4 != 3,
+                             dense=out_type, misalign=misalign)
+    if out_type == A.DTYPE_F32:
+        assert ours.tobytes() == ref.tobytes()
+    else:
+        want = torch.from_numpy(ref).to(torch.bfloat16 if out_type == A.DTYPE_BF16 else torch.float16)
+        assert ours.view(torch.int16).numpy().tobytes() == want.view(torch.int16).numpy().tobytes()
+
+
+def test_backward_dense_rejects_bad_arguments():
+    lib = A.load()
+    pb = make_problem(2, 3, 4, 50, seed=3)
+    trace = oracle.oracle_decode(pb)
+    dp = G.DeviceProblem(pb)
+    t = {k: G.dev(trace[k]) for k in ("parents", "tokens", "lengths", "from_logprob")}
+    bi = A.BackwardInputs()
+    bi.parents, bi.tokens, bi.lengths, bi.from_logprob = (G.ptr(t[k]) for k in ("parents", "tokens", "lengths",
+                                                                                  "from_logprob"))
+    grad = torch.empty((2, 3, 4, 50), dtype=torch.float32, device="cuda")
+    args = dp.args()
+    for gtype in (-1, 3, 7):
+        rc = lib.dbs_cuda_backward_dense(C.byref(args), C.byref(bi), G.ptr(grad), gtype, None, 0, G.stream_ptr())
+        assert rc == A.STATUS_INVALID_ARGUMENT
+    assert lib.dbs_cuda_backward_dense(C.byref(args), C.byref(bi), None, A.DTYPE_F32, None, 0,
+                                       G.stream_ptr()) == A.STATUS_INVALID_ARGUMENT
+    ws_bytes = lib.dbs_cuda_backward_workspace_size(C.byref(args))
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device="cuda")
+    assert lib.dbs_cuda_backward_dense(C.byref(args), C.byref(bi), G.ptr(grad), A.DTYPE_F32, G.ptr(ws), ws_bytes - 1,
+                                       G.stream_ptr()) != A.STATUS_OK
+    bi.logits, bi.logits_type = G.ptr(dp.x), A.DTYPE_F32  # logits without row_lse
+    assert lib.dbs_cuda_backward_dense(C.byref(args), C.byref(bi), G.ptr(grad), A.DTYPE_F32, None, 0,
+                                       G.stream_ptr()) == A.STATUS_INVALID_ARGUMENT
+
+
 def test_path_gradient_parity():
     for seed in range(8):
         pb = random_case(3000 + seed, max_kv=20_000)

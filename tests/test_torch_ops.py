@@ -175,6 +175,12 @@ def test_backward_operators_parity(from_logits):
     ref = oracle.oracle_backward(pb, trace, {"final_scores": g_final, "scores": g_scores},
                                  logits=pb.x if from_logits else None, row_lse=trace["row_lse"] if from_logits else None)
     same(grad, ref, "decode_backward")
+    # The added operator writes the gradient in the input's dtype: decode_backward(...).to(dtype), bit for bit.
+    for dt in (torch.bfloat16, torch.float16, torch.float32):
+        cast = torch.ops.beamgrad_b200.decode_backward_as(gf, None, torch.from_numpy(g_scores).cuda(), None, *args,
+                                                          logits, lse, dt)
+        assert cast.dtype == dt
+        assert torch.equal(cast.cpu().view(torch.uint8), torch.from_numpy(ref).to(dt).view(torch.uint8)), dt
 
 
 @pytest.mark.gpu
