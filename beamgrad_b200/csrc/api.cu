@@ -30,7 +30,7 @@ cudaError_t launch_backward(const BackwardParams& p, cudaStream_t stream);
 cudaError_t launch_logit_correction(const BackwardParams& p, int dtype, const void* logits, const float* row_lse,
                                     cudaStream_t stream);
 cudaError_t launch_dense_grad(const BackwardParams& p, int in_type, const void* logits, const float* row_lse,
-                              int out_type, void* grad, int vec, unsigned grid, cudaStream_t stream);
+                              int out_type, void* grad, int vec, int sm_count, cudaStream_t stream);
 cudaError_t launch_length_penalty(const int32_t* lengths, int64_t count, float alpha, float* out, cudaStream_t stream);
 // search.cu
 cudaError_t launch_advance_prefixes(int B, int K, int step, int stride, const int32_t* parents, const int32_t* tokens,
@@ -658,10 +658,8 @@ DBS_CUDA_EXPORT int dbs_cuda_backward_dense(const DBSCudaDecodeArgs* args, const
     if (launch_backward(p, stream) != cudaSuccess) return DBS_CUDA_STATUS_LAUNCH_FAILED;
     const int vec = (reinterpret_cast<uintptr_t>(grad_inputs) % 16 == 0) &&
                     (!in->logits || reinterpret_cast<uintptr_t>(in->logits) % 16 == 0);
-    const int64_t rows = static_cast<int64_t>(slots);
-    const int64_t grid = std::min<int64_t>(rows, static_cast<int64_t>(sm_count_of_current_device()) * 8);
-    if (grid > 0 && launch_dense_grad(p, in->logits_type, in->logits, in->row_lse, grad_type, grad_inputs, vec,
-                                      static_cast<unsigned>(grid), stream) != cudaSuccess) {
+    if (launch_dense_grad(p, in->logits_type, in->logits, in->row_lse, grad_type, grad_inputs, vec,
+                          sm_count_of_current_device(), stream) != cudaSuccess) {
         return DBS_CUDA_STATUS_LAUNCH_FAILED;
     }
     return finish(stream, nullptr);

@@ -17,6 +17,8 @@
 // update needs no atomics and the result is deterministic.
 #include <cuda_bf16.h>
 
+#include <algorithm>
+
 #include "engine.cuh"
 
 namespace dbsb {
@@ -170,9 +172,10 @@ __global__ void __launch_bounds__(kThreads) logit_correction_kernel(const __grid
 //   logit rows:    0 + (g_v - softmax(x_v, lse) * S) for rows with a path
 //                  gradient (src/decoder.hpp:212-242), 0 for the others;
 // then rounded to nearest-even into OT. This replaces the zero-fill, the
-// read-modify-write of the correction and the cast pass: the gradient is
-// streamed to HBM once (16-byte stores that bypass L2 retention), and logit
-// rows are read once.
+// read-modify-write of the correction and the cast pass. Rows decoded from
+// logits are written here once (16-byte stores that bypass L2 retention)
+// and read once; rows of log-probabilities are almost all zero and take the
+// memset + scatter_dense_kernel path instead (launch_dense_grad).
 //
 // A CTA takes rows r = (b*T + t)*K + q in a grid-stride loop. The children of
 // row r are the slots of step t whose parent is q and whose draw is nonzero
@@ -330,6 +333,38 @@ __global__ void __launch_bounds__(kThreads) dense_grad_kernel(const __grid_const
     }
 }
 
+// Rows of log-probabilities: after the gradient is zero-filled (a memset,
+// the fastest way to stream zeros to HBM), each slot with a nonzero draw
+// writes its entry (t, parent, token) = 0 + draw, rounded into OT. Slots of
+// one step that share (parent, token) are summed in slot order by the first
+// of them (from 0, as the dense kernel and the float32 accumulation do).
+template <int OT>
+__global__ void scatter_dense_kernel(const __grid_constant__ BackwardParams p, void* __restrict__ out) {
+    using OutT = typename OutElem<OT>::T;
+    OutT* grad = static_cast<OutT*>(out);
+    const int K = p.K;
+    const int64_t slots = static_cast<int64_t>(p.B) * p.T * K;
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < slots;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const float d = p.draws[i];
+        if (d == 0.0f) continue;  // draws are nonzero only for valid slots that consumed an entry
+        const int64_t bt = i / K;
+        const int k = static_cast<int>(i - bt * K);
+        const int64_t base = bt * K;
+        const int q = p.parents[i];
+        const int tok = p.tokens[i];
+        bool first = true;
+        for (int j = 0; j < k && first; ++j)
+            first = !(p.draws[base + j] != 0.0f && p.parents[base + j] == q && p.tokens[base + j] == tok);
+        if (!first) continue;
+        float g = __fadd_rn(0.0f, d);
+        for (int j = k + 1; j < K; ++j)
+            if (p.draws[base + j] != 0.0f && p.parents[base + j] == q && p.tokens[base + j] == tok)
+                g = __fadd_rn(g, p.draws[base + j]);
+        grad[(base + q) * static_cast<int64_t>(p.V) + tok] = OutElem<OT>::cvt(__fadd_rn(0.0f, g));
+    }
+}
+
 __global__ void length_penalty_kernel(const int32_t* __restrict__ lengths, int64_t count, float alpha,
                                       float* __restrict__ out) {
     const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
@@ -395,11 +430,29 @@ cudaError_t launch_dense_out(const BackwardParams& p, int out_type, const void* 
     return cudaGetLastError();
 }
 
-// grid: CTAs of the row loop (the caller sizes it to the SM count); vec: 1 when
-// grad and logits start on 16-byte boundaries (16-byte body stores and loads).
+// Log-prob rows: stream-ordered memset of the whole gradient, then the sparse
+// scatter. Logit rows: dense_grad_kernel writes every element once (grid =
+// 8 CTAs per SM); vec: 1 when grad and logits start on 16-byte boundaries.
 cudaError_t launch_dense_grad(const BackwardParams& p, int in_type, const void* logits, const float* row_lse,
-                              int out_type, void* grad, int vec, unsigned grid, cudaStream_t stream) {
-    if (!logits) return launch_dense_out<0, false>(p, out_type, nullptr, nullptr, grad, vec, grid, stream);
+                              int out_type, void* grad, int vec, int sm_count, cudaStream_t stream) {
+    const int64_t rows = static_cast<int64_t>(p.B) * p.T * p.K;
+    if (rows == 0) return cudaSuccess;
+    if (!logits) {
+        const size_t elem = out_type == DBS_CUDA_DTYPE_F32 ? 4 : 2;
+        const cudaError_t e = cudaMemsetAsync(grad, 0, static_cast<size_t>(rows) * static_cast<size_t>(p.V) * elem,
+                                              stream);
+        if (e != cudaSuccess) return e;
+        const int64_t want = (rows + 255) / 256;
+        const int64_t cap = static_cast<int64_t>(sm_count) * 8;
+        const unsigned blocks = static_cast<unsigned>(want < cap ? want : cap);
+        switch (out_type) {
+            case DBS_CUDA_DTYPE_F16: scatter_dense_kernel<1><<<blocks, 256, 0, stream>>>(p, grad); break;
+            case DBS_CUDA_DTYPE_BF16: scatter_dense_kernel<2><<<blocks, 256, 0, stream>>>(p, grad); break;
+            default: scatter_dense_kernel<0><<<blocks, 256, 0, stream>>>(p, grad); break;
+        }
+        return cudaGetLastError();
+    }
+    const unsigned grid = static_cast<unsigned>(std::min<int64_t>(rows, static_cast<int64_t>(sm_count) * 8));
     switch (in_type) {
         case DBS_CUDA_DTYPE_F16: return launch_dense_out<1, true>(p, out_type, logits, row_lse, grad, vec, grid, stream);
         case DBS_CUDA_DTYPE_BF16: return launch_dense_out<2, true>(p, out_type, logits, row_lse, grad, vec, grid, stream);

@@ -57,14 +57,17 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
-    ap.add_argument("--batch", type=int, default=64, help="examples per GPU (C2: 64); smaller only for profiling")
+    ap.add_argument("--batch", type=int, default=None,
+                    help="examples per GPU (C2: 64, C4: 256); smaller only for profiling")
     ap.add_argument("--seq", type=int, default=128, help="decode steps T (C2: 128); smaller only for profiling")
     ap.add_argument("--workload", default="c2", choices=["c2", "c4", "c5"])
     args = ap.parse_args()
+    global B, T, C4
+    if args.workload == "c4" and args.batch is not None:
+        C4 = (args.batch,) + C4[1:]
     if args.workload in ("c4", "c5"):
         return args
-    global B, T
-    B, T = args.batch, args.seq
+    B, T = args.batch if args.batch is not None else 64, args.seq
     return args
 
 
@@ -87,6 +90,22 @@ def peaks() -> tuple[float, str]:
         d = json.loads(p.read_text())
         return float(d["hbm_gbs"]), "measured"
     return 6650.0, "fallback"
+
+
+# Rounded FP32 operations per logit entry of the bit-exact logsumexp and scan: the Cephes
+# exp_nonpositive (22: range reduction, degree-5 polynomial, exponent insertion), the
+# subtraction of the row maximum and the lane add.
+FP32_OPS_PER_ENTRY = 24
+
+
+def fp32_roofline(entries: int, seconds: float, clocks: dict) -> dict:
+    """The FP32-issue bound of a from-logits decode: entries x ops per entry against one FP32
+    operation per lane per clock (148 SMs x 128 lanes) at the SM clock seen under load."""
+    mhz = clocks.get("sm_mhz") or clocks.get("sm_max_mhz") or 1965.0
+    peak = 148 * 128 * mhz * 1e6 / 1e12  # Tops/s
+    achieved = entries * FP32_OPS_PER_ENTRY / seconds / 1e12
+    return {"bound": "fp32_issue", "achieved": achieved, "peak": peak, "unit": "Tops/s", "frac": achieved / peak,
+            "ops_per_entry": FP32_OPS_PER_ENTRY, "entries": entries, "sm_mhz": mhz}
 
 
 class ClockSampler:
@@ -229,7 +248,8 @@ C4_EOS, C4_ALPHA = 50256, 0.0
 
 def c4_workload() -> str:
     B4, T4, K4, V4 = C4
-    return (f"C4: bf16 log-probs [{B4},{T4},{K4},{V4}] = log_softmax(N(0,2)+Zipf(1.1) bias), steps per example "
+    tag = "C4" if B4 == 256 else "C4-shaped (reduced batch, profiling only)"
+    return (f"{tag}: bf16 log-probs [{B4},{T4},{K4},{V4}] = log_softmax(N(0,2)+Zipf(1.1) bias), steps per example "
             f"U{{16..{T4}}}, eos={C4_EOS}, alpha={C4_ALPHA}; decode + dense input gradient (bf16) of the mean "
             f"minimum-risk loss, costs U[0,1]")
 
@@ -897,6 +917,7 @@ def main():
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": measured_traffic(), "peak_kind": peak_kind,
                          "alg_bytes_per_launch": alg_bytes, "rows_read": n_rows},
+            "roofline_fp32": fp32_roofline(n_rows * V, per_launch, clocks.summary()),
             "cpu_baseline": cpu,
             "e2e": e2e,
             "gpu_launches": 2 * args.steps,

@@ -239,6 +239,27 @@ def test_backward_dense_parity(seed):
         assert ours.view(torch.int16).numpy().tobytes() == want.view(torch.int16).numpy().tobytes()
 
 
+@pytest.mark.parametrize("K", [1, 31, 32, 33])
+@pytest.mark.parametrize("from_logits", [False, True])
+def test_backward_dense_warp_and_block_paths(K, from_logits):
+    """Beams <= 32 take the warp-per-row writer, larger beams the CTA-per-row one."""
+    pb = make_problem(3, 5, K, 257, dtype=A.DTYPE_BF16 if from_logits else A.DTYPE_F32, from_logits=from_logits,
+                      seed=60 + K, eos=2, alpha=0.6, variable_steps=True)
+    B, T, K, V = pb.shape
+    trace = oracle.oracle_decode(pb)
+    rng = np.random.default_rng(K)
+    grads = {"final_scores": rng.uniform(-1, 1, (B, K)).astype(np.float32),
+             "scores": rng.uniform(-1, 1, (B, T, K)).astype(np.float32)}
+    logits = pb.x if from_logits else None
+    lse = trace["row_lse"] if from_logits else None
+    ref = oracle.oracle_backward(pb, trace, grads, logits=logits, row_lse=lse)
+    for out_type, tdt in ((A.DTYPE_F32, torch.float32), (A.DTYPE_BF16, torch.bfloat16), (A.DTYPE_F16, torch.float16)):
+        ours = G.engine_backward(pb, trace, grads, logits=logits, row_lse=lse, dense=out_type)
+        want = torch.from_numpy(ref).to(tdt)
+        got = torch.from_numpy(ours) if out_type == A.DTYPE_F32 else ours
+        assert torch.equal(got.view(torch.uint8), want.view(torch.uint8)), (K, out_type)
+
+
 def test_backward_dense_rejects_bad_arguments():
     lib = A.load()
     pb = make_problem(2, 3, 4, 50, seed=3)
