@@ -310,6 +310,30 @@ def c4_cpu_reference(torch, threads: int, n_examples: int = 8):
             f"{n_examples} of the {B4} examples of C4 (decode + dense float32 backward), median of 3 runs")
 
 
+def write_ceiling(torch, buf, stream, reps: int = 5) -> float | None:
+    """GB/s of cudaMemsetAsync over `buf` on this GPU: the speed of a pure write stream, which
+    the copy-based HBM peak understates (a copy also reads)."""
+    try:
+        cudart = C.CDLL("libcudart.so.12")  # the runtime the engine library already loaded
+    except OSError:
+        return None
+    nbytes = buf.numel() * buf.element_size()
+    fn = cudart.cudaMemsetAsync
+    fn.argtypes = [C.c_void_p, C.c_int, C.c_size_t, C.c_void_p]
+    fn.restype = C.c_int
+    sp = C.c_void_p(stream.cuda_stream)
+    for _ in range(2):
+        if fn(C.c_void_p(buf.data_ptr()), 0, nbytes, sp) != 0:
+            return None
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(reps):
+        fn(C.c_void_p(buf.data_ptr()), 0, nbytes, sp)
+    e1.record(stream)
+    e1.synchronize()
+    return nbytes * reps / (e0.elapsed_time(e1) / 1e3) / 1e9
+
+
 def run_c4(args, rank: int, world: int, local: int):
     import torch
 
@@ -440,6 +464,8 @@ def run_c4(args, rank: int, world: int, local: int):
     fwd_s = statistics.mean(e[0].elapsed_time(e[1]) for e in evs) / 1e3
     bwd_s = statistics.mean(e[1].elapsed_time(e[2]) for e in evs) / 1e3
 
+    write_gbs = write_ceiling(torch, grad, stream)
+
     host = {k: v.cpu().numpy() for k, v in out.items()}
     live = ((host["parents"][:, :-1] >= 0) & (host["from_logprob"][:, :-1] == 1) &
             (host["tokens"][:, :-1] != C4_EOS) & np.isfinite(host["raw_scores"][:, :-1]))
@@ -514,6 +540,8 @@ def run_c4(args, rank: int, world: int, local: int):
                          "alg_bytes_per_launch": dominant[1]},
             "roofline_stages": {"decode": {"achieved": fwd_gbs, "frac": fwd_gbs / peak, "alg_bytes": fwd_bytes},
                                 "backward_dense": {"achieved": bwd_gbs, "frac": bwd_gbs / peak,
+                                                   "write_stream_gbs": write_gbs,
+                                                   "frac_of_write_stream": bwd_gbs / write_gbs if write_gbs else None,
                                                    "alg_bytes": bwd_bytes}},
             "cpu_baseline": cpu,
             "e2e": e2e,
