@@ -2586,9 +2586,20 @@ __device__ uint32_t warp_row_record(const DecodeParams& p, WarpRowShared& ws, co
         if (v != skip) lane_top4(tv, ti, x, v);
     };
     if (lane < rs.head && lane < rs.n_ends()) single(rs.end_entry(lane));
+    // Warp-wide insertion threshold: the LIST-th largest of the lanes' best entries so
+    // far (lanes owning an EOS token excluded, as for the bound below) is LIST distinct
+    // eligible entries, so it never exceeds the row's final bound; entries below it are
+    // never candidates and need not enter the lane lists. Without it a warp takes the
+    // insertion branch whenever any one of its 32 lanes has a new top-4 entry.
+    float wthr = f_ninf();
+    auto raise_wthr = [&](int it) {
+        if (it < 2 || (it & 3) == 3)
+            wthr = fmaxf(wthr, __shfl_sync(0xffffffffu, warp_sort_desc(dirty ? f_ninf() : tv[0]), LIST - 1));
+    };
     if constexpr (E::kBytes == 2) {
         uint32_t mx2 = h2_ninf<DT>();
-        for (int c0 = lane; c0 < rs.nvec; c0 += UR * 32) {
+        for (int c00 = 0, it = 0; c00 < rs.nvec; c00 += UR * 32, ++it) {
+            const int c0 = c00 + lane;
             uint4 q[UR];
 #pragma unroll
             for (int u = 0; u < UR; ++u) {
@@ -2599,21 +2610,29 @@ __device__ uint32_t warp_row_record(const DecodeParams& p, WarpRowShared& ws, co
             for (int u = 0; u < UR; ++u) {
                 const int c = c0 + u * 32;
                 if (c < rs.nvec) {
-                    mx2 = h2_max_nan<DT>(mx2, h2_max_nan<DT>(h2_max_nan<DT>(q[u].x, q[u].y), h2_max_nan<DT>(q[u].z, q[u].w)));
-                    const uint32_t m2 = h2_max<DT>(h2_max<DT>(q[u].x, q[u].y), h2_max<DT>(q[u].z, q[u].w));
-                    if (fmaxf(h2_lo<DT>(m2), h2_hi<DT>(m2)) > tv[3]) {
+                    // One NaN-propagating chunk maximum serves both the row maximum and
+                    // the top-4 test: a row holding NaN or +inf discards the lane lists
+                    // (it takes the full-scan fallback), so a chunk skipped because a NaN
+                    // hid its maximum never matters.
+                    const uint32_t m2 = h2_max_nan<DT>(h2_max_nan<DT>(q[u].x, q[u].y), h2_max_nan<DT>(q[u].z, q[u].w));
+                    mx2 = h2_max_nan<DT>(mx2, m2);
+                    const float cmax = fmaxf(h2_lo<DT>(m2), h2_hi<DT>(m2));
+                    if (cmax > tv[3] && cmax >= wthr) {
                         float x[PER];
                         unpack16<DT>(q[u], x);
 #pragma unroll
                         for (int e = 0; e < PER; ++e)
-                            if (rs.head + c * PER + e != skip) lane_top4(tv, ti, x[e], rs.head + c * PER + e);
+                            if (rs.head + c * PER + e != skip && x[e] >= wthr)
+                                lane_top4(tv, ti, x[e], rs.head + c * PER + e);
                     }
                 }
             }
+            raise_wthr(it);
         }
         mxn = max_nan(mxn, max_nan(h2_lo<DT>(mx2), h2_hi<DT>(mx2)));
     } else {
-        for (int c0 = lane; c0 < rs.nvec; c0 += UR * 32) {
+        for (int c00 = 0, it = 0; c00 < rs.nvec; c00 += UR * 32, ++it) {
+            const int c0 = c00 + lane;
             uint4 q[UR];
 #pragma unroll
             for (int u = 0; u < UR; ++u) {
@@ -2626,16 +2645,18 @@ __device__ uint32_t warp_row_record(const DecodeParams& p, WarpRowShared& ws, co
                 if (c < rs.nvec) {
                     const float a = __uint_as_float(q[u].x), b = __uint_as_float(q[u].y);
                     const float d = __uint_as_float(q[u].z), e = __uint_as_float(q[u].w);
-                    mxn = max_nan(mxn, max_nan(max_nan(a, b), max_nan(d, e)));
-                    if (fmaxf(fmaxf(a, b), fmaxf(d, e)) > tv[3]) {
+                    const float cm = max_nan(max_nan(a, b), max_nan(d, e));  // as above
+                    mxn = max_nan(mxn, cm);
+                    if (cm > tv[3] && cm >= wthr) {
                         const int base = rs.head + c * 4;
-                        if (base != skip) lane_top4(tv, ti, a, base);
-                        if (base + 1 != skip) lane_top4(tv, ti, b, base + 1);
-                        if (base + 2 != skip) lane_top4(tv, ti, d, base + 2);
-                        if (base + 3 != skip) lane_top4(tv, ti, e, base + 3);
+                        if (base != skip && a >= wthr) lane_top4(tv, ti, a, base);
+                        if (base + 1 != skip && b >= wthr) lane_top4(tv, ti, b, base + 1);
+                        if (base + 2 != skip && d >= wthr) lane_top4(tv, ti, d, base + 2);
+                        if (base + 3 != skip && e >= wthr) lane_top4(tv, ti, e, base + 3);
                     }
                 }
             }
+            raise_wthr(it);
         }
     }
     if (lane >= rs.head && lane < rs.n_ends()) single(rs.end_entry(lane));
