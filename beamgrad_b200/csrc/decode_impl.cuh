@@ -2592,6 +2592,19 @@ __device__ uint32_t warp_row_record(const DecodeParams& p, WarpRowShared& ws, co
     // never candidates and need not enter the lane lists. Without it a warp takes the
     // insertion branch whenever any one of its 32 lanes has a new top-4 entry.
     float wthr = f_ninf();
+    // Lane 0 keeps a bulk L2 prefetch PD iterations (PD * UR * 512 bytes) ahead of the
+    // warp's loads: more bytes in flight per SM than the registers of UR loads allow.
+    constexpr int PD = 4;
+    constexpr uint32_t kIterBytes = UR * 32 * 16;
+    const uint32_t body_bytes = static_cast<uint32_t>(rs.nvec) * 16u;
+    if (lane == 0 && body_bytes > 0) prefetch_l2_bulk(body, body_bytes < PD * kIterBytes ? body_bytes : PD * kIterBytes);
+    auto prefetch_ahead = [&](int c00) {
+        const uint32_t ahead = static_cast<uint32_t>(c00) * 16u + PD * kIterBytes;
+        if (lane == 0 && ahead < body_bytes) {
+            const uint32_t n = body_bytes - ahead;
+            prefetch_l2_bulk(body + ahead, n < kIterBytes ? n : kIterBytes);
+        }
+    };
     auto raise_wthr = [&](int it) {
         if (it < 2 || (it & 3) == 3)
             wthr = fmaxf(wthr, __shfl_sync(0xffffffffu, warp_sort_desc(dirty ? f_ninf() : tv[0]), LIST - 1));
@@ -2600,6 +2613,7 @@ __device__ uint32_t warp_row_record(const DecodeParams& p, WarpRowShared& ws, co
         uint32_t mx2 = h2_ninf<DT>();
         for (int c00 = 0, it = 0; c00 < rs.nvec; c00 += UR * 32, ++it) {
             const int c0 = c00 + lane;
+            prefetch_ahead(c00);
             uint4 q[UR];
 #pragma unroll
             for (int u = 0; u < UR; ++u) {
@@ -2633,6 +2647,7 @@ __device__ uint32_t warp_row_record(const DecodeParams& p, WarpRowShared& ws, co
     } else {
         for (int c00 = 0, it = 0; c00 < rs.nvec; c00 += UR * 32, ++it) {
             const int c0 = c00 + lane;
+            prefetch_ahead(c00);
             uint4 q[UR];
 #pragma unroll
             for (int u = 0; u < UR; ++u) {

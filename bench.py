@@ -475,8 +475,9 @@ def run_c4(args, rank: int, world: int, local: int):
     bwd_bytes = slots * V4 * 2 + slots * (4 * 4 + 1)  # gradient written once; trace + draws read
     peak, peak_kind = peaks()
     fwd_gbs, bwd_gbs = fwd_bytes / fwd_s / 1e9, bwd_bytes / bwd_s / 1e9
-    dominant = ("dbs_cuda_backward_dense (backward_kernel + dense_grad_kernel)", bwd_bytes, bwd_gbs) \
-        if bwd_s >= fwd_s else ("dbs_cuda_decode_ex2 (decode_chain_kernel)", fwd_bytes, fwd_gbs)
+    dominant = ("dbs_cuda_backward_dense (gradient memset + backward_kernel + scatter_dense_kernel)", bwd_bytes,
+                bwd_gbs) \
+        if bwd_s >= fwd_s else ("dbs_cuda_decode_ex2 (decode_chain_warp_kernel)", fwd_bytes, fwd_gbs)
 
     # End to end: the input from pinned host memory, the decode + backward, the loss back to the host
     # (the gradient stays on the device, where the model's backward consumes it).
