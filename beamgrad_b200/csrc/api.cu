@@ -32,6 +32,8 @@ cudaError_t launch_logit_correction(const BackwardParams& p, int dtype, const vo
 cudaError_t launch_dense_grad(const BackwardParams& p, int in_type, const void* logits, const float* row_lse,
                               int out_type, void* grad, int vec, int sm_count, cudaStream_t stream);
 cudaError_t launch_length_penalty(const int32_t* lengths, int64_t count, float alpha, float* out, cudaStream_t stream);
+cudaError_t launch_selected_weights(int64_t rows, int K, const float* scores, float temperature, float* out,
+                                    cudaStream_t stream);
 // search.cu
 cudaError_t launch_advance_prefixes(int B, int K, int step, int stride, const int32_t* parents, const int32_t* tokens,
                                     const uint8_t* from_logprob, const int32_t* in, int32_t* out, const float* raw,
@@ -630,9 +632,11 @@ DBS_CUDA_EXPORT int dbs_cuda_backward_ex(const DBSCudaDecodeArgs* args, const DB
     return finish(stream, nullptr);
 }
 
-DBS_CUDA_EXPORT int dbs_cuda_backward_dense(const DBSCudaDecodeArgs* args, const DBSCudaBackwardInputs* in,
-                                            void* grad_inputs, int grad_type, void* workspace, int64_t workspace_bytes,
-                                            void* stream_ptr) {
+// The dense gradient of dbs_cuda_backward_dense, with the selected-beam weights term when
+// w_sel / g_wsel are given.
+static int backward_dense(const DBSCudaDecodeArgs* args, const DBSCudaBackwardInputs* in, const float* w_sel,
+                          const float* g_wsel, float sel_temp, void* grad_inputs, int grad_type, void* workspace,
+                          int64_t workspace_bytes, void* stream_ptr) {
     if (!valid_args(args) || !in || !grad_inputs || !valid_dtype(grad_type)) return DBS_CUDA_STATUS_INVALID_ARGUMENT;
     if (!in->parents || !in->tokens || !in->lengths || !in->from_logprob) return DBS_CUDA_STATUS_INVALID_ARGUMENT;
     if (in->reserved0 != 0 || in->reserved[0] || in->reserved[1] || in->reserved[2] || in->reserved[3]) {
@@ -650,6 +654,9 @@ DBS_CUDA_EXPORT int dbs_cuda_backward_dense(const DBSCudaDecodeArgs* args, const
     p.g_final_raw = in->grad_final_raw_scores;
     p.g_scores = in->grad_scores;
     p.g_raw = in->grad_raw_scores;
+    p.w_sel = w_sel;
+    p.g_wsel = g_wsel;
+    p.sel_temp = sel_temp;
     Scratch ws(workspace, workspace_bytes, backward_ws_bytes(a), stream);
     if (ws.status() != DBS_CUDA_STATUS_OK) return ws.status();
     p.draws = ws.at<float>(0);
@@ -660,6 +667,36 @@ DBS_CUDA_EXPORT int dbs_cuda_backward_dense(const DBSCudaDecodeArgs* args, const
                     (!in->logits || reinterpret_cast<uintptr_t>(in->logits) % 16 == 0);
     if (launch_dense_grad(p, in->logits_type, in->logits, in->row_lse, grad_type, grad_inputs, vec,
                           sm_count_of_current_device(), stream) != cudaSuccess) {
+        return DBS_CUDA_STATUS_LAUNCH_FAILED;
+    }
+    return finish(stream, nullptr);
+}
+
+DBS_CUDA_EXPORT int dbs_cuda_backward_dense(const DBSCudaDecodeArgs* args, const DBSCudaBackwardInputs* in,
+                                            void* grad_inputs, int grad_type, void* workspace, int64_t workspace_bytes,
+                                            void* stream) {
+    return backward_dense(args, in, nullptr, nullptr, 1.0f, grad_inputs, grad_type, workspace, workspace_bytes, stream);
+}
+
+DBS_CUDA_EXPORT int dbs_cuda_backward_selected(const DBSCudaDecodeArgs* args, const DBSCudaBackwardInputs* in,
+                                               const float* selected_weights, const float* grad_selected_weights,
+                                               float temperature, void* grad_inputs, int grad_type, void* workspace,
+                                               int64_t workspace_bytes, void* stream) {
+    if (!selected_weights || !grad_selected_weights || !std::isfinite(temperature) || !(temperature > 0.0f)) {
+        return DBS_CUDA_STATUS_INVALID_ARGUMENT;
+    }
+    return backward_dense(args, in, selected_weights, grad_selected_weights, temperature, grad_inputs, grad_type,
+                          workspace, workspace_bytes, stream);
+}
+
+DBS_CUDA_EXPORT int dbs_cuda_selected_weights(const DBSCudaDecodeArgs* args, const float* scores, float temperature,
+                                              float* weights, void* stream_ptr) {
+    if (!valid_args(args) || !scores || !weights || !std::isfinite(temperature) || !(temperature > 0.0f)) {
+        return DBS_CUDA_STATUS_INVALID_ARGUMENT;
+    }
+    cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+    const int64_t rows = static_cast<int64_t>(args->batch_size) * args->steps;
+    if (launch_selected_weights(rows, args->beam_size, scores, temperature, weights, stream) != cudaSuccess) {
         return DBS_CUDA_STATUS_LAUNCH_FAILED;
     }
     return finish(stream, nullptr);

@@ -38,11 +38,21 @@ __global__ void __launch_bounds__(kThreads) backward_kernel(const __grid_constan
     int Kb = p.beams_pe ? p.beams_pe[b] : K;
     steps = steps < 0 ? 0 : (steps > p.T ? p.T : steps);
     Kb = Kb < 0 ? 0 : (Kb > K ? K : Kb);
+    __shared__ float wdot_s;
     for (int k = tid; k < Kb; k += kThreads) next_g[k] = 0.0f;
     block_sync();
     for (int t = steps - 1; t >= 0; --t) {
         const bool last = t == steps - 1;
         const int64_t base = (static_cast<int64_t>(b) * p.T + t) * K;
+        if (p.g_wsel) {
+            // dot(w, gw) over the step's K slots in slot order (src/kernels_scalar.cpp:271-275).
+            if (tid == 0) {
+                float s = 0.0f;
+                for (int k = 0; k < K; ++k) s = __fadd_rn(s, __fmul_rn(p.w_sel[base + k], p.g_wsel[base + k]));
+                wdot_s = s;
+            }
+            block_sync();
+        }
         for (int k = tid; k < Kb; k += kThreads) {
             const int64_t slot = base + k;
             const int q = p.parents[slot];
@@ -50,6 +60,10 @@ __global__ void __launch_bounds__(kThreads) backward_kernel(const __grid_constan
             int pq = -1;
             if (q >= 0 && q < Kb) {
                 float drank = 0.0f;
+                // Selected-beam weights term first (src/decoder.cpp:599-604).
+                if (p.g_wsel)
+                    drank = __fadd_rn(drank, __fdiv_rn(__fmul_rn(p.w_sel[slot], __fsub_rn(p.g_wsel[slot], wdot_s)),
+                                                       p.sel_temp));
                 if (p.g_scores) drank = __fadd_rn(drank, p.g_scores[slot]);
                 if (last && p.g_final) drank = __fadd_rn(drank, p.g_final[static_cast<int64_t>(b) * K + k]);
                 const float inv = __fdiv_rn(1.0f, gnmt_penalty(p.lengths[slot], p.alpha));
@@ -363,6 +377,50 @@ __global__ void scatter_dense_kernel(const __grid_constant__ BackwardParams p, v
                 g = __fadd_rn(g, p.draws[base + j]);
         grad[(base + q) * static_cast<int64_t>(p.V) + tok] = OutElem<OT>::cvt(__fadd_rn(0.0f, g));
     }
+}
+
+// Selected-beam weights: softmax_selected (src/kernels_scalar.cpp:277-302) over each
+// step's K selected scores, one thread per (b, t) in slot order: scores above -1e30
+// take part; maxv = max of score / temperature; w = exp(score / temperature - maxv)
+// summed in slot order; w *= 1 / sum; all zero when no score takes part or the sum
+// is not a positive finite number.
+__global__ void selected_weights_kernel(int64_t rows, int K, const float* __restrict__ scores, float temperature,
+                                        float* __restrict__ out) {
+    const int64_t r = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (r >= rows) return;
+    const float guard = -1.0e30f;
+    const float* sc = scores + r * K;
+    float* o = out + r * K;
+    for (int k = 0; k < K; ++k) o[k] = 0.0f;
+    float maxv = f_ninf();
+    for (int k = 0; k < K; ++k) {
+        if (sc[k] > guard) {
+            const float q = __fdiv_rn(sc[k], temperature);
+            maxv = maxv < q ? q : maxv;
+        }
+    }
+    if (!(maxv > f_ninf() && maxv < f_inf())) return;
+    float sum = 0.0f;
+    for (int k = 0; k < K; ++k) {
+        if (sc[k] > guard) {
+            o[k] = exp_nonpositive(__fsub_rn(__fdiv_rn(sc[k], temperature), maxv));
+            sum = __fadd_rn(sum, o[k]);
+        }
+    }
+    if (!(sum > 0.0f) || !(sum < f_inf())) {
+        for (int k = 0; k < K; ++k) o[k] = 0.0f;
+        return;
+    }
+    const float inv = __fdiv_rn(1.0f, sum);
+    for (int k = 0; k < K; ++k) o[k] = __fmul_rn(o[k], inv);
+}
+
+cudaError_t launch_selected_weights(int64_t rows, int K, const float* scores, float temperature, float* out,
+                                    cudaStream_t stream) {
+    if (rows == 0) return cudaSuccess;
+    selected_weights_kernel<<<static_cast<unsigned>((rows + 127) / 128), 128, 0, stream>>>(rows, K, scores,
+                                                                                            temperature, out);
+    return cudaGetLastError();
 }
 
 __global__ void length_penalty_kernel(const int32_t* __restrict__ lengths, int64_t count, float alpha,

@@ -127,6 +127,9 @@ struct BackwardParams {
     const float* g_raw;
     float* grad;    // dense [B, T, K, V] (+=), or null
     float* draws;   // per slot [B, T, K], or null
+    const float* w_sel;   // selected-beam weights [B, T, K], or null
+    const float* g_wsel;  // their gradient [B, T, K], or null
+    float sel_temp;       // the weights' softmax temperature
 };
 
 __device__ __forceinline__ Meta load_meta(const DecodeParams& p, int b) {

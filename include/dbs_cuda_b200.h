@@ -44,6 +44,26 @@ DBS_CUDA_EXPORT int dbs_cuda_backward_dense(const DBSCudaDecodeArgs* args, const
                                             void* grad_inputs, int grad_type, void* workspace, int64_t workspace_bytes,
                                             void* stream);
 
+/* Selected-beam weights of a decode: for every step, softmax_selected over the K selected
+ * beams' scores (python/beamgrad estimators' "selected" surrogate; the reference computes them
+ * on the CPU only, src/decoder.cpp:344 and src/kernels_scalar.cpp:277-302): scores above -1e30
+ * take part, w = exp(score / T - max) / sum in slot order, all zero for a step without a
+ * finite score. scores / weights are [B, T, K] float32 (the decode's scores output); the
+ * temperature must be finite and positive. Bit-identical to the reference. */
+DBS_CUDA_EXPORT int dbs_cuda_selected_weights(const DBSCudaDecodeArgs* args, const float* scores, float temperature,
+                                              float* weights, void* stream);
+
+/* dbs_cuda_backward_dense plus the gradient that flows through the selected-beam weights:
+ * each slot with a parent adds (w_k * (gw_k - dot(w, gw))) / temperature to its score
+ * gradient before the other terms (src/decoder.cpp:599-604 of beamgrad 2.3.0, the
+ * grad_selected_weights of dbs_backward / dbs_backward_dense in include/dbs.h:440-455).
+ * selected_weights are dbs_cuda_selected_weights' output and grad_selected_weights their
+ * gradient, both [B, T, K] float32. */
+DBS_CUDA_EXPORT int dbs_cuda_backward_selected(const DBSCudaDecodeArgs* args, const DBSCudaBackwardInputs* in,
+                                               const float* selected_weights, const float* grad_selected_weights,
+                                               float temperature, void* grad_inputs, int grad_type, void* workspace,
+                                               int64_t workspace_bytes, void* stream);
+
 /* One step of the token prefixes of a caller-driven search, on the device.
  * After dbs_cuda_decode_step* wrote step `step`'s [B, K] parents, tokens and
  * from_logprob, writes prefixes_out [B, K, prefix_stride] int32:

@@ -631,8 +631,24 @@ static int cmp_entry(const void* x, const void* y) {
 }
 
 /* The path-gradient entries of example b (unsorted); returns their count. */
+/* Selected-beam weights term of drank (src/decoder.cpp:599-604): weights / grad_weights are
+ * the example's [T, K] rows, or NULL. */
+typedef struct {
+    const float* w;
+    const float* gw;
+    float temperature;
+} SelectedTerm;
+
+static int example_entries_sel(const DBSCudaDecodeArgs* a, int b, int steps, int beam,
+                               const DBSCudaBackwardInputs* in, const SelectedTerm* sel, Entry* entries);
+
 static int example_entries(const DBSCudaDecodeArgs* a, int b, int steps, int beam, const DBSCudaBackwardInputs* in,
                            Entry* entries) {
+    return example_entries_sel(a, b, steps, beam, in, NULL, entries);
+}
+
+static int example_entries_sel(const DBSCudaDecodeArgs* a, int b, int steps, int beam,
+                               const DBSCudaBackwardInputs* in, const SelectedTerm* sel, Entry* entries) {
     const int T = a->steps, K = a->beam_size, V = a->vocab_size;
     float* next = (float*)calloc(beam, sizeof(float));
     float* prev = (float*)calloc(beam, sizeof(float));
@@ -640,11 +656,21 @@ static int example_entries(const DBSCudaDecodeArgs* a, int b, int steps, int bea
     for (int t = steps - 1; t >= 0; --t) {
         for (int k = 0; k < beam; ++k) prev[k] = 0.0f;
         const int last = t == steps - 1;
+        const float* w = NULL;
+        const float* gw = NULL;
+        float weighted_dot = 0.0f;
+        if (sel && sel->gw) {
+            /* dot(w, gw, K) in slot order (src/kernels_scalar.cpp:271-275) */
+            w = sel->w + ((int64_t)b * T + t) * K;
+            gw = sel->gw + ((int64_t)b * T + t) * K;
+            for (int k = 0; k < K; ++k) weighted_dot += w[k] * gw[k];
+        }
         for (int k = 0; k < beam; ++k) {
             const int64_t idx = ((int64_t)b * T + t) * K + k;
             const int parent = in->parents[idx];
             if (parent < 0 || parent >= beam) continue;
             float drank = 0.0f;
+            if (gw) drank += (w[k] * (gw[k] - weighted_dot)) / sel->temperature;
             if (in->grad_scores) drank += in->grad_scores[idx];
             if (in->grad_final_scores && last) drank += in->grad_final_scores[(int64_t)b * K + k];
             const int l = in->lengths[idx] > 1 ? in->lengths[idx] : 1;
@@ -671,7 +697,56 @@ static int example_entries(const DBSCudaDecodeArgs* a, int b, int steps, int bea
     return n;
 }
 
+static int backward_sel(const DBSCudaDecodeArgs* a, const DBSCudaBackwardInputs* in, const SelectedTerm* sel,
+                        float* grad);
+
 int oracle_backward(const DBSCudaDecodeArgs* a, const DBSCudaBackwardInputs* in, float* grad) {
+    return backward_sel(a, in, NULL, grad);
+}
+
+int oracle_backward_selected(const DBSCudaDecodeArgs* a, const DBSCudaBackwardInputs* in, const float* weights,
+                             const float* grad_weights, float temperature, float* grad) {
+    if (!weights != !grad_weights || !(temperature > 0.0f)) return DBS_CUDA_STATUS_INVALID_ARGUMENT;
+    SelectedTerm sel = {weights, grad_weights, temperature};
+    return backward_sel(a, in, &sel, grad);
+}
+
+/* softmax_selected (src/kernels_scalar.cpp:277-302) over each step's K selected scores:
+ * weights [B, T, K] from the decode's scores [B, T, K]. */
+void oracle_selected_weights(const DBSCudaDecodeArgs* a, const float* scores, float temperature, float* weights) {
+    const float kNegGuard = -1.0e30f;
+    const int64_t rows = (int64_t)a->batch_size * a->steps;
+    const int K = a->beam_size;
+    for (int64_t r = 0; r < rows; ++r) {
+        const float* sc = scores + r * K;
+        float* out = weights + r * K;
+        for (int i = 0; i < K; ++i) out[i] = 0.0f;
+        float maxv = -INFINITY;
+        for (int i = 0; i < K; ++i) {
+            if (sc[i] > kNegGuard) {
+                const float q = sc[i] / temperature;
+                maxv = maxv < q ? q : maxv; /* std::max */
+            }
+        }
+        if (!isfinite(maxv)) continue;
+        float sum = 0.0f;
+        for (int i = 0; i < K; ++i) {
+            if (sc[i] > kNegGuard) {
+                out[i] = oracle_exp_nonpositive(sc[i] / temperature - maxv);
+                sum += out[i];
+            }
+        }
+        if (!(sum > 0.0f) || !isfinite(sum)) {
+            for (int i = 0; i < K; ++i) out[i] = 0.0f;
+            continue;
+        }
+        const float inv_sum = 1.0f / sum;
+        for (int i = 0; i < K; ++i) out[i] *= inv_sum;
+    }
+}
+
+static int backward_sel(const DBSCudaDecodeArgs* a, const DBSCudaBackwardInputs* in, const SelectedTerm* sel,
+                        float* grad) {
     if (!args_ok(a) || !in || !grad || !in->parents || !in->tokens || !in->lengths || !in->from_logprob) {
         return DBS_CUDA_STATUS_INVALID_ARGUMENT;
     }
@@ -686,7 +761,7 @@ int oracle_backward(const DBSCudaDecodeArgs* a, const DBSCudaBackwardInputs* in,
             steps = steps < 0 ? 0 : (steps > T ? T : steps);
             beam = beam < 0 ? 0 : (beam > K ? K : beam);
         }
-        const int n = example_entries(a, b, steps, beam, in, entries);
+        const int n = example_entries_sel(a, b, steps, beam, in, sel, entries);
         qsort(entries, (size_t)n, sizeof(Entry), cmp_entry);
         float* out = grad + (int64_t)b * T * K * V;
         if (!in->logits) {

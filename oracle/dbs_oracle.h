@@ -34,6 +34,11 @@ int oracle_decode_step(const void* inputs, int data_type, int from_logits, const
                        const DBSCudaDecodeOutputs* outputs, float* row_lse);
 
 int oracle_backward(const DBSCudaDecodeArgs* args, const DBSCudaBackwardInputs* inputs, float* grad_inputs);
+/* oracle_backward plus the selected-beam weights term (src/decoder.cpp:599-604). */
+int oracle_backward_selected(const DBSCudaDecodeArgs* args, const DBSCudaBackwardInputs* inputs, const float* weights,
+                             const float* grad_weights, float temperature, float* grad_inputs);
+/* softmax_selected (src/kernels_scalar.cpp:277-302) per step over the decode's scores [B, T, K]. */
+void oracle_selected_weights(const DBSCudaDecodeArgs* args, const float* scores, float temperature, float* weights);
 
 int oracle_path_gradient(const DBSCudaDecodeArgs* args, const int32_t* parents, const int32_t* tokens,
                          const int32_t* lengths, const uint8_t* from_logprob, const float* grad_final_scores,

@@ -164,6 +164,11 @@ def oracle_lib() -> C.CDLL:
         lib.oracle_lse_from_lanes.argtypes = [_p, C.c_float]
         lib.oracle_half_to_float.restype = C.c_float
         lib.oracle_half_to_float.argtypes = [C.c_uint16, C.c_int]
+        lib.oracle_backward_selected.restype = C.c_int
+        lib.oracle_backward_selected.argtypes = [C.POINTER(A.DecodeArgs), C.POINTER(A.BackwardInputs), _p, _p,
+                                                 C.c_float, _p]
+        lib.oracle_selected_weights.restype = None
+        lib.oracle_selected_weights.argtypes = [C.POINTER(A.DecodeArgs), _p, C.c_float, _p]
         _olib = lib
     return _olib
 
@@ -221,6 +226,45 @@ def oracle_backward(pb: Problem, trace: dict[str, np.ndarray], grads: dict[str, 
     rc = oracle_lib().oracle_backward(C.byref(pb.args()), C.byref(bi), _ptr(grad))
     if rc != 0:
         raise ValueError("oracle_backward: invalid argument")
+    return grad
+
+
+def _backward_inputs(pb: Problem, trace, grads, logits, row_lse) -> A.BackwardInputs:
+    bi = A.BackwardInputs()
+    bi.parents, bi.tokens = _ptr(trace["parents"]), _ptr(trace["tokens"])
+    bi.lengths, bi.from_logprob = _ptr(trace["lengths"]), _ptr(trace["from_logprob"])
+    bi.grad_final_scores = _ptr(grads.get("final_scores"))
+    bi.grad_final_raw_scores = _ptr(grads.get("final_raw_scores"))
+    bi.grad_scores = _ptr(grads.get("scores"))
+    bi.grad_raw_scores = _ptr(grads.get("raw_scores"))
+    if logits is not None:
+        bi.logits = _ptr(logits)
+        bi.logits_type = pb.dtype
+        bi.row_lse = _ptr(row_lse)
+    return bi
+
+
+def oracle_selected_weights(pb: Problem, scores: np.ndarray, temperature: float) -> np.ndarray:
+    """softmax_selected per step (src/kernels_scalar.cpp:277-302) of the decode's scores [B, T, K]."""
+    B, T, K, V = pb.shape
+    sc = np.ascontiguousarray(scores, np.float32)
+    w = np.empty((B, T, K), np.float32)
+    oracle_lib().oracle_selected_weights(C.byref(pb.args()), _ptr(sc), temperature, _ptr(w))
+    return w
+
+
+def oracle_backward_selected(pb: Problem, trace, grads, weights, grad_weights, temperature: float,
+                             logits=None, row_lse=None) -> np.ndarray:
+    """oracle_backward plus the selected-beam weights term (src/decoder.cpp:599-604)."""
+    B, T, K, V = pb.shape
+    grad = np.zeros((B, T, K, V), np.float32)
+    bi = _backward_inputs(pb, trace, grads, logits, row_lse)
+    w = np.ascontiguousarray(weights, np.float32)
+    gw = np.ascontiguousarray(grad_weights, np.float32)
+    rc = oracle_lib().oracle_backward_selected(C.byref(pb.args()), C.byref(bi), _ptr(w), _ptr(gw), temperature,
+                                               _ptr(grad))
+    if rc != 0:
+        raise ValueError("oracle_backward_selected: invalid argument")
     return grad
 
 
@@ -321,6 +365,22 @@ def ref_lib() -> C.CDLL:
         lib.dbs_backward_batch_into_ex.argtypes = [_p, C.POINTER(_BackwardC), C.c_int, _p]
         lib.dbs_last_global_error.restype = C.c_char_p
         lib.dbs_last_global_error.argtypes = []
+        # Single-example API (include/dbs.h:215-221, 448-455, 480-515): the only one that
+        # returns the selected-beam weights.
+        lib.dbs_decode.restype = C.c_int
+        lib.dbs_decode.argtypes = [_p, _p, C.c_int, C.c_int, C.POINTER(_p)]
+        lib.dbs_result_weights.restype = C.POINTER(C.c_float)
+        lib.dbs_result_weights.argtypes = [_p]
+        lib.dbs_backward_dense.restype = C.c_int
+        lib.dbs_backward_dense.argtypes = [_p, _p, _p, _p, _p, C.POINTER(_p)]
+        lib.dbs_backward_grad_log_probs.restype = C.POINTER(C.c_float)
+        lib.dbs_backward_grad_log_probs.argtypes = [_p]
+        lib.dbs_free_result.restype = None
+        lib.dbs_free_result.argtypes = [_p]
+        lib.dbs_free_backward.restype = None
+        lib.dbs_free_backward.argtypes = [_p]
+        lib.dbs_last_error.restype = C.c_char_p
+        lib.dbs_last_error.argtypes = [_p]
         _rlib = lib
     return _rlib
 
@@ -415,3 +475,37 @@ def cpu_count() -> int:
         return len(os.sched_getaffinity(0))
     except AttributeError:  # pragma: no cover
         return os.cpu_count() or 1
+
+
+def ref_selected(x: np.ndarray, beam: int, eos: int, alpha: float, min_length: int, temperature: float,
+                 grad_weights: np.ndarray, grad_final: np.ndarray) -> tuple[np.ndarray, np.ndarray]:
+    """The reference library's own selected-beam weights [T, K] and dense input gradient [T, K, V] of
+    one float32 log-prob example x [T, K, V] (dbs_decode, dbs_result_weights, dbs_backward_dense with
+    grad_selected_weights and grad_final_scores)."""
+    lib = ref_lib()
+    T, K, V = x.shape
+    o = _Options()
+    o.beam_size, o.eos_token, o.selected_temperature = beam, eos, temperature
+    o.length_penalty_alpha, o.min_length = alpha, min_length
+    o.max_dense_gradient_elements = T * K * V + 1
+    h = _p()
+    if lib.dbs_create_ex(o, C.byref(h)) != 0:
+        raise RuntimeError(lib.dbs_last_global_error().decode())
+    res, bw = _p(), _p()
+    try:
+        xc = np.ascontiguousarray(x, np.float32)
+        if lib.dbs_decode(h, _ptr(xc), T, V, C.byref(res)) != 0:
+            raise RuntimeError(lib.dbs_last_error(h).decode())
+        w = np.ctypeslib.as_array(lib.dbs_result_weights(res), shape=(T * K,)).reshape(T, K).copy()
+        gw = np.ascontiguousarray(grad_weights, np.float32)
+        gf = np.ascontiguousarray(grad_final, np.float32)
+        if lib.dbs_backward_dense(h, res, _ptr(gw), None, _ptr(gf), C.byref(bw)) != 0:
+            raise RuntimeError(lib.dbs_last_error(h).decode())
+        g = np.ctypeslib.as_array(lib.dbs_backward_grad_log_probs(bw), shape=(T * K * V,)).reshape(T, K, V).copy()
+    finally:
+        if bw:
+            lib.dbs_free_backward(bw)
+        if res:
+            lib.dbs_free_result(res)
+        lib.dbs_destroy(h)
+    return w, g

@@ -125,6 +125,45 @@ def engine_step(pb: Problem, raw, lengths, finished, prefixes) -> dict[str, np.n
     return out
 
 
+def engine_selected_weights(pb: Problem, scores: np.ndarray, temperature: float) -> np.ndarray:
+    lib = A.load()
+    dp = DeviceProblem(pb)
+    sc = dev(np.ascontiguousarray(scores, np.float32))
+    w = torch.full(sc.shape, 99.0, dtype=torch.float32, device="cuda")
+    A.check(lib.dbs_cuda_selected_weights(C.byref(dp.args()), ptr(sc), temperature, ptr(w), stream_ptr()),
+            "selected_weights")
+    torch.cuda.synchronize()
+    return w.cpu().numpy()
+
+
+def engine_backward_selected(pb: Problem, trace: dict[str, np.ndarray], grads: dict, weights, grad_weights,
+                             temperature: float, logits=None, row_lse=None) -> np.ndarray:
+    """dbs_cuda_backward_selected, float32 dense output."""
+    lib = A.load()
+    dp = DeviceProblem(pb)
+    B, T, K, V = pb.shape
+    t = {k: dev(trace[k]) for k in ("parents", "tokens", "lengths", "from_logprob")}
+    g = {k: dev(v) for k, v in grads.items() if v is not None}
+    bi = A.BackwardInputs()
+    bi.parents, bi.tokens, bi.lengths, bi.from_logprob = (ptr(t[k]) for k in ("parents", "tokens", "lengths", "from_logprob"))
+    bi.grad_final_scores = ptr(g.get("final_scores"))
+    bi.grad_scores = ptr(g.get("scores"))
+    lg = lse = None
+    if logits is not None:
+        lg, lse = dev(logits), dev(row_lse)
+        bi.logits, bi.logits_type, bi.row_lse = ptr(lg), pb.dtype, ptr(lse)
+    w, gw = dev(np.ascontiguousarray(weights, np.float32)), dev(np.ascontiguousarray(grad_weights, np.float32))
+    grad = torch.full((B, T, K, V), 77.0, dtype=torch.float32, device="cuda")
+    args = dp.args()
+    ws_bytes = lib.dbs_cuda_backward_workspace_size(C.byref(args))
+    ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device="cuda")
+    rc = lib.dbs_cuda_backward_selected(C.byref(args), C.byref(bi), ptr(w), ptr(gw), temperature, ptr(grad),
+                                        A.DTYPE_F32, ptr(ws), ws_bytes, stream_ptr())
+    A.check(rc, "backward_selected")
+    torch.cuda.synchronize()
+    return grad.cpu().numpy()
+
+
 def engine_backward(pb: Problem, trace: dict[str, np.ndarray], grads: dict, logits=None, row_lse=None,
                     use_workspace: bool = True, dense: int | None = None, misalign: int = 0):
     """dbs_cuda_backward_ex into a zeroed float32 gradient, or (dense = a DTYPE_*)

@@ -285,6 +285,40 @@ def test_backward_dense_rejects_bad_arguments():
                                        G.stream_ptr()) == A.STATUS_INVALID_ARGUMENT
 
 
+@pytest.mark.parametrize("seed", range(12))
+def test_selected_weights_and_backward_parity(seed):
+    """Selected-beam weights and the backward through them (the oracle's restatement is pinned to
+    the reference library's single-example API in test_oracle.py), bit for bit."""
+    pb = random_case(2300 + seed, max_kv=20_000)
+    B, T, K, V = pb.shape
+    trace = oracle.oracle_decode(pb)
+    temp = (1.0, 0.5, 2.0, 0.01)[seed % 4]
+    want_w = oracle.oracle_selected_weights(pb, trace["scores"], temp)
+    got_w = G.engine_selected_weights(pb, trace["scores"], temp)
+    assert got_w.tobytes() == want_w.tobytes()
+    rng = np.random.default_rng(seed)
+    gw = rng.uniform(-1, 1, (B, T, K)).astype(np.float32)
+    grads = {"final_scores": rng.uniform(-1, 1, (B, K)).astype(np.float32)}
+    if seed % 2:
+        grads["scores"] = rng.uniform(-1, 1, (B, T, K)).astype(np.float32)
+    logits = pb.x if pb.from_logits else None
+    lse = trace["row_lse"] if pb.from_logits else None
+    want = oracle.oracle_backward_selected(pb, trace, grads, want_w, gw, temp, logits=logits, row_lse=lse)
+    got = G.engine_backward_selected(pb, trace, grads, want_w, gw, temp, logits=logits, row_lse=lse)
+    assert got.tobytes() == want.tobytes()
+
+
+def test_selected_weights_reject_bad_temperature():
+    lib = A.load()
+    pb = make_problem(2, 3, 4, 20, seed=1)
+    dp = G.DeviceProblem(pb)
+    sc = torch.zeros((2, 3, 4), dtype=torch.float32, device="cuda")
+    w = torch.empty_like(sc)
+    for temp in (0.0, -1.0, float("inf"), float("nan")):
+        rc = lib.dbs_cuda_selected_weights(C.byref(dp.args()), G.ptr(sc), temp, G.ptr(w), G.stream_ptr())
+        assert rc == A.STATUS_INVALID_ARGUMENT
+
+
 def test_path_gradient_parity():
     for seed in range(8):
         pb = random_case(3000 + seed, max_kv=20_000)

@@ -145,6 +145,32 @@ def test_oracle_backward_matches_reference_library(seed):
 
 
 @needs_ref
+@pytest.mark.parametrize("seed", range(16))
+def test_selected_weights_match_reference_library(seed):
+    """Selected-beam weights (softmax_selected) and their backward term, against the reference
+    library's single-example API (dbs_decode -> dbs_result_weights; dbs_backward_dense with
+    grad_selected_weights), bit for bit."""
+    rng = np.random.default_rng(500 + seed)
+    T = int(rng.integers(1, 9))
+    K = int(rng.choice([1, 2, 3, 4, 8, 13, 33]))
+    V = int(rng.choice([5, 31, 300]))
+    eos = int(rng.integers(-1, V))
+    alpha = float(rng.choice([0.0, 0.6, 1.0]))
+    ml = int(rng.integers(0, 3))
+    temp = float(rng.choice([1.0, 0.5, 2.0, 0.01]))
+    mode = "ties" if seed % 4 == 3 else ("neginf" if seed % 4 == 2 else "continuous")
+    pb = make_problem(1, T, K, V, seed=seed, eos=eos, alpha=alpha, min_length=ml, mode=mode)
+    gw = rng.uniform(-1, 1, (T, K)).astype(np.float32)
+    gf = rng.uniform(-1, 1, (K,)).astype(np.float32)
+    w_ref, g_ref = oracle.ref_selected(pb.x[0], K, eos, alpha, ml, temp, gw, gf)
+    trace = oracle.oracle_decode(pb)
+    w = oracle.oracle_selected_weights(pb, trace["scores"], temp)
+    g = oracle.oracle_backward_selected(pb, trace, {"final_scores": gf[None]}, w, gw[None], temp)
+    assert same_bits(w[0], w_ref)
+    assert same_bits(g[0], g_ref)
+
+
+@needs_ref
 def test_oracle_c1_config_matches_reference():
     # BASELINE configs[0]: fp32 log-probs [8, 32, 4, 1000], eos=2, alpha=0.6, min_length=4.
     pb = make_problem(8, 32, 4, 1000, seed=0, eos=2, alpha=0.6, min_length=4)
