@@ -3,7 +3,7 @@
 bf16 logits [B=64, T=128, K=8, V=32000] = N(0, 2) + Zipf(s=1.1) per-token bias, from_logits,
 eos=2, length-penalty alpha=1.0 -- decoded through the engine's C ABI (dbs_cuda_decode_ex2).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload c2|c4|c5]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload c1|c2|c3|c4|c5]
 
 One JSON line on rank 0. `value` is whole-job candidates/s (B*T*K*V per decode, all ranks)
 with inputs resident in HBM; `e2e` is the same metric through the same C-ABI call with the
@@ -11,6 +11,9 @@ inputs in pinned host memory, copied in and the outputs copied out inside the ti
 Under torchrun each rank decodes its own batch of the config (weak scaling, no collective on
 the data path). `--impl reference` times the reference's own CPU implementation (libdbs,
 oracle/_ref/libdbs.so) with every host thread on the same config.
+
+`--workload c1` / `--workload c3` time BASELINE configs[0] / configs[2] (decode only; the median
+of per-decode CUDA events with L2 flushed between decodes).
 
 `--workload c4` benchmarks BASELINE configs C4: bf16 log-probs [256,256,4,50257] with variable steps,
 the decode plus the dense bf16 input gradient of a minimum-risk loss (dbs_cuda_backward_dense), per GPU
@@ -60,12 +63,12 @@ def parse():
     ap.add_argument("--batch", type=int, default=None,
                     help="examples per GPU (C2: 64, C4: 256); smaller only for profiling")
     ap.add_argument("--seq", type=int, default=128, help="decode steps T (C2: 128); smaller only for profiling")
-    ap.add_argument("--workload", default="c2", choices=["c2", "c4", "c5"])
+    ap.add_argument("--workload", default="c2", choices=["c1", "c2", "c3", "c4", "c5"])
     args = ap.parse_args()
     global B, T, C4
     if args.workload == "c4" and args.batch is not None:
         C4 = (args.batch,) + C4[1:]
-    if args.workload in ("c4", "c5"):
+    if args.workload in ("c1", "c3", "c4", "c5"):
         return args
     B, T = args.batch if args.batch is not None else 64, args.seq
     return args
@@ -554,6 +557,245 @@ def run_c4(args, rank: int, world: int, local: int):
         dist.destroy_process_group()
 
 
+# ---------------------------------------------------------------------------- C1, C3
+class Spec:
+    """A decode-only BASELINE config: shape, dtype, inputs and search options."""
+
+    def __init__(self, name, shape, dtype, from_logits, eos, alpha, min_length=0, banned_frac=0.0, rep=1.0, ngram=0,
+                 sample=1):
+        self.name, self.shape, self.dtype, self.from_logits = name, shape, dtype, from_logits
+        self.eos, self.alpha, self.min_length = eos, alpha, min_length
+        self.banned_frac, self.rep, self.ngram, self.sample = banned_frac, rep, ngram, sample
+
+    def workload(self) -> str:
+        B_, T_, K_, V_ = self.shape
+        kind = "logits" if self.from_logits else "log-probs"
+        extra = ""
+        if self.banned_frac:
+            extra += f", banned {self.banned_frac:.0%} of V, repetition penalty {self.rep}, no_repeat_ngram {self.ngram}"
+        return (f"{self.name}: {self.dtype} {kind} [{B_},{T_},{K_},{V_}], eos={self.eos}, alpha={self.alpha}, "
+                f"min_length={self.min_length}{extra}")
+
+
+SPECS = {
+    # configs[0]: fp32 log_softmax(3*N(0,1)) [8,32,4,1000], eos=2, alpha=0.6, min_length=4.
+    "c1": Spec("C1", (8, 32, 4, 1000), "f32", False, 2, 0.6, min_length=4, sample=8),
+    # configs[2]: fp16 logits N(0,2)+Zipf(1.1) [32,64,8,151936], banned 1%, rep 1.2, 3-gram, EOS suppressed.
+    "c3": Spec("C3", (32, 64, 8, 151936), "f16", True, -1, 0.0, banned_frac=0.01, rep=1.2, ngram=3, sample=2),
+}
+
+
+def spec_inputs(torch, spec: Spec, seed: int, device, n: int | None = None):
+    """The first n examples (all by default) of the config's input, and its banned-token mask."""
+    B_, T_, K_, V_ = spec.shape
+    n = B_ if n is None else n
+    g = torch.Generator(device=device).manual_seed(seed)
+    if spec.name == "C1":
+        x = torch.log_softmax(3.0 * torch.randn((B_, T_, K_, V_), generator=g, device=device), -1)[:n].contiguous()
+        return x, None
+    bias = -1.1 * torch.log(torch.randperm(V_, generator=g, device=device).float() + 1.0)
+    banned = torch.zeros(V_, dtype=torch.uint8, device=device)
+    banned[torch.randperm(V_, generator=g, device=device)[: int(spec.banned_frac * V_)]] = 1
+    x = torch.empty((n, T_, K_, V_), dtype=torch.float16, device=device)
+    for b in range(n):
+        x[b] = (torch.randn((T_, K_, V_), generator=g, device=device) * 2.0 + bias).half()
+    return x, banned
+
+
+def spec_cpu_reference(torch, spec: Spec, threads: int):
+    """The reference CPU library on the first spec.sample examples; candidates/s and the sample."""
+    from oracle import oracle
+    from beamgrad_b200 import _abi as A
+
+    B_, T_, K_, V_ = spec.shape
+    x, banned = spec_inputs(torch, spec, 100, "cuda" if torch.cuda.is_available() else "cpu", spec.sample)
+    xh = x.cpu().numpy() if spec.dtype == "f32" else x.view(torch.int16).cpu().numpy().view(np.uint16)
+    dt = A.DTYPE_F32 if spec.dtype == "f32" else A.DTYPE_F16
+    pb = oracle.Problem(xh, dtype=dt, from_logits=spec.from_logits, eos=spec.eos, alpha=spec.alpha,
+                        min_length=spec.min_length, ngram=spec.ngram, rep_penalty=spec.rep,
+                        banned=None if banned is None else banned.cpu().numpy())
+    times = []
+    with oracle.RefDecoder(pb) as d:
+        for _ in range(3):
+            t0 = time.perf_counter()
+            d.decode(threads=threads)
+            times.append(time.perf_counter() - t0)
+    sec = statistics.median(times)
+    return spec.sample * T_ * K_ * V_ / sec, f"{spec.sample} of the {B_} examples, median of 3 runs of libdbs"
+
+
+def run_decode_only(args, rank: int, world: int, local: int, spec: Spec):
+    """A decode-only config through dbs_cuda_decode_ex2, per GPU (weak scaling under torchrun)."""
+    import torch
+
+    from oracle import oracle
+
+    B_, T_, K_, V_ = spec.shape
+    cand = B_ * T_ * K_ * V_
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        if not oracle.ref_available():
+            print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/libdbs.so was not built"}))
+            return
+        threads = oracle.cpu_count()
+        per = [spec_cpu_reference(torch, spec, threads) for _ in range(args.warmup + args.steps)][args.warmup:]
+        value = statistics.median(v for v, _ in per)
+        print(json.dumps({
+            "impl": "reference", "metric": METRIC, "value": value, "unit": "candidates/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": cand / value * 1e3, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": spec.dtype, "data": "synthetic",
+            "config": {"workload": spec.workload(), "global_batch": B_, "seq_len": T_, "beam": K_, "vocab": V_,
+                       "parallelism": "host threads"},
+            "cpu_baseline": {"value": value, "unit": "candidates/s", "cores": threads, "kind": "reference",
+                             "sample": per[0][1]},
+            "e2e": {"value": value, "unit": "candidates/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        }), flush=True)
+        return
+
+    from beamgrad_b200 import _abi as A
+
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+    lib = A.load()
+    dev = torch.device("cuda", local)
+    x, banned = spec_inputs(torch, spec, 100 + rank, dev)
+    f32, i32, u8 = torch.float32, torch.int32, torch.uint8
+    out = {n: torch.empty(sh, dtype=dt, device=dev) for n, sh, dt in (
+        ("final_scores", (B_, K_), f32), ("final_raw_scores", (B_, K_), f32), ("final_lengths", (B_, K_), i32),
+        ("tokens", (B_, T_, K_), i32), ("parents", (B_, T_, K_), i32), ("lengths", (B_, T_, K_), i32),
+        ("scores", (B_, T_, K_), f32), ("raw_scores", (B_, T_, K_), f32), ("from_logprob", (B_, T_, K_), u8),
+        ("invalid_input", (B_,), u8))}
+    o = A.DecodeOutputs()
+    for k, v in out.items():
+        setattr(o, k, v.data_ptr())
+    a = A.DecodeArgs()
+    a.batch_size, a.steps, a.beam_size, a.vocab_size = B_, T_, K_, V_
+    a.eos_token, a.length_penalty_alpha, a.min_length = spec.eos, spec.alpha, spec.min_length
+    a.repetition_penalty, a.no_repeat_ngram_size = spec.rep, spec.ngram
+    if banned is not None:
+        a.banned_tokens = banned.data_ptr()
+    dt = A.DTYPE_F32 if spec.dtype == "f32" else A.DTYPE_F16
+    row_lse = torch.empty((B_, T_, K_), dtype=f32, device=dev)
+    ws_bytes = lib.dbs_cuda_decode_workspace_size(C.byref(a))
+    ws = torch.empty(ws_bytes, dtype=u8, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    sp = C.c_void_p(stream.cuda_stream)
+
+    def decode(inp):
+        A.check(lib.dbs_cuda_decode_ex2(C.c_void_p(inp.data_ptr()), dt, int(spec.from_logits), C.byref(a), None,
+                                        C.byref(o), C.c_void_p(row_lse.data_ptr()), C.c_void_p(ws.data_ptr()),
+                                        ws_bytes, sp), "decode")
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+
+    for _ in range(args.warmup):
+        decode(x)
+    barrier()
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)  # 256 MB > L2: flushed between decodes
+    try:
+        gpu_id = f"GPU-{torch.cuda.get_device_properties(dev).uuid}"
+    except (AttributeError, RuntimeError):
+        gpu_id = str(local)
+    evs = []
+    with ClockSampler(gpu_id) as clocks:
+        barrier()
+        clocks.start()
+        deadline = time.monotonic() + 0.5
+        while True:  # at least `steps` decodes and half a second, so the clock sampler sees the load
+            for _ in range(args.steps):
+                flush.zero_()
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record(stream)
+                decode(x)
+                e1.record(stream)
+                evs.append((e0, e1))
+            barrier()
+            if time.monotonic() > deadline:
+                break
+        clocks.stop()
+    per = statistics.median(e0.elapsed_time(e1) for e0, e1 in evs) / 1e3
+    t_all = torch.tensor([per], device=dev, dtype=torch.float64)
+    if dist is not None:
+        dist.all_reduce(t_all, op=dist.ReduceOp.MAX)
+    per = float(t_all.item())
+    host = {k: v.cpu().numpy() for k, v in out.items()}
+    live = ((host["parents"][:, :-1] >= 0) & (host["from_logprob"][:, :-1] == 1) &
+            (host["tokens"][:, :-1] != spec.eos) & np.isfinite(host["raw_scores"][:, :-1]))
+    n_rows = int(B_ + live.sum())
+    elem = 4 if spec.dtype == "f32" else 2
+    alg_bytes = n_rows * V_ * elem + B_ * T_ * K_ * 21 + B_ * K_ * 12
+    peak, peak_kind = peaks()
+    achieved = alg_bytes / per / 1e9
+
+    e2e = None
+    if not args.no_e2e:
+        xh = torch.empty(x.shape, dtype=x.dtype, pin_memory=True)
+        xh.copy_(x)
+        xd = torch.empty_like(x)
+        outs_h = {k: torch.empty(v.shape, dtype=v.dtype, pin_memory=True) for k, v in out.items()}
+        n_e2e = max(2, min(args.steps, 5))
+
+        def e2e_step():
+            xd.copy_(xh, non_blocking=True)
+            decode(xd)
+            for k, v in out.items():
+                outs_h[k].copy_(v, non_blocking=True)
+
+        e2e_step()
+        barrier()
+        s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s0.record(stream)
+        for _ in range(n_e2e):
+            e2e_step()
+        s1.record(stream)
+        barrier()
+        e2e_t = torch.tensor([s0.elapsed_time(s1) / 1e3 / n_e2e], device=dev, dtype=torch.float64)
+        if dist is not None:
+            dist.all_reduce(e2e_t, op=dist.ReduceOp.MAX)
+        e2e = {"value": world * cand / float(e2e_t.item()), "unit": "candidates/s",
+               "h2d_bytes_per_step": xh.numel() * xh.element_size(),
+               "d2h_bytes_per_step": sum(v.numel() * v.element_size() for v in outs_h.values())}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and oracle.ref_available():
+        threads = oracle.cpu_count()
+        value, sample = spec_cpu_reference(torch, spec, threads)
+        cpu = {"value": value, "unit": "candidates/s", "cores": threads, "kind": "reference", "sample": sample}
+    if dist is not None:
+        dist.barrier()
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": world * cand / per, "unit": "candidates/s", "n_gpus": world,
+            "steps": len(evs), "warmup": args.warmup, "ms_per_step": per * 1e3, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": spec.dtype, "data": "synthetic",
+            "config": {"workload": spec.workload(), "global_batch": world * B_, "seq_len": T_, "beam": K_,
+                       "vocab": V_, "parallelism": f"batch x{world}" if world > 1 else "single GPU",
+                       "l2": "256 MB buffer written between timed decodes (L2 flushed)",
+                       "timing": "median of per-decode CUDA events", "rows_read": n_rows},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                         "traffic": None, "peak_kind": peak_kind, "alg_bytes_per_launch": alg_bytes},
+            "cpu_baseline": cpu,
+            "e2e": e2e,
+            "gpu_launches": 2 * len(evs),
+            "clocks": clocks.summary(),
+        }
+        if spec.from_logits:
+            line["roofline_fp32"] = fp32_roofline(n_rows * V_, per, clocks.summary())
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.destroy_process_group()
+
+
 # ---------------------------------------------------------------------------- C5
 C5 = (16, 32, 64, 256000)
 C5_EOS, C5_ALPHA = 1, 0.6
@@ -779,6 +1021,8 @@ def main():
         return run_c5(args, rank, world, local)
     if args.workload == "c4":
         return run_c4(args, rank, world, local)
+    if args.workload in ("c1", "c3"):
+        return run_decode_only(args, rank, world, local, SPECS[args.workload])
     if args.impl == "reference":
         return run_reference_arm(args, rank, world)
 
