@@ -2449,8 +2449,12 @@ __global__ void __launch_bounds__(kThreads, 3) decode_chain_kernel(const __grid_
                 }
             };
             Prep o;
-            // From logits, warps 4-7 scan while warps 0-3 compute the logsumexp.
-            prepare_row<DT, LOGITS, LIST>(p, sh, srow, grow, phase, p.staged != 0, !exclusions, LIST, m, o,
+            // From logits, warps 4-7 scan while warps 0-3 compute the logsumexp. The bound
+            // (the LIST-th largest thread maximum) is also used with banned tokens: the record
+            // keeps only eligible entries at or above it, and a row with fewer than LIST such
+            // entries (a banned entry took one of the top thread maxima) is redone below
+            // without a bound.
+            prepare_row<DT, LOGITS, LIST>(p, sh, srow, grow, phase, p.staged != 0, true, LIST, m, o,
                                           [&](const char* src, const RowSplit& rs, float xthr) {
                                               record_scan(std::integral_constant<int, kThreads / 2>{}, src, rs, xthr,
                                                           tid - kThreads / 2);
@@ -2476,6 +2480,36 @@ __global__ void __launch_bounds__(kThreads, 3) decode_chain_kernel(const __grid_
                 if (lane == 0) sh.nlist[warp] = __popc(nz);
                 block_sync();
                 rank_merge<LIST>(sh.wkeys, kWarps, warp, wt.wl, p.rkeys + rowi * LIST);
+            }
+            if (exclusions && o.xthr != f_ninf()) {
+                block_sync();  // the lists' counts of every list warp are visible
+                int found = 0;
+#pragma unroll
+                for (int w = 0; w < kLists; ++w) found += sh.nlist[kWarps - kLists + w];
+                block_sync();
+                if (found < LIST) {
+                    // Fewer than LIST eligible entries reached the bound: the record again, unbounded.
+                    if constexpr (LOGITS) {
+                        if (warp >= kWarps / 2) {
+                            record_scan(std::integral_constant<int, kThreads / 2>{}, o.src, o.rs, f_ninf(),
+                                        tid - kThreads / 2);
+                            const int lw = warp - kWarps / 2;
+                            if (lane < LIST) sh.wkeys[lw * LIST + lane] = wt.wl;
+                            const unsigned nz = __ballot_sync(0xffffffffu, lane < LIST && wt.wl != 0);
+                            if (lane == 0) sh.nlist[warp] = __popc(nz);
+                            half_sync(1);
+                            rank_merge<LIST>(sh.wkeys, kWarps / 2, lw, wt.wl, p.rkeys + rowi * LIST);
+                        }
+                    } else {
+                        record_scan(std::integral_constant<int, kThreads>{}, o.src, o.rs, f_ninf(), tid);
+                        if (lane < LIST) sh.wkeys[warp * LIST + lane] = wt.wl;
+                        const unsigned nz = __ballot_sync(0xffffffffu, lane < LIST && wt.wl != 0);
+                        if (lane == 0) sh.nlist[warp] = __popc(nz);
+                        block_sync();
+                        rank_merge<LIST>(sh.wkeys, kWarps, warp, wt.wl, p.rkeys + rowi * LIST);
+                    }
+                    block_sync();
+                }
             }
             if (tid == 0) {
                 int total = 0;
