@@ -222,6 +222,7 @@ SIGNATURES = {
         [C.POINTER(DecodeArgs), C.POINTER(BackwardInputs), _p, C.c_int, _p, C.c_int64, _p],
     ),
     "dbs_cuda_selected_weights": (C.c_int, [C.POINTER(DecodeArgs), _p, C.c_float, _p, _p]),
+    "dbs_cuda_b200_wait_selftest": (C.c_int, [C.c_int64, _p, _p]),
     "dbs_cuda_backward_selected": (
         C.c_int,
         [C.POINTER(DecodeArgs), C.POINTER(BackwardInputs), _p, _p, C.c_float, _p, C.c_int, _p, C.c_int64, _p],
@@ -242,7 +243,7 @@ SIGNATURES = {
 VSHARD_SYMBOLS = ("dbs_cuda_vshard_plan", "dbs_cuda_vshard_scan", "dbs_cuda_vshard_lanes", "dbs_cuda_vshard_merge",
                   "dbs_cuda_vshard_select", "dbs_cuda_vshard_rescan")
 ADDED_SYMBOLS = ("dbs_cuda_b200_abi_version", "dbs_cuda_backtrack", "dbs_cuda_backward_dense", "dbs_cuda_advance_prefixes",
-                 "dbs_cuda_selected_weights", "dbs_cuda_backward_selected",
+                 "dbs_cuda_selected_weights", "dbs_cuda_backward_selected", "dbs_cuda_b200_wait_selftest",
                  "dbs_cuda_decode_no_alloc") + VSHARD_SYMBOLS
 REFERENCE_SYMBOLS = [n for n in SIGNATURES if n not in ADDED_SYMBOLS]
 

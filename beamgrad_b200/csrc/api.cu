@@ -20,6 +20,7 @@ namespace dbsb {
 cudaError_t launch_decode(const DecodeParams& p, int dtype, bool logits, cudaStream_t stream, int sm_count);
 cudaError_t launch_init(const DecodeParams& p, cudaStream_t stream);
 cudaError_t launch_validate(const DecodeParams& p, int* status, cudaStream_t stream);
+cudaError_t launch_wait_selftest(const DecodeParams& p, const int32_t* flag, int32_t* words, cudaStream_t stream);
 int decode_list_len(int K);
 int decode_chain_list_len(int K);
 size_t decode_chain_wide_smem(int K);
@@ -700,6 +701,22 @@ DBS_CUDA_EXPORT int dbs_cuda_selected_weights(const DBSCudaDecodeArgs* args, con
         return DBS_CUDA_STATUS_LAUNCH_FAILED;
     }
     return finish(stream, nullptr);
+}
+
+DBS_CUDA_EXPORT int dbs_cuda_b200_wait_selftest(int64_t timeout_ns, int32_t* words, void* stream_ptr) {
+    if (!words || timeout_ns < 100000 || timeout_ns > 1000000000) return DBS_CUDA_STATUS_INVALID_ARGUMENT;
+    cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+    // words[0..1]: the waits' results; words[2]: the error word; words[3]: the flag nothing sets.
+    if (cudaMemsetAsync(words, 0, 4 * sizeof(int32_t), stream) != cudaSuccess) return DBS_CUDA_STATUS_LAUNCH_FAILED;
+    DecodeParams p;
+    std::memset(&p, 0, sizeof p);
+    p.timeout_ns = static_cast<unsigned long long>(timeout_ns);
+    p.error = words + 2;
+    if (launch_wait_selftest(p, words + 3, words, stream) != cudaSuccess) return DBS_CUDA_STATUS_LAUNCH_FAILED;
+    if (cudaStreamSynchronize(stream) != cudaSuccess) return DBS_CUDA_STATUS_LAUNCH_FAILED;
+    int32_t e = 0;
+    if (cudaMemcpy(&e, words + 2, sizeof e, cudaMemcpyDeviceToHost) != cudaSuccess) return DBS_CUDA_STATUS_LAUNCH_FAILED;
+    return e == 0 ? DBS_CUDA_STATUS_OK : DBS_CUDA_STATUS_LAUNCH_FAILED;
 }
 
 DBS_CUDA_EXPORT int dbs_cuda_advance_prefixes(int batch_size, int beam_size, int step, int prefix_stride,

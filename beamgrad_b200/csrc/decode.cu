@@ -128,6 +128,29 @@ cudaError_t launch_init(const DecodeParams& p, cudaStream_t stream) {
     return cudaGetLastError();
 }
 
+// Self-test of the bounded waits: warp 0 waits on a flag that nothing sets, warp 1 on
+// an mbarrier that nothing arrives at (no copy is in flight). Both give up after
+// p.timeout_ns, record kErrTimeout in p.error and return false; words[0..1] receive
+// their results (1 = the wait succeeded).
+__global__ void wait_selftest_kernel(DecodeParams p, const int32_t* flag, int32_t* words) {
+    __shared__ unsigned long long mbar;
+    const int lane = threadIdx.x & 31;
+    const int warp = threadIdx.x >> 5;
+    if (threadIdx.x == 0) mbar_init(&mbar);
+    __syncthreads();
+    if (warp == 0) {
+        const bool ok = wait_flag_warp(p, flag, 1);
+        if (lane == 0) words[0] = ok ? 1 : 0;
+    } else if (warp == 1 && lane == 0) {
+        words[1] = mbar_wait(p, &mbar, 0) ? 1 : 0;
+    }
+}
+
+cudaError_t launch_wait_selftest(const DecodeParams& p, const int32_t* flag, int32_t* words, cudaStream_t stream) {
+    wait_selftest_kernel<<<1, 64, 0, stream>>>(p, flag, words);
+    return cudaGetLastError();
+}
+
 cudaError_t launch_validate(const DecodeParams& p, int* status, cudaStream_t stream) {
     validate_meta_kernel<<<static_cast<unsigned>((p.B + 255) / 256), 256, 0, stream>>>(p, status);
     return cudaGetLastError();

@@ -85,6 +85,18 @@ DBS_CUDA_EXPORT int dbs_cuda_advance_prefixes(int batch_size, int beam_size, int
                                               int32_t* prefixes_out, const float* raw_scores, const uint8_t* finished,
                                               uint8_t* any_live, void* stream);
 
+/* Self-test of the engine's failure detection, without a GPU fault. Every inter-CTA wait
+ * of the decode kernels (a flag spin, an mbarrier wait) is bounded: past its limit it
+ * records a timeout in the decode's error word and returns, and the host reports
+ * DBS_CUDA_STATUS_LAUNCH_FAILED when synchronization is on. This runs the same two waits,
+ * one on a flag nothing sets and one on an mbarrier nothing arrives at (no copy in flight),
+ * with a limit of timeout_ns (1e5 .. 1e9); words is a device buffer of 4 int32 (0, 1: the
+ * waits' results; 2: the error word; 3: the unset flag). It synchronizes the stream and
+ * returns DBS_CUDA_STATUS_LAUNCH_FAILED when the error word holds the timeout (the expected
+ * outcome), DBS_CUDA_STATUS_OK otherwise. The context stays usable. No counterpart in the
+ * reference. */
+DBS_CUDA_EXPORT int dbs_cuda_b200_wait_selftest(int64_t timeout_ns, int32_t* words, void* stream);
+
 /* Bytes of the fixed device array behind dbs_cuda_decode_no_alloc (4 MiB). */
 #define DBS_CUDA_B200_NO_ALLOC_SCRATCH_BYTES (4 * 1024 * 1024)
 

@@ -319,6 +319,20 @@ def test_selected_weights_reject_bad_temperature():
         assert rc == A.STATUS_INVALID_ARGUMENT
 
 
+def test_bounded_waits_time_out_and_context_survives():
+    """Failure detection without a GPU fault: the decode kernels' bounded waits (a flag that
+    nothing sets, an mbarrier nothing arrives at) give up after a 2 ms limit, record the timeout
+    in the error word, and the host reports LAUNCH_FAILED; the next decode is still exact."""
+    lib = A.load()
+    words = torch.full((4,), 7, dtype=torch.int32, device="cuda")
+    rc = lib.dbs_cuda_b200_wait_selftest(2_000_000, G.ptr(words), G.stream_ptr())
+    assert rc == A.STATUS_LAUNCH_FAILED
+    assert words.cpu().tolist() == [0, 0, 1, 0]  # both waits gave up; error word = timeout
+    assert lib.dbs_cuda_b200_wait_selftest(10, G.ptr(words), G.stream_ptr()) == A.STATUS_INVALID_ARGUMENT
+    pb = make_problem(2, 5, 4, 300, seed=9, eos=2, alpha=0.6)
+    assert_same(G.engine_decode(pb), oracle.oracle_decode(pb), ctx="after the timeout self-test")
+
+
 def test_path_gradient_parity():
     for seed in range(8):
         pb = random_case(3000 + seed, max_kv=20_000)
