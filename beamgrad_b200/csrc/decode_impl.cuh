@@ -2454,7 +2454,10 @@ __global__ void __launch_bounds__(kThreads, 3) decode_chain_kernel(const __grid_
             // keeps only eligible entries at or above it, and a row with fewer than LIST such
             // entries (a banned entry took one of the top thread maxima) is redone below
             // without a bound.
-            prepare_row<DT, LOGITS, LIST>(p, sh, srow, grow, phase, p.staged != 0, true, LIST, m, o,
+            // With banned tokens the bound is ranked lower (LIST + LIST / 2 thread maxima), so
+            // that a few banned entries among them still leave LIST eligible ones above it.
+            prepare_row<DT, LOGITS, LIST>(p, sh, srow, grow, phase, p.staged != 0, true,
+                                          exclusions ? LIST + LIST / 2 : LIST, m, o,
                                           [&](const char* src, const RowSplit& rs, float xthr) {
                                               record_scan(std::integral_constant<int, kThreads / 2>{}, src, rs, xthr,
                                                           tid - kThreads / 2);
@@ -3439,7 +3442,9 @@ __global__ void __launch_bounds__(kThreads, 2) decode_chain_wide_kernel(const __
     const uint32_t rows_per_step = static_cast<uint32_t>(p.B) * static_cast<uint32_t>(K);
     const uint32_t total = rows_per_step * static_cast<uint32_t>(T);
     const bool exclusions = p.banned != nullptr;
-    const bool want_bound = !exclusions && LIST <= kWarps * 32;
+    // With banned tokens the bound (from thread maxima that may be banned entries) is kept;
+    // a row where fewer than LIST eligible entries reach it takes the block select below.
+    const bool want_bound = LIST <= kWarps * 32;
 
     uint32_t next_ticket = 0;
     if (tid == 0) next_ticket = atomicAdd(p.ticket, 1u);
@@ -3465,7 +3470,10 @@ __global__ void __launch_bounds__(kThreads, 2) decode_chain_wide_kernel(const __
             if (tid == 0) ws.n_cand = 0;
             Prep o;
             // From logits, warps 4-7 collect the entries at or above the bound during pass 2.
-            prepare_row<DT, LOGITS, 32>(p, sh, srow, grow, phase, p.staged != 0, want_bound, LIST, m, o,
+            prepare_row<DT, LOGITS, 32>(p, sh, srow, grow, phase, p.staged != 0, want_bound,
+                                        exclusions ? (LIST + LIST / 2 < kWarps * 32 ? LIST + LIST / 2 : kWarps * 32)
+                                                   : LIST,
+                                        m, o,
                                         [&](const char* src, const RowSplit& rs, float xthr) {
                                             if (xthr != f_ninf())
                                                 collect_candidates<DT, kThreads / 2>(ws, src, rs, tid - kThreads / 2,
@@ -3485,7 +3493,7 @@ __global__ void __launch_bounds__(kThreads, 2) decode_chain_wide_kernel(const __
             uint64_t* rec = p.rkeys + rowi * LIST;
             const int n = ws.n_cand;
             int cnt;
-            if (o.xthr != f_ninf() && n <= kWideCand) {
+            if (o.xthr != f_ninf() && n <= kWideCand && (!exclusions || n >= LIST)) {
                 cnt = sort_candidates(ws, n, LIST, rec);
             } else {
                 auto gen = [&](int v) -> uint64_t {
