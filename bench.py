@@ -3,7 +3,7 @@
 bf16 logits [B=64, T=128, K=8, V=32000] = N(0, 2) + Zipf(s=1.1) per-token bias, from_logits,
 eos=2, length-penalty alpha=1.0 -- decoded through the engine's C ABI (dbs_cuda_decode_ex2).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload c1|c2|c3|c4|c5]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload c1|c2|c3|c4|c5|search]
 
 One JSON line on rank 0. `value` is whole-job candidates/s (B*T*K*V per decode, all ranks)
 with inputs resident in HBM; `e2e` is the same metric through the same C-ABI call with the
@@ -63,12 +63,12 @@ def parse():
     ap.add_argument("--batch", type=int, default=None,
                     help="examples per GPU (C2: 64, C4: 256); smaller only for profiling")
     ap.add_argument("--seq", type=int, default=128, help="decode steps T (C2: 128); smaller only for profiling")
-    ap.add_argument("--workload", default="c2", choices=["c1", "c2", "c3", "c4", "c5"])
+    ap.add_argument("--workload", default="c2", choices=["c1", "c2", "c3", "c4", "c5", "search"])
     args = ap.parse_args()
     global B, T, C4
     if args.workload == "c4" and args.batch is not None:
         C4 = (args.batch,) + C4[1:]
-    if args.workload in ("c1", "c3", "c4", "c5"):
+    if args.workload in ("c1", "c3", "c4", "c5", "search"):
         return args
     B, T = args.batch if args.batch is not None else 64, args.seq
     return args
@@ -796,6 +796,131 @@ def run_decode_only(args, rank: int, world: int, local: int, spec: Spec):
         dist.destroy_process_group()
 
 
+# ---------------------------------------------------------------------------- search loop
+def run_search(args, rank: int, world: int, local: int):
+    """beamgrad's step-by-step search loop (python/beamgrad/_search.py:330-467) on C2's shape
+    with bf16 log-prob rows fed one step at a time: the loop as beamgrad writes it over
+    torch.ops.beamgrad.decode_step (per step: float32 copy of the rows, state clones, the
+    validation read-back and the active.any() check, sequences by gather + cat), against
+    beamgrad_b200.search.DeviceSearch eager (live flag read every step, as beamgrad stops) and
+    the same search captured in one CUDA graph. Each step's "model" is a copy of that step's
+    rows into a fixed buffer. Per GPU; rank 0 prints."""
+    import torch
+
+    from beamgrad_b200 import ops
+    from beamgrad_b200 import search as S
+
+    Bs, Ts, Ks, Vs = 64, 128, 8, 32000
+    cand = Bs * Ts * Ks * Vs
+    if args.impl == "reference":
+        if rank == 0:
+            print(json.dumps({"impl": "reference", "unavailable": "the search loop workload has no CPU arm: "
+                              "beamgrad's loop is the 'loop_reference_style' figure of our line"}))
+        return
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    ops.load()
+    g = torch.Generator(device=dev).manual_seed(7000 + rank)
+    bias = -1.1 * torch.log(torch.randperm(Vs, generator=g, device=dev).float() + 1.0)
+    x = torch.empty((Ts, Bs, Ks, Vs), dtype=torch.bfloat16, device=dev)  # step-major: each step contiguous
+    for t in range(Ts):
+        x[t] = torch.log_softmax(torch.randn((Bs, Ks, Vs), generator=g, device=dev) * 2.0 + bias, -1).to(x.dtype)
+    rows = torch.empty((Bs, Ks, Vs), dtype=torch.bfloat16, device=dev)
+    eos, alpha = 2, 1.0
+    stream = torch.cuda.current_stream(dev)
+
+    def reference_loop():
+        raw = torch.full((Bs, Ks), float("-inf"), device=dev)
+        raw[:, 0] = 0.0
+        lengths = torch.zeros((Bs, Ks), dtype=torch.int32, device=dev)
+        finished = torch.zeros((Bs, Ks), dtype=torch.uint8, device=dev)
+        sequences = torch.empty((Bs, Ks, 0), dtype=torch.int64, device=dev)
+        for t in range(Ts):
+            active = torch.isfinite(raw) & (finished == 0)
+            if t > 0 and not bool(active.any()):
+                break
+            rows.copy_(x[t])
+            tok, par, lengths, scores, raw, flp, finished, final = torch.ops.beamgrad.decode_step(
+                rows.to(torch.float32).contiguous(), raw, lengths, finished, sequences.to(torch.int32), eos, 0, alpha,
+                None, 0, 1.0, True, [])
+            parents, tokens = par.long(), tok.long()
+            source = parents.clamp(min=0)[..., None].expand(Bs, Ks, t)
+            emitted = torch.where(flp.bool(), tokens, -1)
+            sequences = torch.cat([sequences.gather(1, source), emitted[..., None]], dim=2)
+            sequences = torch.where((parents >= 0)[..., None], sequences, -1)
+        return sequences
+
+    search = S.DeviceSearch(Bs, Ks, Vs, Ts, dtype=torch.bfloat16, eos_token=eos, length_penalty_alpha=alpha,
+                            device=dev)
+
+    def device_loop(check_every: int):
+        search.reset()
+        for t in range(Ts):
+            if t > 0 and t % check_every == 0 and not search.live_after(t - 1):
+                break
+            rows.copy_(x[t])
+            search.step(rows)
+
+    def graph_body():
+        search.reset()
+        for t in range(Ts):
+            rows.copy_(x[t])
+            search.step(rows)
+
+    def timed(fn, reps):
+        fn()
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(reps):
+            fn()
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        return e0.elapsed_time(e1) / 1e3 / reps
+
+    reps = max(1, args.steps)
+    for _ in range(max(0, args.warmup - 1)):
+        device_loop(1)
+    try:
+        gpu_id = f"GPU-{torch.cuda.get_device_properties(dev).uuid}"
+    except (AttributeError, RuntimeError):
+        gpu_id = str(local)
+    with ClockSampler(gpu_id) as clocks:
+        clocks.start()
+        t_ref = timed(reference_loop, reps)
+        t_dev1 = timed(lambda: device_loop(1), reps)
+        t_devT = timed(lambda: device_loop(Ts), reps)
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(stream)
+        with torch.cuda.stream(side):
+            graph_body()
+        stream.wait_stream(side)
+        torch.cuda.synchronize(dev)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            graph_body()
+        t_graph = timed(graph.replay, reps)
+        clocks.stop()
+    steps_run = int(search.result().trace.steps[0])
+    same = torch.equal(search.result().sequences[..., :steps_run], reference_loop()[..., :steps_run].long())
+    if rank == 0:
+        print(json.dumps({
+            "metric": METRIC, "value": cand / t_dev1, "unit": "candidates/s", "n_gpus": world, "steps": reps,
+            "warmup": args.warmup, "ms_per_step": t_dev1 * 1e3, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": f"search loop: bf16 log-prob rows [{Bs},{Ks},{Vs}] per step, {Ts} steps "
+                                   f"(C2's shape, log_softmax(N(0,2)+Zipf(1.1))), eos={eos}, alpha={alpha}",
+                       "global_batch": Bs, "seq_len": Ts, "beam": Ks, "vocab": Vs, "steps_run": steps_run,
+                       "step": "one whole search (Ts model steps: a 32.8 MB row copy + one search step)"},
+            "loops_ms": {"loop_reference_style": t_ref * 1e3, "device_search_check_every_step": t_dev1 * 1e3,
+                         "device_search_no_host_sync": t_devT * 1e3, "device_search_cuda_graph": t_graph * 1e3},
+            "speedup_vs_reference_style": t_ref / t_dev1,
+            "sequences_match_reference_style": bool(same),
+            "roofline": None, "cpu_baseline": None, "e2e": None,
+            "gpu_launches": None, "clocks": clocks.summary(),
+        }), flush=True)
+
+
 # ---------------------------------------------------------------------------- C5
 C5 = (16, 32, 64, 256000)
 C5_EOS, C5_ALPHA = 1, 0.6
@@ -1023,6 +1148,8 @@ def main():
         return run_c4(args, rank, world, local)
     if args.workload in ("c1", "c3"):
         return run_decode_only(args, rank, world, local, SPECS[args.workload])
+    if args.workload == "search":
+        return run_search(args, rank, world, local)
     if args.impl == "reference":
         return run_reference_arm(args, rank, world)
 
