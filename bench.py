@@ -7,10 +7,12 @@ eos=2, length-penalty alpha=1.0 -- decoded through the engine's C ABI (dbs_cuda_
 
 One JSON line on rank 0. `value` is whole-job candidates/s (B*T*K*V per decode, all ranks)
 with inputs resident in HBM; `e2e` is the same metric through the same C-ABI call with the
-inputs in pinned host memory, copied in and the outputs copied out inside the timed region.
-Under torchrun each rank decodes its own batch of the config (weak scaling, no collective on
-the data path). `--impl reference` times the reference's own CPU implementation (libdbs,
-oracle/_ref/libdbs.so) with every host thread on the same config.
+inputs in pinned host memory, copied in and the outputs copied out inside the timed region
+(in chunks of examples, each chunk's copy overlapping the previous chunk's decode). Under
+torchrun the config's 64 examples are split contiguously over the ranks (strong scaling, no
+collective on the data path; the outputs stay sharded by example); `--scaling weak` gives every
+rank a batch of its own instead. `--impl reference` times the reference's own CPU
+implementation (libdbs, oracle/_ref/libdbs.so) with every host thread on the same config.
 
 `--workload c1` / `--workload c3` time BASELINE configs[0] / configs[2] (decode only; the median
 of per-decode CUDA events with L2 flushed between decodes).
@@ -61,7 +63,10 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--batch", type=int, default=None,
-                    help="examples per GPU (C2: 64, C4: 256); smaller only for profiling")
+                    help="C2: examples of the whole job (64); C4: examples per GPU (256); smaller only for profiling")
+    ap.add_argument("--scaling", default="strong", choices=["strong", "weak"],
+                    help="C2 on N GPUs: strong = the config's batch split over the ranks (default); "
+                         "weak = every rank decodes a batch of its own")
     ap.add_argument("--seq", type=int, default=128, help="decode steps T (C2: 128); smaller only for profiling")
     ap.add_argument("--workload", default="c2", choices=["c1", "c2", "c3", "c4", "c5", "search"])
     args = ap.parse_args()
@@ -180,12 +185,18 @@ class ClockSampler:
         return out
 
 
-def make_inputs(torch, seed: int, device):
+def make_inputs(torch, seed: int, device, examples=None):
+    """Examples `examples` (default: all B) of the C2 input, bf16 [len(examples), T, K, V].
+
+    Example b is drawn from its own seed, so a rank that holds examples [start, stop) of the
+    batch gets the same bits as the whole-batch input has there, whatever the rank count."""
+    examples = range(B) if examples is None else examples
     g = torch.Generator(device=device).manual_seed(seed)
     bias = -1.1 * torch.log(torch.randperm(V, generator=g, device=device).float() + 1.0)
-    x = torch.empty((B, T, K, V), dtype=torch.bfloat16, device=device)
-    for b in range(B):  # chunked: keeps the float32 temporary small
-        x[b] = (torch.randn((T, K, V), generator=g, device=device) * 2.0 + bias).to(torch.bfloat16)
+    x = torch.empty((len(examples), T, K, V), dtype=torch.bfloat16, device=device)
+    for i, b in enumerate(examples):  # one example at a time: keeps the float32 temporary small
+        g.manual_seed(seed * 1009 + 1 + b)
+        x[i] = (torch.randn((T, K, V), generator=g, device=device) * 2.0 + bias).to(torch.bfloat16)
     return x
 
 
@@ -235,7 +246,7 @@ def run_reference_arm(args, rank: int, world: int):
     print(json.dumps({
         "impl": "reference", "metric": METRIC, "value": value, "unit": "candidates/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": sec * 1e3, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "scaling": args.scaling, "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
         "config": {"workload": workload(), "global_batch": B, "seq_len": T, "beam": K, "vocab": V,
                    "parallelism": "host threads"},
         "cpu_baseline": {"value": value, "unit": "candidates/s", "cores": threads, "kind": "reference",
@@ -1167,28 +1178,40 @@ def main():
 
     lib = A.load()
     dev = torch.device("cuda", local)
-    x = make_inputs(torch, 1000 + rank, dev)
+    strong = args.scaling == "strong"
+    # Strong scaling: rank r decodes examples [start, stop) of the one C2 batch (contiguous,
+    # beamgrad_b200.sharding.shard_range); weak: every rank its own whole batch.
+    if strong:
+        from beamgrad_b200.sharding import shard_range
+
+        start, stop = shard_range(B, rank, world)
+        x = make_inputs(torch, 1000, dev, range(start, stop))
+    else:
+        start, stop = 0, B
+        x = make_inputs(torch, 1000 + rank, dev)
+    Bl = stop - start  # examples on this rank
+    global_batch = B if strong else world * B
 
     # Outputs and workspace allocated once.
     f32, i32, u8 = torch.float32, torch.int32, torch.uint8
     out = {
-        "final_scores": torch.empty((B, K), dtype=f32, device=dev),
-        "final_raw_scores": torch.empty((B, K), dtype=f32, device=dev),
-        "final_lengths": torch.empty((B, K), dtype=i32, device=dev),
-        "tokens": torch.empty((B, T, K), dtype=i32, device=dev),
-        "parents": torch.empty((B, T, K), dtype=i32, device=dev),
-        "lengths": torch.empty((B, T, K), dtype=i32, device=dev),
-        "scores": torch.empty((B, T, K), dtype=f32, device=dev),
-        "raw_scores": torch.empty((B, T, K), dtype=f32, device=dev),
-        "from_logprob": torch.empty((B, T, K), dtype=u8, device=dev),
-        "invalid_input": torch.empty((B,), dtype=u8, device=dev),
+        "final_scores": torch.empty((Bl, K), dtype=f32, device=dev),
+        "final_raw_scores": torch.empty((Bl, K), dtype=f32, device=dev),
+        "final_lengths": torch.empty((Bl, K), dtype=i32, device=dev),
+        "tokens": torch.empty((Bl, T, K), dtype=i32, device=dev),
+        "parents": torch.empty((Bl, T, K), dtype=i32, device=dev),
+        "lengths": torch.empty((Bl, T, K), dtype=i32, device=dev),
+        "scores": torch.empty((Bl, T, K), dtype=f32, device=dev),
+        "raw_scores": torch.empty((Bl, T, K), dtype=f32, device=dev),
+        "from_logprob": torch.empty((Bl, T, K), dtype=u8, device=dev),
+        "invalid_input": torch.empty((Bl,), dtype=u8, device=dev),
     }
-    row_lse = torch.empty((B, T, K), dtype=f32, device=dev)
+    row_lse = torch.empty((Bl, T, K), dtype=f32, device=dev)
     o = A.DecodeOutputs()
     for k, v in out.items():
         setattr(o, k, v.data_ptr())
     a = A.DecodeArgs()
-    a.batch_size, a.steps, a.beam_size, a.vocab_size = B, T, K, V
+    a.batch_size, a.steps, a.beam_size, a.vocab_size = Bl, T, K, V
     a.eos_token, a.length_penalty_alpha, a.repetition_penalty = EOS, ALPHA, 1.0
     ws_bytes = lib.dbs_cuda_decode_workspace_size(C.byref(a))
     ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
@@ -1246,14 +1269,18 @@ def main():
     # Algorithmic bytes of one decode: every row the search read (V bf16 entries) + trace/state writes.
     host = {k: v.cpu().numpy() for k, v in out.items()}
     n_rows = rows_read(host["tokens"], host["parents"], host["from_logprob"], host["raw_scores"])
-    trace_bytes = B * T * K * (4 * 5 + 1) + B * T * K * 4 + B * K * 12
+    trace_bytes = Bl * T * K * (4 * 5 + 1) + Bl * T * K * 4 + Bl * K * 12
     alg_bytes = n_rows * V * 2 + trace_bytes
     peak, peak_kind = peaks()
     achieved = alg_bytes / per_launch / 1e9
 
     # End to end through the same C-ABI call: pinned host input -> device, decode, outputs -> host.
+    # The rank's examples go in chunks: chunk c's copy (on a copy stream) overlaps the decode of
+    # chunk c - 1 (dbs_cuda_decode_ex2 on that chunk's slices of the inputs and outputs).
     e2e = None
     if not args.no_e2e:
+        from beamgrad_b200.sharding import shard_range
+
         xh = torch.empty(x.shape, dtype=x.dtype, pin_memory=True)
         xh.copy_(x)
         xd = torch.empty_like(x)
@@ -1261,10 +1288,36 @@ def main():
         h2d = xh.numel() * xh.element_size()
         d2h = sum(v.numel() * v.element_size() for v in outs_h.values())
         e2e_steps = max(2, min(args.steps, 5))
+        n_chunks = min(Bl, 8)
+        chunks = [shard_range(Bl, c, n_chunks) for c in range(n_chunks)]
+        calls = []
+        for c0, c1 in chunks:
+            ac = A.DecodeArgs()
+            ac.batch_size, ac.steps, ac.beam_size, ac.vocab_size = c1 - c0, T, K, V
+            ac.eos_token, ac.length_penalty_alpha, ac.repetition_penalty = EOS, ALPHA, 1.0
+            oc = A.DecodeOutputs()
+            for k, v in out.items():
+                setattr(oc, k, v[c0:c1].data_ptr())
+            calls.append((c0, c1, ac, oc, lib.dbs_cuda_decode_workspace_size(C.byref(ac))))
+        ws_c = torch.empty(max(c[4] for c in calls), dtype=torch.uint8, device=dev)
+        copy_stream = torch.cuda.Stream(dev)
+        copied = [torch.cuda.Event() for _ in chunks]
+        consumed = [torch.cuda.Event() for _ in chunks]
+        for ev in consumed:
+            ev.record(stream)
 
         def e2e_step():
-            xd.copy_(xh, non_blocking=True)
-            decode(xd)
+            for i, (c0, c1, ac, oc, nb) in enumerate(calls):
+                copy_stream.wait_event(consumed[i])  # the previous step's decode of this chunk is done
+                with torch.cuda.stream(copy_stream):
+                    xd[c0:c1].copy_(xh[c0:c1], non_blocking=True)
+                copied[i].record(copy_stream)
+                stream.wait_event(copied[i])
+                rc = lib.dbs_cuda_decode_ex2(C.c_void_p(xd[c0:c1].data_ptr()), A.DTYPE_BF16, 1, C.byref(ac), None,
+                                             C.byref(oc), C.c_void_p(row_lse[c0:c1].data_ptr()),
+                                             C.c_void_p(ws_c.data_ptr()), nb, C.c_void_p(stream.cuda_stream))
+                A.check(rc, "decode")
+                consumed[i].record(stream)
             for k, v in out.items():
                 outs_h[k].copy_(v, non_blocking=True)
 
@@ -1272,6 +1325,7 @@ def main():
         barrier()
         s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         s0.record(stream)
+        copy_stream.wait_event(s0)
         for _ in range(e2e_steps):
             e2e_step()
         s1.record(stream)
@@ -1279,8 +1333,12 @@ def main():
         e2e_t = torch.tensor([s0.elapsed_time(s1) / 1e3 / e2e_steps], device=dev, dtype=torch.float64)
         if dist is not None:
             dist.all_reduce(e2e_t, op=dist.ReduceOp.MAX)
-        e2e = {"value": world * B * T * K * V / float(e2e_t.item()), "unit": "candidates/s",
-               "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h}
+        # Decoding in chunks gives the same outputs as the whole-shard decode (examples are independent).
+        for k, v in outs_h.items():
+            if v.numpy().tobytes() != host[k].tobytes():
+                raise RuntimeError(f"e2e: chunked decode output {k} differs from the whole-shard decode")
+        e2e = {"value": global_batch * T * K * V / float(e2e_t.item()), "unit": "candidates/s",
+               "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "chunks": n_chunks}
         del xh, xd
 
     cpu = None
@@ -1297,7 +1355,7 @@ def main():
     if dist is not None:
         dist.barrier()
     if rank == 0:
-        cand = world * B * T * K * V
+        cand = global_batch * T * K * V
         line = {
             "metric": METRIC,
             "value": cand / elapsed * args.steps,
@@ -1307,13 +1365,14 @@ def main():
             "warmup": args.warmup,
             "ms_per_step": elapsed / args.steps * 1e3,
             "higher_is_better": True,
-            "scaling": "weak",
+            "scaling": "strong" if strong else "weak",
             "vs_baseline": None,
             "dtype": "bf16",
             "data": "synthetic",
-            "config": {"workload": workload(), "global_batch": world * B, "seq_len": T, "beam": K, "vocab": V,
-                       "parallelism": f"batch x{world}" if world > 1 else "single GPU",
-                       "l2": f"inputs ({B * T * K * V * 2 / 1e9:.2f} GB per GPU) larger than L2 (126 MB)"},
+            "config": {"workload": workload(), "global_batch": global_batch, "seq_len": T, "beam": K, "vocab": V,
+                       "parallelism": (f"batch-sharded over {world} GPUs, {Bl} examples on rank 0" if strong else
+                                       f"batch x{world}, {B} examples per GPU") if world > 1 else "single GPU",
+                       "l2": f"inputs ({Bl * T * K * V * 2 / 1e9:.2f} GB on rank 0) larger than L2 (126 MB)"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": measured_traffic(), "peak_kind": peak_kind,
                          "alg_bytes_per_launch": alg_bytes, "rows_read": n_rows},
