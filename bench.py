@@ -62,6 +62,8 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-reference-gpu", action="store_true",
+                    help="skip timing the reference's own GPU engine (C2 at N=1)")
     ap.add_argument("--batch", type=int, default=None,
                     help="C2: examples of the whole job (64); C4: examples per GPU (256); smaller only for profiling")
     ap.add_argument("--scaling", default="strong", choices=["strong", "weak"],
@@ -220,6 +222,49 @@ def cpu_reference(x_host_bits: np.ndarray, threads: int, min_seconds: float = 10
             d.decode(threads=threads)
             times.append(time.perf_counter() - t0)
     return statistics.median(times), len(times)
+
+
+def reference_gpu(torch, x, dtype: int, from_logits: bool, a, ours: dict, steps: int, dev, stream):
+    """beamgrad 2.3.0's own GPU engine (cuda/dbs_cuda.cu built for sm_100a, oracle/_ref) on the
+    same device-resident input and arguments `a` through the same C ABI call
+    (dbs_cuda_decode_ex2): candidates/s from the median of per-decode CUDA events, and whether
+    its outputs equal this engine's (`ours`, host copies of the decode outputs)."""
+    from oracle import oracle
+    from beamgrad_b200 import _abi as A
+
+    if not oracle.ref_cuda_available():
+        return {"unavailable": "oracle/_ref/libdbs_cuda_ref.so was not built"}
+    lib = oracle.ref_cuda_lib()
+    fields = {name for name, _ in A.DecodeOutputs._fields_}
+    ours = {k: v for k, v in ours.items() if k in fields}
+    out = {k: torch.empty(v.shape, dtype=torch.from_numpy(v).dtype, device=dev) for k, v in ours.items()}
+    o = A.DecodeOutputs()
+    for k, v in out.items():
+        setattr(o, k, v.data_ptr())
+    nb = lib.dbs_cuda_decode_workspace_size(C.byref(a))
+    ws = torch.empty(max(nb, 1), dtype=torch.uint8, device=dev)
+
+    def decode():
+        A.check(lib.dbs_cuda_decode_ex2(C.c_void_p(x.data_ptr()), dtype, int(from_logits), C.byref(a), None,
+                                        C.byref(o), None, C.c_void_p(ws.data_ptr()), nb,
+                                        C.c_void_p(stream.cuda_stream)), "reference decode")
+
+    decode()
+    torch.cuda.synchronize(dev)
+    same = all(out[k].cpu().numpy().tobytes() == ours[k].tobytes() for k in ours)
+    times = []
+    for _ in range(max(3, min(steps, 10))):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        decode()
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        times.append(e0.elapsed_time(e1) / 1e3)
+    sec = statistics.median(times)
+    cand = a.batch_size * a.steps * a.beam_size * a.vocab_size
+    return {"value": cand / sec, "unit": "candidates/s", "ms_per_step": sec * 1e3,
+            "kind": "beamgrad 2.3.0 cuda/dbs_cuda.cu, unmodified, built for sm_100a (oracle/Makefile)",
+            "matches_this_engine": same, "decodes_timed": len(times)}
 
 
 def run_reference_arm(args, rank: int, world: int):
@@ -481,6 +526,10 @@ def run_c4(args, rank: int, world: int, local: int):
     write_gbs = write_ceiling(torch, grad, stream)
 
     host = {k: v.cpu().numpy() for k, v in out.items()}
+    ref_gpu = None
+    if world == 1 and not args.no_reference_gpu:
+        # The reference engine's decode of the same input (its backward is not timed here).
+        ref_gpu = reference_gpu(torch, x, A.DTYPE_BF16, False, a, host, args.steps, dev, stream)
     live = ((host["parents"][:, :-1] >= 0) & (host["from_logprob"][:, :-1] == 1) &
             (host["tokens"][:, :-1] != C4_EOS) & np.isfinite(host["raw_scores"][:, :-1]))
     n_rows = int(B4 + live.sum())
@@ -559,6 +608,7 @@ def run_c4(args, rank: int, world: int, local: int):
                                                    "frac_of_write_stream": bwd_gbs / write_gbs if write_gbs else None,
                                                    "alg_bytes": bwd_bytes}},
             "cpu_baseline": cpu,
+            "reference_gpu": ref_gpu,
             "e2e": e2e,
             "gpu_launches": args.steps * 4,
             "clocks": clocks.summary(),
@@ -777,6 +827,9 @@ def run_decode_only(args, rank: int, world: int, local: int, spec: Spec):
                "h2d_bytes_per_step": xh.numel() * xh.element_size(),
                "d2h_bytes_per_step": sum(v.numel() * v.element_size() for v in outs_h.values())}
 
+    ref_gpu = None
+    if world == 1 and not args.no_reference_gpu:
+        ref_gpu = reference_gpu(torch, x, dt, spec.from_logits, a, host, args.steps, dev, stream)
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline and oracle.ref_available():
         threads = oracle.cpu_count()
@@ -796,6 +849,7 @@ def run_decode_only(args, rank: int, world: int, local: int, spec: Spec):
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                          "traffic": None, "peak_kind": peak_kind, "alg_bytes_per_launch": alg_bytes},
             "cpu_baseline": cpu,
+            "reference_gpu": ref_gpu,
             "e2e": e2e,
             "gpu_launches": 2 * len(evs),
             "clocks": clocks.summary(),
@@ -1109,6 +1163,16 @@ def run_c5(args, rank: int, world: int, local: int):
                "d2h_bytes_per_step": d2h}
         del xh
 
+    ref_gpu = None
+    if world == 1 and not args.no_reference_gpu:
+        # One shard is the whole vocabulary in token order: the reference engine decodes it as is.
+        from beamgrad_b200 import _abi as A
+
+        a = A.DecodeArgs()
+        a.batch_size, a.steps, a.beam_size, a.vocab_size = B5, T5, K5, V5
+        a.eos_token, a.length_penalty_alpha, a.repetition_penalty = C5_EOS, C5_ALPHA, 1.0
+        host = {("invalid_input" if k == "invalid" else k): v.cpu().numpy() for k, v in d.out.items()}
+        ref_gpu = reference_gpu(torch, x, A.DTYPE_F32, True, a, host, args.steps, dev, stream)
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline and oracle.ref_available():
         threads = oracle.cpu_count()
@@ -1139,6 +1203,7 @@ def run_c5(args, rank: int, world: int, local: int):
                          "traffic": None, "peak_kind": peak_kind, "kernel": "vs_scan_kernel",
                          "alg_bytes_per_launch": scan_bytes},
             "cpu_baseline": cpu,
+            "reference_gpu": ref_gpu,
             "e2e": e2e,
             "gpu_launches": args.steps * (5 + d.rounds * 2),
             "clocks": clocks.summary(),
@@ -1341,6 +1406,10 @@ def main():
                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "chunks": n_chunks}
         del xh, xd
 
+    ref_gpu = None
+    if world == 1 and not args.no_reference_gpu:
+        ref_gpu = reference_gpu(torch, x, A.DTYPE_BF16, True, a, host, args.steps, dev, stream)
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         from oracle import oracle
@@ -1378,6 +1447,7 @@ def main():
                          "alg_bytes_per_launch": alg_bytes, "rows_read": n_rows},
             "roofline_fp32": fp32_roofline(n_rows * V, per_launch, clocks.summary()),
             "cpu_baseline": cpu,
+            "reference_gpu": ref_gpu,
             "e2e": e2e,
             "gpu_launches": 2 * args.steps,
             "clocks": clocks.summary(),

@@ -7,9 +7,11 @@
   (oracle/Makefile); called through its public C ABI (include/dbs.h:
   dbs_create_ex, dbs_set_extra_eos_tokens, dbs_decode_batch_into_ex,
   dbs_backward_batch_into_ex).
+* ``_ref/libdbs_cuda_ref.so`` -- beamgrad 2.3.0's GPU engine (cuda/dbs_cuda.cu) built for
+  sm_100a; called through its include/dbs_cuda.h (the reference GPU speed bar).
 
-Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline / reference
-arms import this module. Inputs are numpy arrays: float32 values, or the raw
+Only tests/, __graft_entry__.smoke() and bench.py's baseline legs (the CPU
+baseline, the reference arm, the reference GPU engine's timing) import this module. Inputs are numpy arrays: float32 values, or the raw
 uint16 bits of float16 / bfloat16 values.
 """
 
@@ -27,6 +29,7 @@ HERE = Path(__file__).resolve().parent
 ROOT = HERE.parent
 ORACLE_LIB = HERE / "liboracle.so"
 REF_LIB = HERE / "_ref" / "libdbs.so"
+REF_CUDA_LIB = HERE / "_ref" / "libdbs_cuda_ref.so"
 
 import sys  # noqa: E402
 
@@ -41,9 +44,20 @@ def _ptr(a):
     return None if a is None else a.ctypes.data_as(_p)
 
 
+def reference_dir() -> Path | None:
+    """The reference source tree (beamgrad 2.3.0): $BEAMGRAD_REF, else a directory named
+    ``reference`` beside this repository; None when neither holds the sources."""
+    for cand in (os.environ.get("BEAMGRAD_REF"), ROOT.parent / "reference"):
+        if cand and (Path(cand) / "src" / "decoder.cpp").exists():
+            return Path(cand)
+    return None
+
+
 def build(verbose: bool = False) -> None:
-    """Compile liboracle.so and, where the reference sources exist, _ref/libdbs.so."""
-    cmd = ["make", "-s", "-C", str(HERE), "all"]
+    """Compile liboracle.so and, where the reference sources exist, _ref/libdbs.so and
+    _ref/libdbs_cuda_ref.so (the reference's own GPU engine, for sm_100a)."""
+    ref = reference_dir()
+    cmd = ["make", "-s", "-C", str(HERE), "all"] + ([f"REF={ref}"] if ref is not None else [])
     out = subprocess.run(cmd, capture_output=True, text=True)
     if out.returncode != 0:
         raise RuntimeError(f"oracle build failed:\n{out.stdout}\n{out.stderr}")
@@ -340,10 +354,32 @@ class _BackwardC(C.Structure):  # DBSBackwardInputsC, include/dbs.h:373-397
 
 
 _rlib = None
+_rclib = None
 
 
 def ref_available() -> bool:
     return REF_LIB.exists()
+
+
+def ref_cuda_available() -> bool:
+    return REF_CUDA_LIB.exists()
+
+
+def ref_cuda_lib() -> C.CDLL:
+    """beamgrad 2.3.0's own GPU engine (cuda/dbs_cuda.cu built for sm_100a by oracle/Makefile),
+    with the 17 entry points of its include/dbs_cuda.h typed like this repository's (the
+    structs are layout-identical). The reference speed bar and a second parity check."""
+    global _rclib
+    if _rclib is None:
+        if not REF_CUDA_LIB.exists():
+            raise FileNotFoundError(f"{REF_CUDA_LIB} was not built (needs the reference sources and nvcc)")
+        lib = C.CDLL(str(REF_CUDA_LIB))
+        for name, (res, args) in A.SIGNATURES.items():
+            fn = getattr(lib, name, None)
+            if fn is not None:
+                fn.restype, fn.argtypes = res, args
+        _rclib = lib
+    return _rclib
 
 
 def ref_lib() -> C.CDLL:

@@ -79,8 +79,11 @@ def _out_struct(o) -> A.DecodeOutputs:
     return s
 
 
-def engine_decode(pb: Problem, use_workspace: bool = True, dp: DeviceProblem | None = None) -> dict[str, np.ndarray]:
-    lib = A.load()
+def engine_decode(pb: Problem, use_workspace: bool = True, dp: DeviceProblem | None = None,
+                  lib=None) -> dict[str, np.ndarray]:
+    """dbs_cuda_decode_ex2 of this repository's engine, or of `lib` (another library with the
+    same C ABI, e.g. the reference's own GPU engine)."""
+    lib = lib or A.load()
     dp = dp or DeviceProblem(pb)
     B, T, K, V = pb.shape
     o = _outputs(B, T, K)

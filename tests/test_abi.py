@@ -18,9 +18,11 @@ from pathlib import Path
 import pytest
 
 from beamgrad_b200 import _abi as A
+from oracle import oracle
 
 ROOT = Path(__file__).resolve().parents[1]
-REF_HEADER = Path("/root/reference/include/dbs_cuda.h")
+_REF = oracle.reference_dir()
+REF_HEADER = _REF / "include" / "dbs_cuda.h" if _REF is not None else Path("reference-header-not-found")
 
 STRUCTS = {
     "DBSCudaDecodeArgs": A.DecodeArgs,
