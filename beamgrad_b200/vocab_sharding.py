@@ -185,13 +185,18 @@ class ShardDecode:
         self.stage("scan")
 
     def stage(self, name: str) -> None:
+        self.timed(name, lambda: self.engine.run(name, self))
+
+    def timed(self, name: str, fn: Callable[[], None]) -> None:
+        """fn() (a device stage or a collective on this rank's stream), between two CUDA events
+        recorded under `name` when timings are enabled."""
         if self.timings is None:
-            self.engine.run(name, self)
+            fn()
             return
         s = torch.cuda.current_stream(self.device)
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(s)
-        self.engine.run(name, self)
+        fn()
         e1.record(s)
         self.timings.setdefault(name, []).append((e0, e1))
 
@@ -276,9 +281,9 @@ def decode_vocab_sharded(shard: torch.Tensor | ShardDecode, vocab_size: int | No
         return decode_vocab_shards([d], validate=validate)
     d.begin()
     if d.from_logits:
-        dist.all_reduce(d.row_max, op=dist.ReduceOp.MAX, group=group)
+        d.timed("allreduce_max", lambda: dist.all_reduce(d.row_max, op=dist.ReduceOp.MAX, group=group))
         d.stage("lanes")
-    _gather(d.exchange_all, d.exchange, group)
+    d.timed("allgather", lambda: _gather(d.exchange_all, d.exchange, group))
     d.stage("merge")
     for _ in range(d.B * d.T + 1):
         d.stage("select")
@@ -288,7 +293,7 @@ def decode_vocab_sharded(shard: torch.Tensor | ShardDecode, vocab_size: int | No
             break
         d.set_rescan(rows)
         d.stage("rescan")
-        _gather(d.rescan_all, d.rescan, group)
+        d.timed("allgather_rescan", lambda: _gather(d.rescan_all, d.rescan, group))
     else:
         raise RuntimeError("vocab-sharded decode: selection made no progress")
     _check_invalid(d, validate)

@@ -1126,6 +1126,15 @@ def run_c5(args, rank: int, world: int, local: int):
     decode()
     stage = d.stage_ms()
     d.timings = None
+    # Every rank's stage times (the collectives included), gathered to rank 0.
+    stage_keys = ("scan", "allreduce_max", "lanes", "allgather", "merge", "select", "rescan", "allgather_rescan")
+    mine = torch.tensor([stage.get(k, 0.0) for k in stage_keys], dtype=torch.float64, device=dev)
+    per_rank = [mine.cpu().tolist()]
+    if dist is not None:
+        parts = [torch.empty_like(mine) for _ in range(world)]
+        dist.all_gather(parts, mine)
+        per_rank = [t.cpu().tolist() for t in parts]
+    stage_per_rank = [{k: round(v, 4) for k, v in zip(stage_keys, r) if k in stage} for r in per_rank]
     Vr = d.plan.shard_vocab
     scan_rows = B5 * (1 + (T5 - 1) * K5)  # rows the search may read: the scan's
     scan_bytes = scan_rows * Vr * 4 + scan_rows * d.plan.row_words * 8
@@ -1198,7 +1207,8 @@ def run_c5(args, rank: int, world: int, local: int):
             "config": {"workload": c5_workload(), "global_batch": B5, "seq_len": T5, "beam": K5, "vocab": V5,
                        "parallelism": f"vocab x{world}" if world > 1 else "single GPU (vocab-shard path, one shard)",
                        "l2": f"inputs ({shard_bytes / 1e9:.2f} GB per GPU) larger than L2 (126 MB)",
-                       "stage_ms": {k: round(v, 4) for k, v in stage.items()}, "rescan_rounds": d.rounds},
+                       "stage_ms": {k: round(v, 4) for k, v in stage.items()}, "rescan_rounds": d.rounds,
+                       "stage_ms_per_rank": stage_per_rank},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                          "traffic": None, "peak_kind": peak_kind, "kernel": "vs_scan_kernel",
                          "alg_bytes_per_launch": scan_bytes},
