@@ -3,11 +3,14 @@
 // The C ABI of libdbs_cuda (include/dbs_cuda.h): argument checks, workspace
 // layout, launches. Every entry point is asynchronous on the caller's stream
 // except where the header says it synchronizes.
+#include <algorithm>
 #include <atomic>
 #include <cmath>
 #include <cstdlib>
 #include <cstring>
+#include <iterator>
 #include <limits>
+#include <memory>
 #include <mutex>
 
 #include "dbs_cuda.h"
@@ -56,49 +59,81 @@ constexpr unsigned long long kTimeoutNs = 20ull * 1000ull * 1000ull * 1000ull;  
 constexpr int kMaxRowSmem = 160 * 1024;  // largest row staged in shared memory
 constexpr int64_t kLanesPerRow = 256;     // logsumexp lanes of a row (the reference's fixed order)
 
+// Synchronous checking: dbs_cuda_set_synchronization(1), or either environment variable set
+// to 1 (include/dbs_cuda.h). The process-wide flag is the only state the library keeps.
 std::atomic<int> g_sync{0};
+constexpr const char* kSyncVariables[] = {"DBS_CUDA_SYNC_CHECK", "DBS_CUDA_DEBUG_SYNC"};
 
 int64_t align_up(int64_t n) { return (n + kAlign - 1) / kAlign * kAlign; }
 
 bool sync_requested() {
-    if (g_sync.load(std::memory_order_relaxed)) return true;
-    const char* a = std::getenv("DBS_CUDA_SYNC_CHECK");
-    const char* b = std::getenv("DBS_CUDA_DEBUG_SYNC");
-    return (a && a[0] == '1') || (b && b[0] == '1');
+    if (g_sync.load(std::memory_order_relaxed) != 0) return true;
+    return std::any_of(std::begin(kSyncVariables), std::end(kSyncVariables), [](const char* name) {
+        const char* v = std::getenv(name);
+        return v != nullptr && v[0] == '1';
+    });
 }
 
-int elem_bytes(int dtype) { return dtype == DBS_CUDA_DTYPE_F32 ? 4 : 2; }
-bool valid_dtype(int d) { return d == DBS_CUDA_DTYPE_F32 || d == DBS_CUDA_DTYPE_F16 || d == DBS_CUDA_DTYPE_BF16; }
+// Element types of inputs and gradients: the header's code and the bytes per element.
+struct DtypeInfo {
+    int code;
+    int bytes;
+};
+constexpr DtypeInfo kDtypes[] = {{DBS_CUDA_DTYPE_F32, 4}, {DBS_CUDA_DTYPE_F16, 2}, {DBS_CUDA_DTYPE_BF16, 2}};
+
+int elem_bytes(int code) {
+    for (const DtypeInfo& d : kDtypes)
+        if (d.code == code) return d.bytes;
+    return 0;
+}
+bool valid_dtype(int code) { return elem_bytes(code) > 0; }
 
 bool has_per_example(const DBSCudaDecodeArgs& a) {
-    return a.steps_per_example || a.beam_sizes_per_example || a.eos_tokens_per_example || a.min_lengths_per_example;
+    const void* arrays[] = {a.steps_per_example, a.beam_sizes_per_example, a.eos_tokens_per_example,
+                            a.min_lengths_per_example};
+    return std::any_of(std::begin(arrays), std::end(arrays), [](const void* q) { return q != nullptr; });
 }
 bool constrained(const DBSCudaDecodeArgs& a) { return a.no_repeat_ngram_size > 0 || a.repetition_penalty > 1.0f; }
 
+// The problems the engine accepts (include/dbs_cuda.h), one predicate per rule.
+using ArgRule = bool (*)(const DBSCudaDecodeArgs&);
+constexpr ArgRule kArgRules[] = {
+    [](const DBSCudaDecodeArgs& a) { return a.batch_size > 0 && a.steps > 0 && a.beam_size > 0 && a.vocab_size > 0; },
+    [](const DBSCudaDecodeArgs& a) { return a.beam_size <= DBS_CUDA_MAX_BEAM; },
+    [](const DBSCudaDecodeArgs& a) { return a.eos_token >= -1 && a.eos_token < a.vocab_size; },
+    [](const DBSCudaDecodeArgs& a) { return a.min_length >= 0 && a.reserved0 == 0; },
+    [](const DBSCudaDecodeArgs& a) { return std::isfinite(a.length_penalty_alpha) && a.length_penalty_alpha >= 0.0f; },
+    [](const DBSCudaDecodeArgs& a) { return std::isfinite(a.repetition_penalty) && a.repetition_penalty >= 0.0f; },
+    // A candidate's index parent * V + token is a 32-bit key field.
+    [](const DBSCudaDecodeArgs& a) {
+        return static_cast<int64_t>(a.beam_size) * a.vocab_size <= std::numeric_limits<int32_t>::max();
+    },
+    // Row tickets (B * K * T of them) are counted in 31 bits.
+    [](const DBSCudaDecodeArgs& a) {
+        return static_cast<int64_t>(a.batch_size) * a.beam_size * a.steps <= (int64_t{1} << 31);
+    },
+    [](const DBSCudaDecodeArgs& a) {
+        return static_cast<double>(a.batch_size) * a.steps * a.beam_size * a.vocab_size < 9.0e18;
+    },
+};
+
 bool valid_args(const DBSCudaDecodeArgs* a) {
-    if (!a) return false;
-    if (a->batch_size <= 0 || a->steps <= 0 || a->beam_size <= 0 || a->vocab_size <= 0) return false;
-    if (a->beam_size > DBS_CUDA_MAX_BEAM) return false;
-    if (a->eos_token < -1 || a->eos_token >= a->vocab_size) return false;
-    if (a->min_length < 0 || a->reserved0 != 0) return false;
-    if (!std::isfinite(a->length_penalty_alpha) || a->length_penalty_alpha < 0.0f) return false;
-    if (!std::isfinite(a->repetition_penalty) || a->repetition_penalty < 0.0f) return false;
-    // Candidate indices parent * V + token fit in 32 bits (keys), tickets B*K*T fit in 31 bits.
-    const int64_t cand = static_cast<int64_t>(a->beam_size) * a->vocab_size;
-    if (cand > std::numeric_limits<int32_t>::max()) return false;
-    const int64_t tickets = static_cast<int64_t>(a->batch_size) * a->beam_size * a->steps;
-    if (tickets > (int64_t{1} << 31)) return false;
-    const double elems = static_cast<double>(a->batch_size) * a->steps * a->beam_size * a->vocab_size;
-    return elems < 9.0e18;
+    return a != nullptr &&
+           std::all_of(std::begin(kArgRules), std::end(kArgRules), [a](ArgRule rule) { return rule(*a); });
 }
 
+// Search options: reserved fields zero, at most DBS_CUDA_MAX_EXTRA_EOS extra EOS tokens, each
+// inside the vocabulary, and only with EOS handling on.
 bool valid_options(const DBSCudaSearchOptions* o, const DBSCudaDecodeArgs& a) {
-    if (!o) return true;
-    if (o->reserved0 != 0 || o->reserved[0] || o->reserved[1] || o->reserved[2] || o->reserved[3]) return false;
-    if (o->extra_eos_count < 0 || o->extra_eos_count > DBS_CUDA_MAX_EXTRA_EOS) return false;
-    for (int i = 0; i < o->extra_eos_count; ++i)
-        if (o->extra_eos_tokens[i] < 0 || o->extra_eos_tokens[i] >= a.vocab_size) return false;
-    return o->extra_eos_count == 0 || a.eos_token >= 0 || a.eos_tokens_per_example;
+    if (o == nullptr) return true;
+    if (o->reserved0 != 0) return false;
+    if (std::any_of(std::begin(o->reserved), std::end(o->reserved), [](const void* r) { return r != nullptr; }))
+        return false;
+    const int n = o->extra_eos_count;
+    if (n < 0 || n > DBS_CUDA_MAX_EXTRA_EOS) return false;
+    const bool inside = std::all_of(o->extra_eos_tokens, o->extra_eos_tokens + n,
+                                    [&a](int32_t tok) { return tok >= 0 && tok < a.vocab_size; });
+    return inside && (n == 0 || a.eos_token >= 0 || a.eos_tokens_per_example != nullptr);
 }
 
 // Largest row-record area of a chained decode; larger decodes use the waiting kernel.
@@ -164,41 +199,44 @@ DecodeLayout make_layout(const DBSCudaDecodeArgs& a, bool step_api, bool force_c
     return L;
 }
 
-// Scratch owned for the duration of one call when the caller passed none.
-class Scratch {
-public:
-    Scratch(void* user, int64_t user_bytes, int64_t need, cudaStream_t s) : stream_(s) {
-        if (user) {
-            ptr_ = static_cast<char*>(user);
-            status_ = user_bytes >= need ? DBS_CUDA_STATUS_OK : DBS_CUDA_STATUS_INVALID_ARGUMENT;
-            return;
-        }
-        void* p = nullptr;
-        if (cudaMallocAsync(&p, static_cast<size_t>(need > 0 ? need : 1), s) != cudaSuccess) {
-            cudaGetLastError();
-            status_ = DBS_CUDA_STATUS_OUT_OF_MEMORY;
-            return;
-        }
-        ptr_ = static_cast<char*>(p);
-        owned_ = true;
+// The memory one call works in: the caller's workspace (rejected when smaller than the
+// layout needs), or, when the caller passed none, a stream-ordered allocation on the call's
+// stream that is released (also stream-ordered) when the call returns.
+struct StreamOrderedFree {
+    cudaStream_t stream;
+    void operator()(char* p) const {
+        if (p != nullptr) cudaFreeAsync(p, stream);
     }
-    ~Scratch() {
-        if (owned_) cudaFreeAsync(ptr_, stream_);
-    }
-    Scratch(const Scratch&) = delete;
-    Scratch& operator=(const Scratch&) = delete;
-    int status() const { return status_; }
+};
+
+struct WorkArea {
+    std::unique_ptr<char, StreamOrderedFree> owned;
+    char* base = nullptr;
+    int status = DBS_CUDA_STATUS_OK;
+    // The sub-buffer at byte offset `off` of the layout (-1: not in this layout).
     template <class T>
     T* at(int64_t off) const {
-        return off < 0 ? nullptr : reinterpret_cast<T*>(ptr_ + off);
+        return off < 0 ? nullptr : reinterpret_cast<T*>(base + off);
     }
-
-private:
-    cudaStream_t stream_;
-    char* ptr_ = nullptr;
-    bool owned_ = false;
-    int status_ = DBS_CUDA_STATUS_OK;
 };
+
+WorkArea work_area(void* caller, int64_t caller_bytes, int64_t need, cudaStream_t stream) {
+    WorkArea w{std::unique_ptr<char, StreamOrderedFree>(nullptr, StreamOrderedFree{stream})};
+    if (caller != nullptr) {
+        w.base = static_cast<char*>(caller);
+        w.status = caller_bytes >= need ? DBS_CUDA_STATUS_OK : DBS_CUDA_STATUS_INVALID_ARGUMENT;
+        return w;
+    }
+    void* p = nullptr;
+    if (cudaMallocAsync(&p, static_cast<size_t>(std::max<int64_t>(need, 1)), stream) != cudaSuccess) {
+        cudaGetLastError();  // clear the sticky-free error so later calls are not blamed for it
+        w.status = DBS_CUDA_STATUS_OUT_OF_MEMORY;
+        return w;
+    }
+    w.owned.reset(static_cast<char*>(p));
+    w.base = w.owned.get();
+    return w;
+}
 
 int sm_count_of_current_device() {
     static std::mutex mu;
@@ -214,20 +252,18 @@ int sm_count_of_current_device() {
     return n;
 }
 
-// End of a call: launch errors, then (debug) a synchronizing check of the
-// stream and of the engine's error word.
-int finish(cudaStream_t stream, const int32_t* error_word) {
+// The status a call returns once its work is enqueued: LAUNCH_FAILED when a launch failed;
+// with synchronous checking also when the stream reports an error or a kernel recorded one
+// in the engine's error word (a bounded wait that gave up).
+int close_call(cudaStream_t stream, const int32_t* error_word) {
     if (cudaGetLastError() != cudaSuccess) return DBS_CUDA_STATUS_LAUNCH_FAILED;
-    if (sync_requested()) {
-        if (cudaStreamSynchronize(stream) != cudaSuccess) return DBS_CUDA_STATUS_LAUNCH_FAILED;
-        if (error_word) {
-            int32_t e = 0;
-            if (cudaMemcpy(&e, error_word, sizeof e, cudaMemcpyDeviceToHost) != cudaSuccess) return DBS_CUDA_STATUS_LAUNCH_FAILED;
-            if (e != 0) return DBS_CUDA_STATUS_LAUNCH_FAILED;
-        }
-        if (cudaGetLastError() != cudaSuccess) return DBS_CUDA_STATUS_LAUNCH_FAILED;
-    }
-    return DBS_CUDA_STATUS_OK;
+    if (!sync_requested()) return DBS_CUDA_STATUS_OK;
+    int32_t recorded = 0;
+    bool fine = cudaStreamSynchronize(stream) == cudaSuccess;
+    if (fine && error_word != nullptr)
+        fine = cudaMemcpy(&recorded, error_word, sizeof recorded, cudaMemcpyDeviceToHost) == cudaSuccess;
+    fine = fine && cudaGetLastError() == cudaSuccess && recorded == 0;
+    return fine ? DBS_CUDA_STATUS_OK : DBS_CUDA_STATUS_LAUNCH_FAILED;
 }
 
 void fill_params(DecodeParams& p, const DBSCudaDecodeArgs& a, const DBSCudaSearchOptions* o) {
@@ -287,8 +323,8 @@ int run_decode(const void* inputs, int dtype, int from_logits, const DBSCudaDeco
     if (!valid_options(options, *args)) return DBS_CUDA_STATUS_INVALID_ARGUMENT;
     const DBSCudaDecodeArgs& a = *args;
     const DecodeLayout L = make_layout(a, false);
-    Scratch ws(workspace, workspace_bytes, L.total, stream);
-    if (ws.status() != DBS_CUDA_STATUS_OK) return ws.status();
+    const WorkArea ws = work_area(workspace, workspace_bytes, L.total, stream);
+    if (ws.status != DBS_CUDA_STATUS_OK) return ws.status;
     DecodeParams p;
     fill_params(p, a, options);
     p.inputs = inputs;
@@ -321,7 +357,7 @@ int run_decode(const void* inputs, int dtype, int from_logits, const DBSCudaDeco
     if (launch_decode(p, dtype, from_logits != 0, stream, sm_count_of_current_device()) != cudaSuccess) {
         return DBS_CUDA_STATUS_LAUNCH_FAILED;
     }
-    return finish(stream, p.error);
+    return close_call(stream, p.error);
 }
 
 int run_step(const void* inputs, int dtype, int from_logits, const DBSCudaDecodeArgs* args,
@@ -336,8 +372,8 @@ int run_step(const void* inputs, int dtype, int from_logits, const DBSCudaDecode
     }
     if (constrained(a) && state->prefix_stride > 0 && !state->prefixes) return DBS_CUDA_STATUS_INVALID_ARGUMENT;
     const DecodeLayout L = make_layout(a, true);
-    Scratch ws(workspace, workspace_bytes, L.total, stream);
-    if (ws.status() != DBS_CUDA_STATUS_OK) return ws.status();
+    const WorkArea ws = work_area(workspace, workspace_bytes, L.total, stream);
+    if (ws.status != DBS_CUDA_STATUS_OK) return ws.status;
     DecodeParams p;
     fill_params(p, a, options);
     p.inputs = inputs;
@@ -368,7 +404,7 @@ int run_step(const void* inputs, int dtype, int from_logits, const DBSCudaDecode
     if (launch_decode(p, dtype, from_logits != 0, stream, sm_count_of_current_device()) != cudaSuccess) {
         return DBS_CUDA_STATUS_LAUNCH_FAILED;
     }
-    return finish(stream, p.error);
+    return close_call(stream, p.error);
 }
 
 int64_t backward_ws_bytes(const DBSCudaDecodeArgs& a) {
@@ -518,15 +554,23 @@ DBS_CUDA_EXPORT int dbs_cuda_available(void) {
     return ok ? 1 : 0;
 }
 
+// Status texts (include/dbs_cuda.h: the same text for each code as beamgrad's library).
+struct StatusText {
+    int status;
+    const char* text;
+};
+constexpr StatusText kStatusTexts[] = {
+    {DBS_CUDA_STATUS_OK, "ok"},
+    {DBS_CUDA_STATUS_UNAVAILABLE, "CUDA backend unavailable"},
+    {DBS_CUDA_STATUS_INVALID_ARGUMENT, "invalid argument"},
+    {DBS_CUDA_STATUS_LAUNCH_FAILED, "CUDA launch failed"},
+    {DBS_CUDA_STATUS_OUT_OF_MEMORY, "CUDA out of memory"},
+};
+
 DBS_CUDA_EXPORT const char* dbs_cuda_status_string(int status) {
-    switch (status) {
-        case DBS_CUDA_STATUS_OK: return "ok";
-        case DBS_CUDA_STATUS_UNAVAILABLE: return "CUDA backend unavailable";
-        case DBS_CUDA_STATUS_INVALID_ARGUMENT: return "invalid argument";
-        case DBS_CUDA_STATUS_LAUNCH_FAILED: return "CUDA launch failed";
-        case DBS_CUDA_STATUS_OUT_OF_MEMORY: return "CUDA out of memory";
-        default: return "unknown CUDA status";
-    }
+    for (const StatusText& e : kStatusTexts)
+        if (e.status == status) return e.text;
+    return "unknown CUDA status";
 }
 
 DBS_CUDA_EXPORT int dbs_cuda_set_synchronization(int synchronize) {
@@ -618,10 +662,10 @@ DBS_CUDA_EXPORT int dbs_cuda_backward_ex(const DBSCudaDecodeArgs* args, const DB
     if (!in->logits) {
         p.grad = grad_inputs;
         if (launch_backward(p, stream) != cudaSuccess) return DBS_CUDA_STATUS_LAUNCH_FAILED;
-        return finish(stream, nullptr);
+        return close_call(stream, nullptr);
     }
-    Scratch ws(workspace, workspace_bytes, backward_ws_bytes(a), stream);
-    if (ws.status() != DBS_CUDA_STATUS_OK) return ws.status();
+    const WorkArea ws = work_area(workspace, workspace_bytes, backward_ws_bytes(a), stream);
+    if (ws.status != DBS_CUDA_STATUS_OK) return ws.status;
     p.draws = ws.at<float>(0);
     const size_t slots = static_cast<size_t>(a.batch_size) * a.steps * a.beam_size;
     if (cudaMemsetAsync(p.draws, 0, slots * sizeof(float), stream) != cudaSuccess) return DBS_CUDA_STATUS_LAUNCH_FAILED;
@@ -630,7 +674,7 @@ DBS_CUDA_EXPORT int dbs_cuda_backward_ex(const DBSCudaDecodeArgs* args, const DB
     if (launch_logit_correction(p, in->logits_type, in->logits, in->row_lse, stream) != cudaSuccess) {
         return DBS_CUDA_STATUS_LAUNCH_FAILED;
     }
-    return finish(stream, nullptr);
+    return close_call(stream, nullptr);
 }
 
 // The dense gradient of dbs_cuda_backward_dense, with the selected-beam weights term when
@@ -658,8 +702,8 @@ static int backward_dense(const DBSCudaDecodeArgs* args, const DBSCudaBackwardIn
     p.w_sel = w_sel;
     p.g_wsel = g_wsel;
     p.sel_temp = sel_temp;
-    Scratch ws(workspace, workspace_bytes, backward_ws_bytes(a), stream);
-    if (ws.status() != DBS_CUDA_STATUS_OK) return ws.status();
+    const WorkArea ws = work_area(workspace, workspace_bytes, backward_ws_bytes(a), stream);
+    if (ws.status != DBS_CUDA_STATUS_OK) return ws.status;
     p.draws = ws.at<float>(0);
     const size_t slots = static_cast<size_t>(a.batch_size) * a.steps * a.beam_size;
     if (cudaMemsetAsync(p.draws, 0, slots * sizeof(float), stream) != cudaSuccess) return DBS_CUDA_STATUS_LAUNCH_FAILED;
@@ -670,7 +714,7 @@ static int backward_dense(const DBSCudaDecodeArgs* args, const DBSCudaBackwardIn
                           sm_count_of_current_device(), stream) != cudaSuccess) {
         return DBS_CUDA_STATUS_LAUNCH_FAILED;
     }
-    return finish(stream, nullptr);
+    return close_call(stream, nullptr);
 }
 
 DBS_CUDA_EXPORT int dbs_cuda_backward_dense(const DBSCudaDecodeArgs* args, const DBSCudaBackwardInputs* in,
@@ -700,7 +744,7 @@ DBS_CUDA_EXPORT int dbs_cuda_selected_weights(const DBSCudaDecodeArgs* args, con
     if (launch_selected_weights(rows, args->beam_size, scores, temperature, weights, stream) != cudaSuccess) {
         return DBS_CUDA_STATUS_LAUNCH_FAILED;
     }
-    return finish(stream, nullptr);
+    return close_call(stream, nullptr);
 }
 
 DBS_CUDA_EXPORT int dbs_cuda_b200_wait_selftest(int64_t timeout_ns, int32_t* words, void* stream_ptr) {
@@ -738,7 +782,7 @@ DBS_CUDA_EXPORT int dbs_cuda_advance_prefixes(int batch_size, int beam_size, int
                                 stream) != cudaSuccess) {
         return DBS_CUDA_STATUS_LAUNCH_FAILED;
     }
-    return finish(stream, nullptr);
+    return close_call(stream, nullptr);
 }
 
 DBS_CUDA_EXPORT int dbs_cuda_backward(const DBSCudaDecodeArgs* args, const int32_t* parents, const int32_t* tokens,
@@ -766,7 +810,7 @@ DBS_CUDA_EXPORT int dbs_cuda_length_penalty(const int32_t* lengths, int64_t coun
     if (count == 0) return DBS_CUDA_STATUS_OK;
     cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
     if (launch_length_penalty(lengths, count, alpha, out, stream) != cudaSuccess) return DBS_CUDA_STATUS_LAUNCH_FAILED;
-    return finish(stream, nullptr);
+    return close_call(stream, nullptr);
 }
 
 DBS_CUDA_EXPORT int dbs_cuda_path_gradient(const DBSCudaDecodeArgs* args, const int32_t* parents,
@@ -787,7 +831,7 @@ DBS_CUDA_EXPORT int dbs_cuda_path_gradient(const DBSCudaDecodeArgs* args, const 
     p.g_final = grad_final_scores;
     p.draws = draws;
     if (launch_backward(p, stream) != cudaSuccess) return DBS_CUDA_STATUS_LAUNCH_FAILED;
-    return finish(stream, nullptr);
+    return close_call(stream, nullptr);
 }
 
 // ---------------------------------------------------------------------------
@@ -803,7 +847,7 @@ DBS_CUDA_EXPORT int dbs_cuda_backtrack(const DBSCudaDecodeArgs* args, const int3
         cudaSuccess) {
         return DBS_CUDA_STATUS_LAUNCH_FAILED;
     }
-    return finish(stream, nullptr);
+    return close_call(stream, nullptr);
 }
 
 DBS_CUDA_EXPORT int dbs_cuda_b200_abi_version(void) { return DBS_CUDA_B200_ABI_VERSION; }
@@ -834,7 +878,7 @@ DBS_CUDA_EXPORT int dbs_cuda_vshard_scan(const DBSCudaVocabShardCall* call, void
         launch_vshard_scan(q, call->data_type, stream, sm_count_of_current_device()) != cudaSuccess) {
         return DBS_CUDA_STATUS_LAUNCH_FAILED;
     }
-    return finish(stream, q.d.error);
+    return close_call(stream, q.d.error);
 }
 
 DBS_CUDA_EXPORT int dbs_cuda_vshard_lanes(const DBSCudaVocabShardCall* call, void* stream_ptr) {
@@ -846,7 +890,7 @@ DBS_CUDA_EXPORT int dbs_cuda_vshard_lanes(const DBSCudaVocabShardCall* call, voi
     if (launch_vshard_lanes(q, call->data_type, stream, sm_count_of_current_device()) != cudaSuccess) {
         return DBS_CUDA_STATUS_LAUNCH_FAILED;
     }
-    return finish(stream, q.d.error);
+    return close_call(stream, q.d.error);
 }
 
 DBS_CUDA_EXPORT int dbs_cuda_vshard_merge(const DBSCudaVocabShardCall* call, void* stream_ptr) {
@@ -857,7 +901,7 @@ DBS_CUDA_EXPORT int dbs_cuda_vshard_merge(const DBSCudaVocabShardCall* call, voi
     if (launch_vshard_merge(q, call->from_logits != 0, stream, sm_count_of_current_device()) != cudaSuccess) {
         return DBS_CUDA_STATUS_LAUNCH_FAILED;
     }
-    return finish(stream, q.d.error);
+    return close_call(stream, q.d.error);
 }
 
 DBS_CUDA_EXPORT int dbs_cuda_vshard_select(const DBSCudaVocabShardCall* call, void* stream_ptr) {
@@ -867,7 +911,7 @@ DBS_CUDA_EXPORT int dbs_cuda_vshard_select(const DBSCudaVocabShardCall* call, vo
     if (!call->outputs.final_scores) return DBS_CUDA_STATUS_INVALID_ARGUMENT;
     cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
     if (launch_vshard_select(q, call->from_logits != 0, stream) != cudaSuccess) return DBS_CUDA_STATUS_LAUNCH_FAILED;
-    return finish(stream, q.d.error);
+    return close_call(stream, q.d.error);
 }
 
 DBS_CUDA_EXPORT int dbs_cuda_vshard_rescan(const DBSCudaVocabShardCall* call, void* stream_ptr) {
@@ -879,7 +923,7 @@ DBS_CUDA_EXPORT int dbs_cuda_vshard_rescan(const DBSCudaVocabShardCall* call, vo
         cudaSuccess) {
         return DBS_CUDA_STATUS_LAUNCH_FAILED;
     }
-    return finish(stream, q.d.error);
+    return close_call(stream, q.d.error);
 }
 
 }  // extern "C"
