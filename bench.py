@@ -64,6 +64,10 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-reference-gpu", action="store_true",
                     help="skip timing the reference's own GPU engine (C2 at N=1)")
+    ap.add_argument("--with-backward", action="store_true",
+                    help="C2: also time the dense bf16 input gradient of the decode (a stage of its own)")
+    ap.add_argument("--c5-path", default="sharded", choices=["sharded", "chained"],
+                    help="C5 on one GPU: the vocabulary-shard stages (default) or the single-GPU chained decode")
     ap.add_argument("--batch", type=int, default=None,
                     help="C2: examples of the whole job (64); C4: examples per GPU (256); smaller only for profiling")
     ap.add_argument("--scaling", default="strong", choices=["strong", "weak"],
@@ -72,9 +76,15 @@ def parse():
     ap.add_argument("--seq", type=int, default=128, help="decode steps T (C2: 128); smaller only for profiling")
     ap.add_argument("--workload", default="c2", choices=["c1", "c2", "c3", "c4", "c5", "search"])
     args = ap.parse_args()
-    global B, T, C4
+    global B, T, C4, C5
     if args.workload == "c4" and args.batch is not None:
         C4 = (args.batch,) + C4[1:]
+    if args.workload == "c5" and args.batch is not None:
+        C5 = (args.batch,) + C5[1:]
+    if args.workload in ("c1", "c3") and args.batch is not None:
+        spec = SPECS[args.workload]
+        spec.shape = (args.batch,) + spec.shape[1:]
+        spec.name += "-shaped (reduced batch, profiling only)"
     if args.workload in ("c1", "c3", "c4", "c5", "search"):
         return args
     B, T = args.batch if args.batch is not None else 64, args.seq
@@ -993,7 +1003,8 @@ C5_EOS, C5_ALPHA = 1, 0.6
 
 def c5_workload() -> str:
     B5, T5, K5, V5 = C5
-    return (f"C5: fp32 logits [{B5},{T5},{K5},{V5}] N(0,2)+Zipf(1.1) bias, from_logits, eos={C5_EOS}, "
+    tag = "C5" if B5 == 16 else "C5-shaped (reduced batch, profiling only)"
+    return (f"{tag}: fp32 logits [{B5},{T5},{K5},{V5}] N(0,2)+Zipf(1.1) bias, from_logits, eos={C5_EOS}, "
             f"alpha={C5_ALPHA}, vocabulary lane-interleaved over the ranks")
 
 
@@ -1035,6 +1046,64 @@ def c5_cpu_reference(torch, device, threads: int, n_examples: int = 1):
     return n_examples * T5 * K5 * V5 / sec, f"{n_examples} example(s) of C5 (full vocabulary), median of 3 runs"
 
 
+def run_c5_chained(args, world: int, local: int):
+    """C5 on one GPU through dbs_cuda_decode_ex2 (the chained decode for beams above 16,
+    decode_chain_wide_kernel): median of per-decode CUDA events."""
+    import torch
+
+    from beamgrad_b200 import _abi as A
+
+    if world != 1:
+        raise SystemExit("--c5-path chained runs on one GPU")
+    B5, T5, K5, V5 = C5
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    lib = A.load()
+    x = c5_shard(torch, 1, 0, dev)  # one shard: the whole vocabulary in token order
+    f32, i32, u8 = torch.float32, torch.int32, torch.uint8
+    out = {n: torch.empty(sh, dtype=dt, device=dev) for n, sh, dt in (
+        ("final_scores", (B5, K5), f32), ("final_raw_scores", (B5, K5), f32), ("final_lengths", (B5, K5), i32),
+        ("tokens", (B5, T5, K5), i32), ("parents", (B5, T5, K5), i32), ("lengths", (B5, T5, K5), i32),
+        ("scores", (B5, T5, K5), f32), ("raw_scores", (B5, T5, K5), f32), ("from_logprob", (B5, T5, K5), u8),
+        ("invalid_input", (B5,), u8))}
+    o = A.DecodeOutputs()
+    for k, v in out.items():
+        setattr(o, k, v.data_ptr())
+    a = A.DecodeArgs()
+    a.batch_size, a.steps, a.beam_size, a.vocab_size = B5, T5, K5, V5
+    a.eos_token, a.length_penalty_alpha, a.repetition_penalty = C5_EOS, C5_ALPHA, 1.0
+    nb = lib.dbs_cuda_decode_workspace_size(C.byref(a))
+    ws = torch.empty(nb, dtype=u8, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def decode():
+        A.check(lib.dbs_cuda_decode_ex2(C.c_void_p(x.data_ptr()), A.DTYPE_F32, 1, C.byref(a), None, C.byref(o), None,
+                                        C.c_void_p(ws.data_ptr()), nb, C.c_void_p(stream.cuda_stream)), "decode")
+
+    for _ in range(args.warmup):
+        decode()
+    torch.cuda.synchronize(dev)
+    times = []
+    for _ in range(args.steps):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        decode()
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        times.append(e0.elapsed_time(e1) / 1e3)
+    sec = statistics.median(times)
+    cand = B5 * T5 * K5 * V5
+    print(json.dumps({
+        "metric": METRIC, "value": cand / sec, "unit": "candidates/s", "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": sec * 1e3, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": c5_workload() + "; one GPU, chained decode (decode_chain_wide_kernel)",
+                   "global_batch": B5, "seq_len": T5, "beam": K5, "vocab": V5, "parallelism": "single GPU",
+                   "timing": "median of per-decode CUDA events"},
+        "gpu_launches": 2 * args.steps,
+    }), flush=True)
+
+
 def run_c5(args, rank: int, world: int, local: int):
     import torch
 
@@ -1070,6 +1139,8 @@ def run_c5(args, rank: int, world: int, local: int):
 
     from beamgrad_b200 import vocab_sharding as vs
 
+    if args.c5_path == "chained":
+        return run_c5_chained(args, world, local)
     torch.cuda.set_device(local)
     dist = None
     if world > 1:
@@ -1349,6 +1420,76 @@ def main():
     peak, peak_kind = peaks()
     achieved = alg_bytes / per_launch / 1e9
 
+    # --with-backward: the dense bf16 input gradient of the decode, written once by
+    # dbs_cuda_backward_dense (from logits: every row with a path gradient gets its softmax
+    # correction, every other entry 0), upstream gradient linspace(-1, 1) over the beams.
+    backward = None
+    if args.with_backward:
+        g_final = torch.linspace(-1.0, 1.0, K, device=dev).repeat(Bl, 1).contiguous()
+        bi = A.BackwardInputs()
+        bi.parents, bi.tokens = out["parents"].data_ptr(), out["tokens"].data_ptr()
+        bi.lengths, bi.from_logprob = out["lengths"].data_ptr(), out["from_logprob"].data_ptr()
+        bi.grad_final_scores = g_final.data_ptr()
+        bi.logits, bi.logits_type, bi.row_lse = x.data_ptr(), A.DTYPE_BF16, row_lse.data_ptr()
+        bws = lib.dbs_cuda_backward_workspace_size(C.byref(a))
+        bw = torch.empty(max(bws, 1), dtype=torch.uint8, device=dev)
+        grad = torch.empty_like(x)
+
+        def backward_dense():
+            A.check(lib.dbs_cuda_backward_dense(C.byref(a), C.byref(bi), C.c_void_p(grad.data_ptr()), A.DTYPE_BF16,
+                                                C.c_void_p(bw.data_ptr()), bws, C.c_void_p(stream.cuda_stream)),
+                    "backward")
+
+        for _ in range(2):
+            backward_dense()
+        bt = []
+        for _ in range(max(3, min(args.steps, 10))):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            backward_dense()
+            e1.record(stream)
+            torch.cuda.synchronize(dev)
+            bt.append(e0.elapsed_time(e1) / 1e3)
+        bsec = statistics.median(bt)
+        # Written: the whole gradient; read: the logits rows with a path gradient, i.e. the rows
+        # (b, t, parent) along the final beams' backtracked paths (beams share prefixes).
+        par, flp = host["parents"], host["from_logprob"]
+        grad_rows = set()
+        for b in range(Bl):
+            slots = list(range(K))
+            for t in range(T - 1, -1, -1):
+                nxt = []
+                for k in slots:
+                    pk = int(par[b, t, k])
+                    if pk < 0:
+                        continue
+                    if flp[b, t, k]:  # a token read from row (b, t, parent); carried-forward slots read none
+                        grad_rows.add((b, t, pk))
+                    nxt.append(pk)
+                slots = sorted(set(nxt))
+        bbytes = grad.numel() * grad.element_size() + len(grad_rows) * V * 2
+        backward = {"ms": bsec * 1e3, "alg_bytes": bbytes, "rows_with_path_gradient": len(grad_rows),
+                    "achieved_gbs": bbytes / bsec / 1e9, "frac": bbytes / bsec / 1e9 / peak,
+                    "kernel": "backward_kernel + dense_grad_kernel (dbs_cuda_backward_dense, bf16)"}
+        del grad
+        # The reference-compatible form: += into a zeroed float32 gradient (dbs_cuda_backward_ex:
+        # backward_kernel, then logit_correction_kernel over the rows with a path gradient).
+        g32 = torch.zeros(x.shape, dtype=torch.float32, device=dev)
+        ex_t = []
+        for i in range(4):
+            g32.zero_()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            A.check(lib.dbs_cuda_backward_ex(C.byref(a), C.byref(bi), C.c_void_p(g32.data_ptr()),
+                                             C.c_void_p(bw.data_ptr()), bws, C.c_void_p(stream.cuda_stream)),
+                    "backward_ex")
+            e1.record(stream)
+            torch.cuda.synchronize(dev)
+            if i:
+                ex_t.append(e0.elapsed_time(e1) / 1e3)
+        backward["backward_ex_f32_ms"] = statistics.median(ex_t) * 1e3
+        del g32
+
     # End to end through the same C-ABI call: pinned host input -> device, decode, outputs -> host.
     # The rank's examples go in chunks: chunk c's copy (on a copy stream) overlaps the decode of
     # chunk c - 1 (dbs_cuda_decode_ex2 on that chunk's slices of the inputs and outputs).
@@ -1458,6 +1599,7 @@ def main():
             "roofline_fp32": fp32_roofline(n_rows * V, per_launch, clocks.summary()),
             "cpu_baseline": cpu,
             "reference_gpu": ref_gpu,
+            "backward": backward,
             "e2e": e2e,
             "gpu_launches": 2 * args.steps,
             "clocks": clocks.summary(),
