@@ -165,6 +165,42 @@ class VocabShardCall(C.Structure):
     ]
 
 
+class PoolOutputs(C.Structure):
+    """DBSCudaPoolOutputs."""
+
+    _fields_ = [
+        ("parents", _p),
+        ("tokens", _p),
+        ("lengths", _p),
+        ("scores", _p),
+        ("raw_scores", _p),
+        ("from_logprob", _p),
+        ("relaxed_weights", _p),
+        ("reserved", _p * 4),
+    ]
+
+
+class PoolGradients(C.Structure):
+    """DBSCudaPoolGradients."""
+
+    _fields_ = [
+        ("pool_size", C.c_int32),
+        ("reserved0", C.c_int32),
+        ("parents", _p),
+        ("tokens", _p),
+        ("lengths", _p),
+        ("from_logprob", _p),
+        ("relaxed_weights", _p),
+        ("grad_relaxed_weights", _p),
+        ("grad_pool_scores", _p),
+        ("grad_pool_raw_scores", _p),
+        ("soft_topk_temperature", C.c_float),
+        ("reserved", _p * 4),
+    ]
+
+
+MAX_POOL = 1024  # DBS_CUDA_B200_MAX_POOL
+
 VSHARD_MAX_WORLD = 8
 
 # name -> (restype, argtypes). The 17 reference entry points, then this engine's additions.
@@ -238,13 +274,20 @@ SIGNATURES = {
     "dbs_cuda_vshard_merge": (C.c_int, [C.POINTER(VocabShardCall), _p]),
     "dbs_cuda_vshard_select": (C.c_int, [C.POINTER(VocabShardCall), _p]),
     "dbs_cuda_vshard_rescan": (C.c_int, [C.POINTER(VocabShardCall), _p]),
+    "dbs_cuda_relaxed_pool": (
+        C.c_int,
+        [_p, C.c_int, C.c_int, C.POINTER(DecodeArgs), C.POINTER(DecodeOutputs), _p, C.c_int, C.c_float, C.c_float,
+         C.c_int, C.POINTER(PoolOutputs), _p],
+    ),
+    "dbs_cuda_backward_pool": (
+        C.c_int, [C.POINTER(DecodeArgs), C.POINTER(BackwardInputs), C.POINTER(PoolGradients), _p, _p]),
 }
 
 VSHARD_SYMBOLS = ("dbs_cuda_vshard_plan", "dbs_cuda_vshard_scan", "dbs_cuda_vshard_lanes", "dbs_cuda_vshard_merge",
                   "dbs_cuda_vshard_select", "dbs_cuda_vshard_rescan")
 ADDED_SYMBOLS = ("dbs_cuda_b200_abi_version", "dbs_cuda_backtrack", "dbs_cuda_backward_dense", "dbs_cuda_advance_prefixes",
                  "dbs_cuda_selected_weights", "dbs_cuda_backward_selected", "dbs_cuda_b200_wait_selftest",
-                 "dbs_cuda_decode_no_alloc") + VSHARD_SYMBOLS
+                 "dbs_cuda_decode_no_alloc", "dbs_cuda_relaxed_pool", "dbs_cuda_backward_pool") + VSHARD_SYMBOLS
 REFERENCE_SYMBOLS = [n for n in SIGNATURES if n not in ADDED_SYMBOLS]
 
 # Size of the fixed device array behind dbs_cuda_decode_no_alloc (DBS_CUDA_B200_NO_ALLOC_SCRATCH_BYTES).

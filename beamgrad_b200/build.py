@@ -40,7 +40,7 @@ NVCC_FLAGS = [
     "-fPIC,-ffp-contract=off,-fvisibility=hidden",
 ]
 LIB_SOURCES = ["decode.cu", "decode_f32.cu", "decode_f16.cu", "decode_bf16.cu", "backward.cu", "api.cu", "static_scratch.cu",
-               "vshard.cu", "search.cu"]
+               "vshard.cu", "search.cu", "pool.cu"]
 
 
 def _nvcc() -> str:

@@ -31,6 +31,12 @@ size_t decode_select_smem(int K);
 
 
 cudaError_t launch_backward(const BackwardParams& p, cudaStream_t stream);
+// pool.cu
+cudaError_t launch_relaxed_pool(const DecodeParams& d, int dtype, bool logits, int P, const float* row_lse,
+                                const int32_t* parents, const int32_t* tokens, const int32_t* lengths, const float* raw,
+                                const uint8_t* from_logprob, int32_t* pool_parents, int32_t* pool_tokens,
+                                int32_t* pool_lengths, float* pool_scores, float* pool_raw, uint8_t* pool_from,
+                                float* relaxed, float temperature, float tolerance, int max_iters, cudaStream_t stream);
 cudaError_t launch_logit_correction(const BackwardParams& p, int dtype, const void* logits, const float* row_lse,
                                     cudaStream_t stream);
 cudaError_t launch_dense_grad(const BackwardParams& p, int in_type, const void* logits, const float* row_lse,
@@ -674,6 +680,86 @@ DBS_CUDA_EXPORT int dbs_cuda_backward_ex(const DBSCudaDecodeArgs* args, const DB
     if (launch_logit_correction(p, in->logits_type, in->logits, in->row_lse, stream) != cudaSuccess) {
         return DBS_CUDA_STATUS_LAUNCH_FAILED;
     }
+    return close_call(stream, nullptr);
+}
+
+// ---------------------------------------------------------------------------
+// Relaxed pool (pool.cu) and its gradient terms (backward_kernel)
+// ---------------------------------------------------------------------------
+namespace {
+
+bool null_reserved(void* const (&r)[4]) {
+    return std::all_of(std::begin(r), std::end(r), [](const void* q) { return q == nullptr; });
+}
+
+// What the pool supports, beyond the decode's own rules: no prefix constraints, no
+// per-example settings other than steps, no extra EOS tokens.
+bool pool_problem_ok(const DBSCudaDecodeArgs& a) {
+    return !constrained(a) && !a.beam_sizes_per_example && !a.eos_tokens_per_example && !a.min_lengths_per_example;
+}
+
+}  // namespace
+
+DBS_CUDA_EXPORT int dbs_cuda_relaxed_pool(const void* inputs, int data_type, int from_logits,
+                                          const DBSCudaDecodeArgs* args, const DBSCudaDecodeOutputs* trace,
+                                          const float* row_lse, int pool_size, float soft_topk_temperature,
+                                          float soft_topk_tolerance, int soft_topk_max_iters,
+                                          const DBSCudaPoolOutputs* pool, void* stream_ptr) {
+    if (!inputs || !valid_dtype(data_type) || !valid_args(args) || !trace || !pool) return DBS_CUDA_STATUS_INVALID_ARGUMENT;
+    if (!pool_problem_ok(*args) || !null_reserved(pool->reserved)) return DBS_CUDA_STATUS_INVALID_ARGUMENT;
+    if (!trace->parents || !trace->tokens || !trace->lengths || !trace->raw_scores || !trace->from_logprob)
+        return DBS_CUDA_STATUS_INVALID_ARGUMENT;
+    if (from_logits && !row_lse) return DBS_CUDA_STATUS_INVALID_ARGUMENT;
+    if (pool_size < args->beam_size || pool_size > DBS_CUDA_B200_MAX_POOL) return DBS_CUDA_STATUS_INVALID_ARGUMENT;
+    if (pool->relaxed_weights &&
+        (!std::isfinite(soft_topk_temperature) || !(soft_topk_temperature > 0.0f) ||
+         !std::isfinite(soft_topk_tolerance) || soft_topk_tolerance < 0.0f || soft_topk_max_iters < 0))
+        return DBS_CUDA_STATUS_INVALID_ARGUMENT;
+    cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+    DecodeParams d;
+    fill_params(d, *args, nullptr);
+    d.inputs = inputs;
+    if (launch_relaxed_pool(d, data_type, from_logits != 0, pool_size, row_lse, trace->parents, trace->tokens,
+                            trace->lengths, trace->raw_scores, trace->from_logprob, pool->parents, pool->tokens,
+                            pool->lengths, pool->scores, pool->raw_scores, pool->from_logprob, pool->relaxed_weights,
+                            soft_topk_temperature, soft_topk_tolerance, soft_topk_max_iters, stream) != cudaSuccess)
+        return DBS_CUDA_STATUS_LAUNCH_FAILED;
+    return close_call(stream, nullptr);
+}
+
+DBS_CUDA_EXPORT int dbs_cuda_backward_pool(const DBSCudaDecodeArgs* args, const DBSCudaBackwardInputs* in,
+                                           const DBSCudaPoolGradients* pool, float* grad_inputs, void* stream_ptr) {
+    if (!valid_args(args) || !in || !pool || !grad_inputs || !pool_problem_ok(*args)) return DBS_CUDA_STATUS_INVALID_ARGUMENT;
+    if (!in->parents || !in->tokens || !in->lengths || !in->from_logprob || in->logits) return DBS_CUDA_STATUS_INVALID_ARGUMENT;
+    if (in->reserved0 != 0 || !null_reserved(in->reserved) || pool->reserved0 != 0 || !null_reserved(pool->reserved))
+        return DBS_CUDA_STATUS_INVALID_ARGUMENT;
+    if (pool->pool_size < args->beam_size || pool->pool_size > DBS_CUDA_B200_MAX_POOL) return DBS_CUDA_STATUS_INVALID_ARGUMENT;
+    if (!pool->parents || !pool->tokens || !pool->lengths || !pool->from_logprob) return DBS_CUDA_STATUS_INVALID_ARGUMENT;
+    if (pool->grad_relaxed_weights &&
+        (!pool->relaxed_weights || !std::isfinite(pool->soft_topk_temperature) || !(pool->soft_topk_temperature > 0.0f)))
+        return DBS_CUDA_STATUS_INVALID_ARGUMENT;
+    cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+    BackwardParams p = backward_params(*args);
+    p.parents = in->parents;
+    p.tokens = in->tokens;
+    p.lengths = in->lengths;
+    p.from_logprob = in->from_logprob;
+    p.g_final = in->grad_final_scores;
+    p.g_final_raw = in->grad_final_raw_scores;
+    p.g_scores = in->grad_scores;
+    p.g_raw = in->grad_raw_scores;
+    p.grad = grad_inputs;
+    p.P = pool->pool_size;
+    p.pool_parents = pool->parents;
+    p.pool_tokens = pool->tokens;
+    p.pool_lengths = pool->lengths;
+    p.pool_from = pool->from_logprob;
+    p.relaxed = pool->relaxed_weights;
+    p.g_relaxed = pool->grad_relaxed_weights;
+    p.g_pool_scores = pool->grad_pool_scores;
+    p.g_pool_raw = pool->grad_pool_raw_scores;
+    p.soft_temp = pool->soft_topk_temperature;
+    if (launch_backward(p, stream) != cudaSuccess) return DBS_CUDA_STATUS_LAUNCH_FAILED;
     return close_call(stream, nullptr);
 }
 

@@ -25,12 +25,44 @@ namespace dbsb {
 
 
 
+// Ascending bitonic sort of n (a power of two, <= DBS_CUDA_MAX_BEAM) 32-bit keys in shared
+// memory by the whole CTA.
+__device__ void bitonic_sort_u32(uint32_t* keys, int n) {
+    for (int size = 2; size <= n; size <<= 1) {
+        for (int stride = size >> 1; stride > 0; stride >>= 1) {
+            for (int i = threadIdx.x; i < n; i += kThreads) {
+                const int j = i ^ stride;
+                if (j > i) {
+                    const bool up = (i & size) == 0;
+                    const uint32_t a = keys[i], c = keys[j];
+                    if ((a > c) == up) {
+                        keys[i] = c;
+                        keys[j] = a;
+                    }
+                }
+            }
+            block_sync();
+        }
+    }
+}
+
+constexpr int kPoolCap = DBS_CUDA_B200_MAX_POOL;  // pool candidates per step
+
+// Beams above this many: parents find their children through one sort per step instead of
+// each parent scanning every slot (without pool gradients).
+constexpr int kScanParentsUpTo = 64;
+
 // One CTA per example; its beams' running gradients live in shared memory.
 __global__ void __launch_bounds__(kThreads) backward_kernel(const __grid_constant__ BackwardParams p) {
     __shared__ float next_g[DBS_CUDA_MAX_BEAM];
     __shared__ float prev_g[DBS_CUDA_MAX_BEAM];
     __shared__ float draw_s[DBS_CUDA_MAX_BEAM];
     __shared__ int32_t par_s[DBS_CUDA_MAX_BEAM];
+    __shared__ uint32_t child_s[DBS_CUDA_MAX_BEAM];  // (parent << 11 | slot), sorted
+    __shared__ float pdraw_s[kPoolCap];               // pool candidates' raw-score gradients
+    __shared__ int32_t ppar_s[kPoolCap];              // and parents (-1: none)
+    __shared__ float pool_center_s;
+    __shared__ int pool_relaxed_s;
     const int b = blockIdx.x;
     const int tid = threadIdx.x;
     const int K = p.K;
@@ -86,12 +118,95 @@ __global__ void __launch_bounds__(kThreads) backward_kernel(const __grid_constan
             par_s[k] = pq;
         }
         block_sync();
-        // prev[q] = sum of its children's draws in slot order, from 0.
-        for (int q = tid; q < Kb; q += kThreads) {
-            float sum = 0.0f;
-            for (int k = 0; k < Kb; ++k)
-                if (par_s[k] == q) sum = __fadd_rn(sum, draw_s[k]);
-            prev_g[q] = sum;
+        const bool pool = p.P > 0;
+        if (pool) {
+            // Pool candidates after the selected beams (src/decoder.cpp:621-657): the relaxed
+            // weights' implicit gradient through the bisection threshold, and the pool scores'
+            // own gradients; their sums over the pool run in pool order.
+            const int64_t pbase = (static_cast<int64_t>(b) * p.T + t) * p.P;
+            if (tid == 0) {
+                int relaxed = 0;
+                float center = 0.0f;
+                if (p.g_relaxed) {
+                    float denom = 0.0f, numer = 0.0f;
+                    for (int i = 0; i < p.P; ++i) {
+                        const float r = p.relaxed[pbase + i];
+                        const float a = __fmul_rn(r, __fsub_rn(1.0f, r));
+                        denom = __fadd_rn(denom, a);
+                        numer = __fadd_rn(numer, __fmul_rn(p.g_relaxed[pbase + i], a));
+                    }
+                    if (denom > 1.0e-12f) {
+                        relaxed = 1;
+                        center = __fdiv_rn(numer, denom);
+                    }
+                }
+                pool_relaxed_s = relaxed;
+                pool_center_s = center;
+            }
+            block_sync();
+            const float inv_temp = pool_relaxed_s ? __fdiv_rn(1.0f, p.soft_temp) : 0.0f;
+            for (int i = tid; i < p.P; i += kThreads) {
+                const int64_t slot = pbase + i;
+                const int q = p.pool_parents[slot];
+                float d = 0.0f;
+                int pq = -1;
+                if (q >= 0 && q < Kb) {
+                    float drank = 0.0f;
+                    if (pool_relaxed_s) {
+                        const float r = p.relaxed[slot];
+                        const float a = __fmul_rn(r, __fsub_rn(1.0f, r));
+                        drank = __fadd_rn(drank, __fmul_rn(__fmul_rn(a, inv_temp), __fsub_rn(p.g_relaxed[slot], pool_center_s)));
+                    }
+                    if (p.g_pool_scores) drank = __fadd_rn(drank, p.g_pool_scores[slot]);
+                    d = __fmul_rn(drank, __fdiv_rn(1.0f, gnmt_penalty(p.pool_lengths[slot], p.alpha)));
+                    if (p.g_pool_raw) d = __fadd_rn(d, p.g_pool_raw[slot]);
+                    if (d != 0.0f) {
+                        pq = q;
+                        const int tok = p.pool_tokens[slot];
+                        if (p.grad && p.pool_from[slot] && tok >= 0 && tok < p.V) {
+                            // After the selected beams' terms (the barrier above); pool entries are
+                            // distinct candidates, so no two threads add to one element here.
+                            const int64_t g = (base + q) * static_cast<int64_t>(p.V) + tok;
+                            p.grad[g] = __fadd_rn(p.grad[g], d);
+                        }
+                    }
+                }
+                pdraw_s[i] = d;
+                ppar_s[i] = pq;
+            }
+            block_sync();
+        }
+        // prev[q] = sum of its children's draws in slot order (then its pool candidates' in
+        // pool order), from 0 (src/decoder.cpp:592-661).
+        if (Kb <= kScanParentsUpTo || pool) {
+            for (int q = tid; q < Kb; q += kThreads) {
+                float sum = 0.0f;
+                for (int k = 0; k < Kb; ++k)
+                    if (par_s[k] == q) sum = __fadd_rn(sum, draw_s[k]);
+                if (pool)
+                    for (int i = 0; i < p.P; ++i)
+                        if (ppar_s[i] == q) sum = __fadd_rn(sum, pdraw_s[i]);
+                prev_g[q] = sum;
+            }
+        } else {
+            // Children sorted by (parent, slot): each parent's children are one run, in slot
+            // order; slots without a draw sort last.
+            int n2 = 1;
+            while (n2 < Kb) n2 <<= 1;
+            for (int i = tid; i < n2; i += kThreads) {
+                child_s[i] = (i < Kb && par_s[i] >= 0) ? (static_cast<uint32_t>(par_s[i]) << 11) | static_cast<uint32_t>(i)
+                                                       : 0xffffffffu;
+                if (i < Kb) prev_g[i] = 0.0f;
+            }
+            block_sync();
+            bitonic_sort_u32(child_s, n2);
+            for (int i = tid; i < n2; i += kThreads) {
+                const uint32_t q = child_s[i] >> 11;
+                if (child_s[i] == 0xffffffffu || (i > 0 && (child_s[i - 1] >> 11) == q)) continue;
+                float sum = 0.0f;  // i starts parent q's run
+                for (int j = i; j < n2 && (child_s[j] >> 11) == q; ++j) sum = __fadd_rn(sum, draw_s[child_s[j] & 2047u]);
+                prev_g[q] = sum;
+            }
         }
         block_sync();
         for (int k = tid; k < Kb; k += kThreads) next_g[k] = prev_g[k];

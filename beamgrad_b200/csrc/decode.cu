@@ -1,34 +1,10 @@
 // SPDX-License-Identifier: MIT
 //
-// The fused decode step of the B200 engine: one persistent kernel runs every
-// step of every example.
-//
-// Work items are beam rows (t, b, k), handed out by an atomic ticket in
-// t-major order. A CTA that takes row (t, b, k) waits (bounded) until example
-// b's step t-1 is published, reads the parent's state, and, when the row is
-// read by the search (live, unfinished parent of an active step), streams it
-// from HBM once:
-//   - from logits: the row is staged in shared memory by a 1-D TMA bulk copy
-//     (cp.async.bulk + mbarrier); pass 1 takes the maximum and the NaN/+inf
-//     flag, pass 2 sums exp(x - max) with thread j owning logsumexp lane j
-//     (v = j mod 256, increasing v, the reference's fixed order), then the
-//     pairwise lane tree gives lse; pass 3 turns entries into candidate keys;
-//   - from log-probs: a single streaming pass of 128-bit loads;
-// and keeps the row's best candidates (register top-k per thread for beams up
-// to 16, a block radix select above). The CTA that completes the last row of
-// (t, b) merges the K row lists with the carried-forward finished beams, writes
-// the step's trace and the new state, and publishes step t of example b.
-//
-// Tickets of step t are all handed out before any of step t+1, and a CTA only
-// waits for a step whose tickets are lower than its own (held by running CTAs),
-// so the hand-off cannot deadlock; every wait is also bounded by a timeout that
-// sets the workspace error word.
-//
-// Candidate order: within one step every scanned candidate of an example
-// extends a beam of the same length, so ranking by (raw desc, parent*V+token
-// asc) -- a 64-bit key -- equals the CPU decoder's ranking by (score, raw,
-// parent, token) (src/common.hpp:269-276 of beamgrad 2.3.0). Carried-forward
-// candidates are merged with the full comparator.
+// Host-side dispatch of the decode kernels (decode_impl.cuh): the kernel family by data
+// type and input kind, the chained or waiting decode, and the small helper kernels that
+// every decode shares (workspace initialisation, per-example argument validation, the
+// bounded-wait self test). The per-dtype kernel instantiations live in decode_f32.cu,
+// decode_f16.cu and decode_bf16.cu so that they compile in parallel.
 #include "decode_impl.cuh"
 
 namespace dbsb {

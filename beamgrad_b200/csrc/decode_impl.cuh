@@ -1,34 +1,34 @@
 // SPDX-License-Identifier: MIT
 //
-// The fused decode step of the B200 engine: one persistent kernel runs every
-// step of every example.
+// The decode kernels of the B200 engine (included by decode.cu and the per-dtype
+// decode_*.cu units). Three kernels run a whole decode in one persistent launch each:
 //
-// Work items are beam rows (t, b, k), handed out by an atomic ticket in
-// t-major order. A CTA that takes row (t, b, k) waits (bounded) until example
-// b's step t-1 is published, reads the parent's state, and, when the row is
-// read by the search (live, unfinished parent of an active step), streams it
-// from HBM once:
-//   - from logits: the row is staged in shared memory by a 1-D TMA bulk copy
-//     (cp.async.bulk + mbarrier); pass 1 takes the maximum and the NaN/+inf
-//     flag, pass 2 sums exp(x - max) with thread j owning logsumexp lane j
-//     (v = j mod 256, increasing v, the reference's fixed order), then the
-//     pairwise lane tree gives lse; pass 3 turns entries into candidate keys;
-//   - from log-probs: a single streaming pass of 128-bit loads;
-// and keeps the row's best candidates (register top-k per thread for beams up
-// to 16, a block radix select above). The CTA that completes the last row of
-// (t, b) merges the K row lists with the carried-forward finished beams, writes
-// the step's trace and the new state, and publishes step t of example b.
+//   decode_chain_kernel       beams <= 16, rows staged in shared memory by a TMA bulk
+//                             copy (or streamed when they do not fit): pass 1 (maximum,
+//                             minimum, NaN/+inf flag, per-thread maxima -> a filter bound),
+//                             from logits pass 2 (the reference's fixed-order logsumexp on
+//                             warps 0-3, packed f32x2) beside the row record on warps 4-7;
+//   decode_chain_warp_kernel  log-probability rows, beams <= 16, one warp per row straight
+//                             from HBM;
+//   decode_chain_wide_kernel  beams 17..1024, records of 2K entries, block selection.
 //
-// Tickets of step t are all handed out before any of step t+1, and a CTA only
-// waits for a step whose tickets are lower than its own (held by running CTAs),
-// so the hand-off cannot deadlock; every wait is also bounded by a timeout that
-// sets the workspace error word.
+// Chained protocol (no CTA ever waits for another): work items are beam rows (t, b, k)
+// handed out by an atomic ticket in t-major order. A row needs nothing from the previous
+// step: it is reduced to a parent-independent record (its best entries by x, its
+// logsumexp and flags). Each (b, t) counts arrivals -- its K rows and, for t > 0, the
+// selection of step t-1 -- and the CTA (or warp) that completes the count selects step t
+// from the K records and the carried-forward finished beams, then arrives for t+1. A
+// record that cannot prove it holds the row's best candidates (raw scores that round
+// together, constraints) is rescanned by the selecting group with the parent known.
 //
-// Candidate order: within one step every scanned candidate of an example
-// extends a beam of the same length, so ranking by (raw desc, parent*V+token
-// asc) -- a 64-bit key -- equals the CPU decoder's ranking by (score, raw,
-// parent, token) (src/common.hpp:269-276 of beamgrad 2.3.0). Carried-forward
-// candidates are merged with the full comparator.
+// decode_kernel (the waiting variant) serves the step API and decodes whose record area
+// would be too large: step t of example b waits (bounded; a timeout sets the error word)
+// for step t-1 to be published, then scans its row with the parent known.
+//
+// Candidate order: within one step every scanned candidate of an example extends a beam
+// of the same length, so ranking by (raw desc, parent*V+token asc) -- a 64-bit key --
+// equals the CPU decoder's ranking by (score, raw, parent, token) (src/common.hpp:269-276
+// of beamgrad 2.3.0). Carried-forward candidates are merged with the full comparator.
 #pragma once
 #include <type_traits>
 

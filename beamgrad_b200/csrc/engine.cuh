@@ -8,6 +8,7 @@
 #include <cuda_runtime.h>
 
 #include "dbs_cuda.h"
+#include "dbs_cuda_b200.h"
 #include "detmath.cuh"
 
 namespace dbsb {
@@ -130,6 +131,17 @@ struct BackwardParams {
     const float* w_sel;   // selected-beam weights [B, T, K], or null
     const float* g_wsel;  // their gradient [B, T, K], or null
     float sel_temp;       // the weights' softmax temperature
+    // Relaxed pool (P candidates per step), when pool gradients are given (P = 0: none).
+    int P;
+    const int32_t* pool_parents;  // [B, T, P]
+    const int32_t* pool_tokens;
+    const int32_t* pool_lengths;
+    const uint8_t* pool_from;
+    const float* relaxed;         // relaxed weights [B, T, P] (with g_relaxed)
+    const float* g_relaxed;       // their gradient, or null
+    const float* g_pool_scores;   // [B, T, P] or null
+    const float* g_pool_raw;      // [B, T, P] or null
+    float soft_temp;              // the relaxed weights' sigmoid temperature
 };
 
 __device__ __forceinline__ Meta load_meta(const DecodeParams& p, int b) {

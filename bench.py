@@ -112,10 +112,12 @@ def peaks() -> tuple[float, str]:
     return 6650.0, "fallback"
 
 
-# Rounded FP32 operations per logit entry of the bit-exact logsumexp and scan: the Cephes
-# exp_nonpositive (22: range reduction, degree-5 polynomial, exponent insertion), the
-# subtraction of the row maximum and the lane add.
-FP32_OPS_PER_ENTRY = 24
+# FP32 lane operations per logit entry of the bit-exact logsumexp, counted by ncu on the C2
+# decode (profiles/decode_chain_kernel.c2_pipes.md): 11.0 packed FFMA2 instructions per entry
+# (two lane operations each: the subtraction of the row maximum, the Cephes exp_nonpositive's
+# range reduction and degree-5 polynomial, the lane add) and 1.0 scalar FADD (the
+# round-toward-minus-infinity floor) -- 23 operations on the FMA pipes.
+FP32_OPS_PER_ENTRY = 23
 
 
 def fp32_roofline(entries: int, seconds: float, clocks: dict) -> dict:

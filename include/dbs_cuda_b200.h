@@ -97,6 +97,70 @@ DBS_CUDA_EXPORT int dbs_cuda_advance_prefixes(int batch_size, int beam_size, int
  * reference. */
 DBS_CUDA_EXPORT int dbs_cuda_b200_wait_selftest(int64_t timeout_ns, int32_t* words, void* stream);
 
+/* ------------------------------------------------------------------------
+ * Relaxed pool (beamgrad 2.3.0 src/decoder.cpp:294-312 record_pool and the
+ * pool terms of run_backward, :621-657; include/dbs.h:64-79, 337-349, 373-397;
+ * the CPU library's relaxed_pool_multiplier). The reference computes the pool
+ * only on the CPU; these run it on the GPU with identical results.
+ *
+ * dbs_cuda_relaxed_pool: after a decode, the P = pool_size (K <= P <= 1024) best candidates of
+ * every step under the full candidate order (the first K of them are the
+ * step's selected beams), written [B, T, P] in that order (fewer than P
+ * candidates: parent/token -1, length 0, scores -inf, from_logprob 0; steps
+ * past an example's length are empty), and, when relaxed_weights is set, each
+ * step's relaxed top-K membership sigmoid((score - theta) / temperature) with
+ * theta bisected so that the weights sum to K (src/kernels_scalar.cpp:304-366).
+ * inputs / data_type / from_logits / args are the decode's; trace is its
+ * output (parents, tokens, lengths, raw_scores and from_logprob are read);
+ * row_lse its row logsumexp (needed from logits). Not supported (as by
+ * beamgrad's relaxed_topk): n-gram blocking, a repetition penalty, per-example
+ * beam sizes / EOS tokens / minimum lengths, extra EOS tokens.
+ * ------------------------------------------------------------------------ */
+#define DBS_CUDA_B200_MAX_POOL 1024
+
+typedef struct DBSCudaPoolOutputs {
+    int32_t* parents;         /* [B, T, P] */
+    int32_t* tokens;          /* [B, T, P] */
+    int32_t* lengths;         /* [B, T, P] */
+    float* scores;            /* [B, T, P] length-penalised ranking scores */
+    float* raw_scores;        /* [B, T, P] cumulative log-probabilities */
+    uint8_t* from_logprob;    /* [B, T, P] */
+    float* relaxed_weights;   /* [B, T, P] relaxed top-K membership, or NULL */
+    void* reserved[4];        /* must be NULL */
+} DBSCudaPoolOutputs;
+
+DBS_CUDA_EXPORT int dbs_cuda_relaxed_pool(const void* inputs, int data_type, int from_logits,
+                                          const DBSCudaDecodeArgs* args, const DBSCudaDecodeOutputs* trace,
+                                          const float* row_lse, int pool_size, float soft_topk_temperature,
+                                          float soft_topk_tolerance, int soft_topk_max_iters,
+                                          const DBSCudaPoolOutputs* pool, void* stream);
+
+/* The pool of a decode and the gradients of its outputs, for
+ * dbs_cuda_backward_pool. grad_relaxed_weights needs relaxed_weights. */
+typedef struct DBSCudaPoolGradients {
+    int pool_size;                        /* P */
+    int reserved0;                        /* must be 0 */
+    const int32_t* parents;               /* [B, T, P] as dbs_cuda_relaxed_pool wrote them */
+    const int32_t* tokens;
+    const int32_t* lengths;
+    const uint8_t* from_logprob;
+    const float* relaxed_weights;         /* [B, T, P], with grad_relaxed_weights */
+    const float* grad_relaxed_weights;    /* [B, T, P] or NULL */
+    const float* grad_pool_scores;        /* [B, T, P] or NULL */
+    const float* grad_pool_raw_scores;    /* [B, T, P] or NULL */
+    float soft_topk_temperature;          /* the relaxed weights' temperature (> 0) */
+    void* reserved[4];                    /* must be NULL */
+} DBSCudaPoolGradients;
+
+/* dbs_cuda_backward_ex plus the pool terms (src/decoder.cpp:621-657): per step the
+ * selected beams' raw-score gradients, then each pool candidate's
+ *   d = (relaxed term + grad_pool_scores) / penalty(length) + grad_pool_raw_scores,
+ * with parents summing their selected children in slot order and then their pool
+ * candidates in pool order; accumulated (+=) into the caller-zeroed float32
+ * [B, T, K, V] grad_inputs. Log-probability inputs only (in->logits must be NULL). */
+DBS_CUDA_EXPORT int dbs_cuda_backward_pool(const DBSCudaDecodeArgs* args, const DBSCudaBackwardInputs* in,
+                                           const DBSCudaPoolGradients* pool, float* grad_inputs, void* stream);
+
 /* Bytes of the fixed device array behind dbs_cuda_decode_no_alloc (4 MiB). */
 #define DBS_CUDA_B200_NO_ALLOC_SCRATCH_BYTES (4 * 1024 * 1024)
 
@@ -116,7 +180,12 @@ DBS_CUDA_EXPORT int dbs_cuda_b200_wait_selftest(int64_t timeout_ns, int32_t* wor
  * caches it; make that first call before any stream capture. Every call on a
  * device uses the same array, and each decode starts by resetting what it
  * reads: calls whose work overlaps on the GPU (other streams, other threads)
- * race on the array, so order them on one stream or otherwise serialize them. */
+ * race on the array, so order them on one stream or otherwise serialize them.
+ * The cached address belongs to the device's context at the first call: after
+ * cudaDeviceReset on that device it is stale, so do not call this entry point
+ * on that device again in the process. 4 MiB covers small and medium decodes
+ * (the chained decode needs about 130 bytes per row of B x T x K); the
+ * BASELINE C2 decode [64, 128, 8, 32000] needs 8.4 MB and is refused. */
 DBS_CUDA_EXPORT int dbs_cuda_decode_no_alloc(const void* inputs, int data_type, int from_logits,
                                              const DBSCudaDecodeArgs* args, const DBSCudaSearchOptions* options,
                                              const DBSCudaDecodeOutputs* outputs, float* row_lse, void* stream);

@@ -424,7 +424,7 @@ def ref_lib() -> C.CDLL:
 class RefDecoder:
     """A libdbs decoder handle configured like `pb` (no per-example beams / EOS / min lengths)."""
 
-    def __init__(self, pb: Problem):
+    def __init__(self, pb: Problem, pool_multiplier: int = 0):
         if pb.beams is not None or pb.eos_pe is not None or pb.minlen_pe is not None:
             raise ValueError("libdbs has no per-example beam sizes, EOS tokens or minimum lengths")
         lib = ref_lib()
@@ -433,6 +433,8 @@ class RefDecoder:
         o.eos_token = pb.eos
         o.length_penalty_alpha = pb.alpha
         o.min_length = pb.min_length
+        o.relaxed_pool_multiplier = pool_multiplier  # P = K * pool_multiplier pool candidates per step
+        self.P = pb.shape[2] * pool_multiplier
         o.validate_inputs = 0  # NaN/+inf entries are never selected (the engine reports flags instead)
         h = _p()
         if lib.dbs_create_ex(o, C.byref(h)) != 0:
@@ -462,6 +464,7 @@ class RefDecoder:
         return c
 
     def decode(self, threads: int = 1) -> dict[str, np.ndarray]:
+        """The decode's outputs; with a pool also pool_parents ... pool_from_logprob [B, T, P]."""
         pb = self.pb
         B, T, K, V = pb.shape
         out = empty_outputs(B, T, K)
@@ -469,6 +472,12 @@ class RefDecoder:
         for n in TRACE_FIELDS:
             setattr(ex.base, n, _ptr(out[n]))
         ex.row_lse = _ptr(out["row_lse"])
+        if self.P:
+            P = self.P
+            for n, dt in (("parents", np.int32), ("tokens", np.int32), ("lengths", np.int32), ("scores", np.float32),
+                          ("raw_scores", np.float32), ("from_logprob", np.uint8)):
+                out["pool_" + n] = np.full((B, T, P), 77, dt)
+                setattr(ex, "pool_" + n, _ptr(out["pool_" + n]))
         c = self._constraints()
         x = np.ascontiguousarray(pb.x)
         rc = ref_lib().dbs_decode_batch_into_ex(self.h, _ptr(x), pb.dtype, int(pb.from_logits), B, T, V,
@@ -478,12 +487,20 @@ class RefDecoder:
             raise RuntimeError(ref_lib().dbs_last_global_error().decode())
         return out
 
-    def backward(self, trace, grads, logits=None, row_lse=None, threads: int = 1) -> np.ndarray:
+    def backward(self, trace, grads, logits=None, row_lse=None, threads: int = 1, pool=None) -> np.ndarray:
+        """Dense float32 input gradient; pool: the decode's pool_* arrays, with grads'
+        pool_scores / pool_raw_scores gradients [B, T, P]."""
         pb = self.pb
         B, T, K, V = pb.shape
         grad = np.zeros((B, T, K, V), np.float32)
         bi = _BackwardC()
         bi.batch_size, bi.steps, bi.vocab_size, bi.pool_size = B, T, V, 0
+        if pool is not None:
+            bi.pool_size = self.P
+            bi.pool_parents, bi.pool_tokens = _ptr(pool["pool_parents"]), _ptr(pool["pool_tokens"])
+            bi.pool_lengths, bi.pool_from_logprob = _ptr(pool["pool_lengths"]), _ptr(pool["pool_from_logprob"])
+            bi.grad_pool_scores = _ptr(grads.get("pool_scores"))
+            bi.grad_pool_raw_scores = _ptr(grads.get("pool_raw_scores"))
         bi.steps_per_example = _ptr(pb.steps)
         bi.parents, bi.tokens = _ptr(trace["parents"]), _ptr(trace["tokens"])
         bi.lengths, bi.from_logprob = _ptr(trace["lengths"]), _ptr(trace["from_logprob"])
@@ -545,3 +562,53 @@ def ref_selected(x: np.ndarray, beam: int, eos: int, alpha: float, min_length: i
             lib.dbs_free_result(res)
         lib.dbs_destroy(h)
     return w, g
+
+
+def ref_relaxed(x: np.ndarray, beam: int, eos: int, alpha: float, min_length: int, multiplier: int, temperature: float,
+                tolerance: float, max_iters: int, grad_relaxed: np.ndarray, grad_final: np.ndarray):
+    """The reference library's relaxed pool of one float32 log-prob example x [T, K, V]: the pool
+    (tokens, parents, lengths, scores, raw scores [T, P]), its relaxed weights [T, P] and the dense
+    input gradient [T, K, V] for grad_relaxed_weights and grad_final_scores (dbs_decode,
+    dbs_result_pool_* / dbs_result_relaxed_weights, dbs_backward_dense: include/dbs.h:215-221,
+    448-455, 494-501)."""
+    lib = ref_lib()
+    for name, res_t in (("dbs_result_relaxed_weights", C.POINTER(C.c_float)),
+                        ("dbs_result_pool_scores", C.POINTER(C.c_float)),
+                        ("dbs_result_pool_raw_scores", C.POINTER(C.c_float)),
+                        ("dbs_result_pool_tokens", C.POINTER(C.c_int32)),
+                        ("dbs_result_pool_parents", C.POINTER(C.c_int32)),
+                        ("dbs_result_pool_lengths", C.POINTER(C.c_int32))):
+        fn = getattr(lib, name)
+        fn.restype, fn.argtypes = res_t, [_p]
+    T, K, V = x.shape
+    P = K * multiplier
+    o = _Options()
+    o.beam_size, o.eos_token, o.length_penalty_alpha, o.min_length = beam, eos, alpha, min_length
+    o.relaxed_pool_multiplier, o.soft_topk_temperature = multiplier, temperature
+    o.soft_topk_tolerance, o.soft_topk_max_iters = tolerance, max_iters
+    o.max_dense_gradient_elements = T * K * V + 1
+    h = _p()
+    if lib.dbs_create_ex(o, C.byref(h)) != 0:
+        raise RuntimeError(lib.dbs_last_global_error().decode())
+    res, bw = _p(), _p()
+    out = {}
+    try:
+        xc = np.ascontiguousarray(x, np.float32)
+        if lib.dbs_decode(h, _ptr(xc), T, V, C.byref(res)) != 0:
+            raise RuntimeError(lib.dbs_last_error(h).decode())
+        for key, fn in (("relaxed_weights", lib.dbs_result_relaxed_weights), ("pool_scores", lib.dbs_result_pool_scores),
+                        ("pool_raw_scores", lib.dbs_result_pool_raw_scores), ("pool_tokens", lib.dbs_result_pool_tokens),
+                        ("pool_parents", lib.dbs_result_pool_parents), ("pool_lengths", lib.dbs_result_pool_lengths)):
+            out[key] = np.ctypeslib.as_array(fn(res), shape=(T * P,)).reshape(T, P).copy()
+        gr = np.ascontiguousarray(grad_relaxed, np.float32)
+        gf = np.ascontiguousarray(grad_final, np.float32)
+        if lib.dbs_backward_dense(h, res, None, _ptr(gr), _ptr(gf), C.byref(bw)) != 0:
+            raise RuntimeError(lib.dbs_last_error(h).decode())
+        out["grad"] = np.ctypeslib.as_array(lib.dbs_backward_grad_log_probs(bw), shape=(T * K * V,)).reshape(T, K, V).copy()
+    finally:
+        if bw:
+            lib.dbs_free_backward(bw)
+        if res:
+            lib.dbs_free_result(res)
+        lib.dbs_destroy(h)
+    return out

@@ -36,6 +36,8 @@ B200_STRUCTS = {
     "DBSCudaVocabShardPlan": A.VocabShardPlan,
     "DBSCudaVocabShardBuffers": A.VocabShardBuffers,
     "DBSCudaVocabShardCall": A.VocabShardCall,
+    "DBSCudaPoolOutputs": A.PoolOutputs,
+    "DBSCudaPoolGradients": A.PoolGradients,
 }
 
 

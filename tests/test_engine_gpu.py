@@ -214,6 +214,51 @@ def test_backward_parity(seed):
     assert ours.tobytes() == ref.tobytes()
 
 
+@pytest.mark.parametrize("K", [65, 256, 1024])
+@pytest.mark.parametrize("mode", ["continuous", "ties"])
+def test_backward_large_beams_parity(K, mode):
+    """Beams above 64 find each parent's children through one sort per step (slot order kept)."""
+    pb = make_problem(2, 5, K, 9 if K == 1024 else 61, mode=mode, seed=K, eos=3, alpha=0.6, variable_steps=True)
+    B, T, K, V = pb.shape
+    trace = oracle.oracle_decode(pb)
+    rng = np.random.default_rng(K)
+    grads = {"final_scores": rng.uniform(-1, 1, (B, K)).astype(np.float32),
+             "scores": rng.uniform(-1, 1, (B, T, K)).astype(np.float32)}
+    ours = G.engine_backward(pb, trace, grads)
+    assert ours.tobytes() == oracle.oracle_backward(pb, trace, grads).tobytes()
+    draws = G.engine_path_gradient(pb, trace, grads["final_scores"])
+    assert draws.tobytes() == oracle.oracle_path_gradient(pb, trace, grads["final_scores"]).tobytes()
+
+
+def test_backward_time_at_beam_1024(capsys):
+    """The per-step parent sums at K = 1024 (one CTA per example walking its steps): timed."""
+    import ctypes as C
+
+    pb = make_problem(4, 32, 1024, 9, seed=5, eos=3, alpha=0.6)
+    B, T, K, V = pb.shape
+    trace = oracle.oracle_decode(pb)
+    lib = A.load()
+    dp = G.DeviceProblem(pb)
+    t = {k: G.dev(trace[k]) for k in ("parents", "tokens", "lengths", "from_logprob")}
+    g = G.dev(np.linspace(-1, 1, B * K, dtype=np.float32).reshape(B, K))
+    draws = torch.empty((B, T, K), dtype=torch.float32, device="cuda")
+    call = lambda: A.check(lib.dbs_cuda_path_gradient(C.byref(dp.args()), G.ptr(t["parents"]), G.ptr(t["tokens"]),  # noqa: E731
+                                                      G.ptr(t["lengths"]), G.ptr(t["from_logprob"]), G.ptr(g),
+                                                      G.ptr(draws), G.stream_ptr()), "path_gradient")
+    call()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(10):
+        call()
+    e1.record()
+    torch.cuda.synchronize()
+    with capsys.disabled():
+        print(f"\nbackward path gradient, B={B} T={T} K={K}: {e0.elapsed_time(e1) / 10 * 1e3:.1f} us per call")
+    ref = oracle.oracle_path_gradient(pb, trace, g.cpu().numpy())
+    assert draws.cpu().numpy().tobytes() == ref.tobytes()
+
+
 @pytest.mark.parametrize("seed", range(12))
 def test_backward_dense_parity(seed):
     """dbs_cuda_backward_dense == zero-filled float32 backward, cast to the output type, bit for bit."""
