@@ -66,6 +66,9 @@ def parse():
                     help="skip timing the reference's own GPU engine (C2 at N=1)")
     ap.add_argument("--with-backward", action="store_true",
                     help="C2: also time the dense bf16 input gradient of the decode (a stage of its own)")
+    ap.add_argument("--with-pool", type=int, default=0, metavar="M",
+                    help="C2: also time the relaxed pool of the decode (P = K x M candidates per step and "
+                         "their relaxed top-K weights, dbs_cuda_relaxed_pool)")
     ap.add_argument("--c5-path", default="sharded", choices=["sharded", "chained"],
                     help="C5 on one GPU: the vocabulary-shard stages (default) or the single-GPU chained decode")
     ap.add_argument("--batch", type=int, default=None,
@@ -1340,20 +1343,29 @@ def main():
     Bl = stop - start  # examples on this rank
     global_batch = B if strong else world * B
 
-    # Outputs and workspace allocated once.
+    # Outputs and workspace allocated once. The outputs are views of one flat byte buffer, so
+    # that under strong scaling one all_gather_into_tensor per decode (inside the timed
+    # region) leaves the whole batch's outputs on every rank, as one GPU would have them.
     f32, i32, u8 = torch.float32, torch.int32, torch.uint8
-    out = {
-        "final_scores": torch.empty((Bl, K), dtype=f32, device=dev),
-        "final_raw_scores": torch.empty((Bl, K), dtype=f32, device=dev),
-        "final_lengths": torch.empty((Bl, K), dtype=i32, device=dev),
-        "tokens": torch.empty((Bl, T, K), dtype=i32, device=dev),
-        "parents": torch.empty((Bl, T, K), dtype=i32, device=dev),
-        "lengths": torch.empty((Bl, T, K), dtype=i32, device=dev),
-        "scores": torch.empty((Bl, T, K), dtype=f32, device=dev),
-        "raw_scores": torch.empty((Bl, T, K), dtype=f32, device=dev),
-        "from_logprob": torch.empty((Bl, T, K), dtype=u8, device=dev),
-        "invalid_input": torch.empty((Bl,), dtype=u8, device=dev),
-    }
+    most = max(b1 - b0 for b0, b1 in (shard_range(B, r, world) for r in range(world))) if strong else Bl
+    layout = [("final_scores", (K,), f32), ("final_raw_scores", (K,), f32), ("final_lengths", (K,), i32),
+              ("tokens", (T, K), i32), ("parents", (T, K), i32), ("lengths", (T, K), i32), ("scores", (T, K), f32),
+              ("raw_scores", (T, K), f32), ("from_logprob", (T, K), u8), ("invalid_input", (), u8)]
+    offsets, flat_bytes = {}, 0
+    for name, shape, dt in layout:
+        offsets[name] = flat_bytes
+        n = most * (int(np.prod(shape)) if shape else 1) * torch.empty((), dtype=dt).element_size()
+        flat_bytes += (n + 15) // 16 * 16
+    flat = torch.zeros(flat_bytes, dtype=u8, device=dev)
+    out = {}
+    for name, shape, dt in layout:
+        n = Bl * (int(np.prod(shape)) if shape else 1) * torch.empty((), dtype=dt).element_size()
+        out[name] = flat[offsets[name]: offsets[name] + n].view(dt).view((Bl,) + shape)
+    gathered = torch.empty(world * flat_bytes, dtype=u8, device=dev) if strong and world > 1 else None
+
+    def gather_outputs():
+        if gathered is not None:
+            dist.all_gather_into_tensor(gathered, flat)
     row_lse = torch.empty((Bl, T, K), dtype=f32, device=dev)
     o = A.DecodeOutputs()
     for k, v in out.items():
@@ -1378,6 +1390,7 @@ def main():
 
     for _ in range(args.warmup):
         decode(x)
+        gather_outputs()
     barrier()
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     launch_ms = []
@@ -1395,6 +1408,7 @@ def main():
             decode(x)
             e1.record(stream)
             launch_ms.append((e0, e1))
+            gather_outputs()
         stop.record(stream)
         barrier()
         clocks.stop()
@@ -1491,6 +1505,46 @@ def main():
                 ex_t.append(e0.elapsed_time(e1) / 1e3)
         backward["backward_ex_f32_ms"] = statistics.median(ex_t) * 1e3
         del g32
+
+    # --with-pool M: the relaxed pool of the decode (one CTA per (example, step) re-reads the
+    # step's rows), with its relaxed top-K weights (temperature 0.5, tolerance 1e-4, 50 iterations).
+    pool = None
+    if args.with_pool > 0:
+        P = K * args.with_pool
+        pl = {k: torch.empty((Bl, T, P), dtype=dt, device=dev)
+              for k, dt in (("parents", torch.int32), ("tokens", torch.int32), ("lengths", torch.int32),
+                            ("scores", torch.float32), ("raw_scores", torch.float32), ("from_logprob", torch.uint8),
+                            ("relaxed_weights", torch.float32))}
+        po = A.PoolOutputs()
+        for k, v in pl.items():
+            setattr(po, k, v.data_ptr())
+        tr = A.DecodeOutputs()
+        for k in ("parents", "tokens", "lengths", "raw_scores", "from_logprob"):
+            setattr(tr, k, out[k].data_ptr())
+
+        def relaxed_pool():
+            A.check(lib.dbs_cuda_relaxed_pool(C.c_void_p(x.data_ptr()), A.DTYPE_BF16, 1, C.byref(a), C.byref(tr),
+                                              C.c_void_p(row_lse.data_ptr()), P, 0.5, 1e-4, 50, C.byref(po),
+                                              C.c_void_p(stream.cuda_stream)), "relaxed_pool")
+
+        for _ in range(2):
+            relaxed_pool()
+        pt = []
+        for _ in range(max(3, min(args.steps, 10))):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            relaxed_pool()
+            e1.record(stream)
+            torch.cuda.synchronize(dev)
+            pt.append(e0.elapsed_time(e1) / 1e3)
+        psec = statistics.median(pt)
+        # Read: the rows the decode read (the pool's scanned candidates come from the same rows)
+        # and the trace; written: the seven [B, T, P] pool arrays.
+        pbytes = n_rows * V * 2 + Bl * T * K * 17 + Bl * T * P * 25
+        pool = {"ms": psec * 1e3, "multiplier": args.with_pool, "pool_size": P, "alg_bytes": pbytes,
+                "achieved_gbs": pbytes / psec / 1e9, "frac": pbytes / psec / 1e9 / peak,
+                "kernel": "pool_kernel (dbs_cuda_relaxed_pool, relaxed weights on)"}
+        del pl
 
     # End to end through the same C-ABI call: pinned host input -> device, decode, outputs -> host.
     # The rank's examples go in chunks: chunk c's copy (on a copy stream) overlaps the decode of
@@ -1592,7 +1646,8 @@ def main():
             "dtype": "bf16",
             "data": "synthetic",
             "config": {"workload": workload(), "global_batch": global_batch, "seq_len": T, "beam": K, "vocab": V,
-                       "parallelism": (f"batch-sharded over {world} GPUs, {Bl} examples on rank 0" if strong else
+                       "parallelism": (f"batch-sharded over {world} GPUs, {Bl} examples on rank 0, outputs "
+                                       f"all-gathered to every rank in the timed region" if strong else
                                        f"batch x{world}, {B} examples per GPU") if world > 1 else "single GPU",
                        "l2": f"inputs ({Bl * T * K * V * 2 / 1e9:.2f} GB on rank 0) larger than L2 (126 MB)"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
@@ -1602,6 +1657,7 @@ def main():
             "cpu_baseline": cpu,
             "reference_gpu": ref_gpu,
             "backward": backward,
+            "pool": pool,
             "e2e": e2e,
             "gpu_launches": 2 * args.steps,
             "clocks": clocks.summary(),

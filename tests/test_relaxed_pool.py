@@ -99,6 +99,9 @@ _POOL_CASES = [
     (1, 6, 16, 2000, 4, dict(eos=9, alpha=1.2, dtype=A.DTYPE_F16)),
     (2, 4, 6, 64, 1, dict(eos=-1, alpha=0.6)),                   # no EOS: nothing carried
     (1, 3, 64, 512, 16, dict(eos=4, alpha=0.6)),                 # P = 1024, the largest pool
+    (1, 3, 4, 12000, 2, dict(eos=1, alpha=0.6, mode="ties")),    # > 2048 keys reach the bound
+    (2, 5, 6, 700, 4, dict(eos=2, alpha=0.6, mode="neginf")),    # -inf entries are not candidates
+    (2, 4, 32, 300, 8, dict(eos=3, alpha=0.6)),                  # P = 256, the largest compacted pool
 ]
 
 
