@@ -61,31 +61,42 @@ __device__ __forceinline__ float sigmoid_exact(float x) {
 
 constexpr float kNegGuard = -1.0e30f;
 
-__device__ float sum_sigmoid_offset(const float* s, int n, float ref, float offset, float temperature) {
-    float sum = 0.0f;
-    for (int i = 0; i < n; ++i)
-        if (s[i] > kNegGuard) sum = __fadd_rn(sum, sigmoid_exact(__fdiv_rn(__fsub_rn(__fsub_rn(s[i], ref), offset), temperature)));
-    return sum;
+// The weight of score x at offset theta: sigmoid((x - ref - theta) / temperature), 0 for
+// empty slots.
+__device__ __forceinline__ float pool_weight(float x, float ref, float offset, float temperature) {
+    return x > kNegGuard ? sigmoid_exact(__fdiv_rn(__fsub_rn(__fsub_rn(x, ref), offset), temperature)) : 0.0f;
 }
 
 // Relaxed top-k membership: sigmoid((score - theta) / temperature) with theta bisected so
 // that the weights sum to target_k (src/kernels_scalar.cpp:304-366, operation for operation).
-__device__ void soft_topk_inclusion(const float* s, float* out, int n, int target_k, float temperature, float tolerance,
-                                    int max_iters) {
+// One warp: the lanes evaluate the sigmoids (into w[], P floats of shared memory), lane 0 adds
+// them in index order (the reference's sequential sum; a skipped empty slot adds nothing,
+// and adding +0 to a sum of non-negative terms leaves it unchanged), every lane follows the
+// same bisection from the broadcast sum.
+__device__ void soft_topk_inclusion_warp(const float* s, float* w, float* out, int n, int target_k, float temperature,
+                                         float tolerance, int max_iters) {
+    const int lane = threadIdx.x & 31;
     int active = 0;
     float min_s = f_inf(), max_s = f_ninf();
-    for (int i = 0; i < n; ++i) {
-        out[i] = 0.0f;
+    for (int i = lane; i < n; i += 32) {
         if (s[i] > kNegGuard) {
             ++active;
             min_s = fminf(min_s, s[i]);
             max_s = fmaxf(max_s, s[i]);
         }
     }
-    if (active == 0 || target_k <= 0) return;
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) {
+        active += __shfl_xor_sync(0xffffffffu, active, o);
+        min_s = fminf(min_s, __shfl_xor_sync(0xffffffffu, min_s, o));
+        max_s = fmaxf(max_s, __shfl_xor_sync(0xffffffffu, max_s, o));
+    }
+    if (active == 0 || target_k <= 0) {
+        for (int i = lane; i < n; i += 32) out[i] = 0.0f;
+        return;
+    }
     if (target_k >= active) {
-        for (int i = 0; i < n; ++i)
-            if (s[i] > kNegGuard) out[i] = 1.0f;
+        for (int i = lane; i < n; i += 32) out[i] = s[i] > kNegGuard ? 1.0f : 0.0f;
         return;
     }
     const float ref = max_s;
@@ -95,7 +106,14 @@ __device__ void soft_topk_inclusion(const float* s, float* out, int n, int targe
     constexpr float kFourEps = 4.0f * 1.1920928955078125e-07f;  // 4 x FLT_EPSILON, exact
     for (int it = 0; it < max_iters; ++it) {
         const float mid = __fmul_rn(0.5f, __fadd_rn(lo, hi));
-        const float err = __fsub_rn(sum_sigmoid_offset(s, n, ref, mid, temperature), static_cast<float>(target_k));
+        for (int i = lane; i < n; i += 32) w[i] = pool_weight(s[i], ref, mid, temperature);
+        __syncwarp();
+        float sum = 0.0f;
+        if (lane == 0)
+            for (int i = 0; i < n; ++i) sum = __fadd_rn(sum, w[i]);
+        sum = __shfl_sync(0xffffffffu, sum, 0);
+        __syncwarp();
+        const float err = __fsub_rn(sum, static_cast<float>(target_k));
         const float ulps = __fmul_rn(kFourEps, fabsf(mid));
         if (fabsf(err) <= tolerance || __fsub_rn(hi, lo) <= fmaxf(bracket, ulps)) {
             lo = hi = mid;
@@ -105,9 +123,10 @@ __device__ void soft_topk_inclusion(const float* s, float* out, int n, int targe
         else hi = mid;
     }
     const float offset = __fmul_rn(0.5f, __fadd_rn(lo, hi));
-    for (int i = 0; i < n; ++i)
-        out[i] = s[i] > kNegGuard ? sigmoid_exact(__fdiv_rn(__fsub_rn(__fsub_rn(s[i], ref), offset), temperature)) : 0.0f;
+    for (int i = lane; i < n; i += 32) out[i] = pool_weight(s[i], ref, offset, temperature);
 }
+
+constexpr int kPoolBuf = 2048;  // compacted candidates at or above the thread-maximum bound
 
 template <int DT, bool LOGITS>
 __global__ void __launch_bounds__(kThreads) pool_kernel(const __grid_constant__ PoolParams q) {
@@ -121,8 +140,13 @@ __global__ void __launch_bounds__(kThreads) pool_kernel(const __grid_constant__ 
     const DecodeParams& p = q.d;
     const int P = q.P, K = p.K, V = p.V;
     uint64_t* keys = reinterpret_cast<uint64_t*>(dyn);        // [P] scanned candidates' keys
-    PoolCand* cand = reinterpret_cast<PoolCand*>(keys + P);    // [P + K] scanned then carried
+    uint64_t* buf = keys + P;                                  // [kPoolBuf] compacted candidates
+    PoolCand* cand = reinterpret_cast<PoolCand*>(buf + kPoolBuf);  // [P + K] scanned then carried
     float* pscore = reinterpret_cast<float*>(cand + P + K);    // [P] the pool's scores, pool order
+    float* wtmp = pscore + P;                                  // [P] bisection scratch
+    __shared__ uint64_t tmax_s[kThreads];
+    __shared__ uint64_t bound_s;
+    __shared__ int n_buf;
     const int b = blockIdx.x / p.T, t = blockIdx.x - (blockIdx.x / p.T) * p.T;
     const int tid = threadIdx.x;
     const Meta m = load_meta(p, b);
@@ -183,7 +207,64 @@ __global__ void __launch_bounds__(kThreads) pool_kernel(const __grid_constant__ 
         if (!(lp < f_inf()) || lp == f_ninf()) return 0;
         return make_key(__fadd_rn(s_raw[k], lp), static_cast<uint32_t>(i));
     };
-    const int n_scanned = block_select(sh, gen, K * V, P, [&](int pos, uint64_t key) { keys[pos] = key; });
+    // f(key) for every candidate key the calling thread owns: the rows read at this step,
+    // streamed in 16-byte chunks (the same candidates and keys as gen, in another order).
+    auto scan_keys = [&](auto&& f) {
+        for (int k = 0; k < K; ++k) {
+            if (s_kind[k] != 1) continue;
+            const int64_t row = (static_cast<int64_t>(b) * p.T + t) * K + k;
+            const char* src = in + row * static_cast<int64_t>(V) * Elem<DT>::kBytes;
+            const RowSplit rs = RowSplit::of<Elem<DT>::kBytes>(src, V);
+            const float lse = LOGITS ? q.row_lse[row] : 0.0f;
+            const float base = s_raw[k];
+            const bool eos_masked = mask_eos && s_len[k] + 1 < m.min_length;
+            const uint32_t first = static_cast<uint32_t>(k) * static_cast<uint32_t>(V);
+            for_chunks<DT>(src, rs, false, [&](float x, int v) {
+                if (p.banned && p.banned[v]) return;
+                if (eos_masked && v == m.eos) return;
+                const float lp = LOGITS ? __fsub_rn(x, lse) : x;
+                if (!(lp < f_inf()) || lp == f_ninf()) return;
+                f(make_key(__fadd_rn(base, lp), first + static_cast<uint32_t>(v)));
+            });
+        }
+    };
+    // The P best keys lie at or above the P-th largest thread maximum (P threads each own a
+    // key that reaches it); when P <= 256 they are compacted first, and the select runs over
+    // the compacted keys (the whole candidate set when too many reach the bound).
+    const int n_all = K * V;
+    auto put = [&](int pos, uint64_t key) { keys[pos] = key; };
+    int n_scanned;
+    bool compacted = false;
+    if (P <= kThreads) {
+        uint64_t tmax = 0;
+        scan_keys([&](uint64_t key) { tmax = key > tmax ? key : tmax; });
+        tmax_s[tid] = tmax;
+        if (tid == 0) {
+            bound_s = 0;
+            n_buf = 0;
+        }
+        block_sync();
+        int above = 0;  // keys are unique, so exactly one nonzero thread maximum has rank P - 1
+        for (int j = 0; j < kThreads; ++j) above += tmax_s[j] > tmax ? 1 : 0;
+        if (tmax != 0 && above == P - 1) bound_s = tmax;
+        block_sync();
+        const uint64_t bound = bound_s;
+        if (bound != 0) {
+            scan_keys([&](uint64_t key) {
+                if (key >= bound) {
+                    const int pos = atomicAdd(&n_buf, 1);
+                    if (pos < kPoolBuf) buf[pos] = key;
+                }
+            });
+            block_sync();
+            const int nb = n_buf;
+            if (nb <= kPoolBuf) {
+                n_scanned = block_select(sh, [&](int i) { return buf[i]; }, nb, P, put);
+                compacted = true;
+            }
+        }
+    }
+    if (!compacted) n_scanned = block_select(sh, gen, n_all, P, put);
     // Full candidates: the scanned ones, then the carried-forward finished beams.
     for (int i = tid; i < n_scanned; i += kThreads) {
         const uint64_t key = keys[i];
@@ -216,14 +297,14 @@ __global__ void __launch_bounds__(kThreads) pool_kernel(const __grid_constant__ 
     }
     if (q.relaxed) {
         block_sync();
-        if (tid == 0) soft_topk_inclusion(pscore, q.relaxed + obase, P, K, q.temperature, q.tolerance, q.max_iters);
+        if (tid < 32) soft_topk_inclusion_warp(pscore, wtmp, q.relaxed + obase, P, K, q.temperature, q.tolerance, q.max_iters);
     }
 }
 
 template <int DT, bool LOGITS>
 cudaError_t launch_pool_as(const PoolParams& q, cudaStream_t stream) {
-    const size_t dyn = static_cast<size_t>(q.P) * 8 + static_cast<size_t>(q.P + q.d.K) * sizeof(PoolCand) +
-                       static_cast<size_t>(q.P) * 4;
+    const size_t dyn = static_cast<size_t>(q.P) * 8 + static_cast<size_t>(kPoolBuf) * 8 +
+                       static_cast<size_t>(q.P + q.d.K) * sizeof(PoolCand) + static_cast<size_t>(q.P) * 8;
     auto kernel = pool_kernel<DT, LOGITS>;
     cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(dyn));
     if (e != cudaSuccess) return e;
