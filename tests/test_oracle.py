@@ -195,3 +195,25 @@ def test_path_gradient_scatters_to_dense():
                 if p >= 0 and trace["from_logprob"][b, t, k]:
                     scattered[b, t, p, tok] += draws[b, t, k]
     assert same_bits(scattered, dense)
+
+
+@needs_ref
+@pytest.mark.parametrize("seed", range(4))
+def test_reference_pool_apis_agree(seed):
+    """The two reference checkers of the relaxed pool (the batch API's pool outputs and the
+    single-example API's pool accessors) give the same pool, whose first K entries per step
+    are the step's selected beams; the relaxed weights of a step sum to K within tolerance."""
+    K, m, temp, tol = 4, 3, 0.5, 1e-4
+    pb = make_problem(2, 6, K, 80, seed=300 + seed, eos=2, alpha=0.6, min_length=seed % 3)
+    with oracle.RefDecoder(pb, pool_multiplier=m) as ref:
+        out = ref.decode()
+    assert (out["pool_parents"][:, :, :K] == out["parents"]).all()
+    P = K * m
+    for b in range(2):
+        one = oracle.ref_relaxed(pb.x[b], K, pb.eos, pb.alpha, pb.min_length, m, temp, tol, 60,
+                                 np.zeros((6, P), np.float32), np.zeros(K, np.float32))
+        for k in ("pool_scores", "pool_raw_scores", "pool_tokens", "pool_parents", "pool_lengths"):
+            assert one[k].tobytes() == out[k][b].tobytes(), k
+        live = (one["pool_parents"] >= 0).sum(1) > K
+        sums = one["relaxed_weights"].sum(1)
+        assert np.all(np.abs(sums[live] - K) < 1e-2)
