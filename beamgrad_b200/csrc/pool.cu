@@ -128,6 +128,79 @@ __device__ void soft_topk_inclusion_warp(const float* s, float* w, float* out, i
 
 constexpr int kPoolBuf = 2048;  // compacted candidates at or above the thread-maximum bound
 
+// The largest entry of a row among those the calling thread owns (for_chunks' assignment),
+// NaN ignored; -inf when there is none. Four 16-byte loads in flight per thread.
+template <int DT>
+__device__ float thread_row_max(const char* row, const RowSplit& rs) {
+    using E = Elem<DT>;
+    const int tid = threadIdx.x;
+    const char* body = row + static_cast<size_t>(rs.head) * E::kBytes;
+    auto chunk_max = [](const uint4& a) -> float {
+        if constexpr (E::kBytes == 2) {
+            const uint32_t m2 = h2_max<DT>(h2_max<DT>(a.x, a.y), h2_max<DT>(a.z, a.w));
+            return fmaxf(h2_lo<DT>(m2), h2_hi<DT>(m2));
+        } else {
+            return fmaxf(fmaxf(__uint_as_float(a.x), __uint_as_float(a.y)), fmaxf(__uint_as_float(a.z), __uint_as_float(a.w)));
+        }
+    };
+    float top = f_ninf();
+    int c = tid;
+    for (; c + 3 * kThreads < rs.nvec; c += 4 * kThreads) {
+        uint4 a[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) a[u] = ld_stream_v4(body + static_cast<size_t>(c + u * kThreads) * 16);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) top = fmaxf(top, chunk_max(a[u]));
+    }
+    for (; c < rs.nvec; c += kThreads) top = fmaxf(top, chunk_max(ld_stream_v4(body + static_cast<size_t>(c) * 16)));
+    if (tid < rs.n_ends()) top = fmaxf(top, load_elem<DT>(row, rs.end_entry(tid)));
+    return top;
+}
+
+// hit(x, v) for every entry the calling thread owns with x >= xf; a 16-byte chunk is
+// unpacked only when its largest entry reaches xf. Four loads in flight per thread.
+template <int DT, class Hit>
+__device__ void scan_row_above(const char* row, const RowSplit& rs, float xf, Hit&& hit) {
+    using E = Elem<DT>;
+    constexpr int PER = 16 / E::kBytes;
+    const int tid = threadIdx.x;
+    const char* body = row + static_cast<size_t>(rs.head) * E::kBytes;
+    constexpr uint32_t kNegFill = E::kBytes == 2 ? h2_ninf<DT>() : 0xff800000u;
+    for (int c0 = tid; c0 < rs.nvec; c0 += 4 * kThreads) {
+        uint4 a[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int c = c0 + u * kThreads;
+            a[u] = c < rs.nvec ? ld_stream_v4(body + static_cast<size_t>(c) * 16)
+                               : make_uint4(kNegFill, kNegFill, kNegFill, kNegFill);
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            float top;
+            if constexpr (E::kBytes == 2) {
+                const uint32_t m2 = h2_max<DT>(h2_max<DT>(a[u].x, a[u].y), h2_max<DT>(a[u].z, a[u].w));
+                top = fmaxf(h2_lo<DT>(m2), h2_hi<DT>(m2));
+            } else {
+                top = fmaxf(fmaxf(__uint_as_float(a[u].x), __uint_as_float(a[u].y)),
+                            fmaxf(__uint_as_float(a[u].z), __uint_as_float(a[u].w)));
+            }
+            if (top >= xf) {
+                float x[PER];
+                unpack16<DT>(a[u], x);
+                const int v0 = rs.head + (c0 + u * kThreads) * PER;
+#pragma unroll
+                for (int j = 0; j < PER; ++j)
+                    if (x[j] >= xf) hit(x[j], v0 + j);
+            }
+        }
+    }
+    if (tid < rs.n_ends()) {
+        const int v = rs.end_entry(tid);
+        const float x = load_elem<DT>(row, v);
+        if (x >= xf) hit(x, v);
+    }
+}
+
 template <int DT, bool LOGITS>
 __global__ void __launch_bounds__(kThreads) pool_kernel(const __grid_constant__ PoolParams q) {
     __shared__ RowShared sh;
@@ -236,26 +309,72 @@ __global__ void __launch_bounds__(kThreads) pool_kernel(const __grid_constant__ 
     int n_scanned;
     bool compacted = false;
     if (P <= kThreads) {
-        uint64_t tmax = 0;
-        scan_keys([&](uint64_t key) { tmax = key > tmax ? key : tmax; });
-        tmax_s[tid] = tmax;
+        // Pass 1: a lower bound on each thread's best key. Without banned tokens it comes from
+        // the thread's largest entry of each row read (packed maxima; no bound from a row
+        // whose masked EOS the thread owns): the key of that entry's raw score with the
+        // lowest index part. With banned tokens, the thread's best key itself.
+        uint64_t lb = 0;
+        if (!p.banned) {
+            for (int k = 0; k < K; ++k) {
+                if (s_kind[k] != 1) continue;
+                const int64_t row = (static_cast<int64_t>(b) * p.T + t) * K + k;
+                const char* src = in + row * static_cast<int64_t>(V) * Elem<DT>::kBytes;
+                const RowSplit rs = RowSplit::of<Elem<DT>::kBytes>(src, V);
+                if (mask_eos && s_len[k] + 1 < m.min_length && rs.owns(m.eos)) continue;
+                const float top = thread_row_max<DT>(src, rs);
+                if (!(top < f_inf()) || top == f_ninf()) continue;
+                const float lp = LOGITS ? __fsub_rn(top, q.row_lse[row]) : top;
+                if (!(lp < f_inf()) || lp == f_ninf()) continue;
+                const uint64_t key = make_key(__fadd_rn(s_raw[k], lp), 0xffffffffu);
+                lb = key > lb ? key : lb;
+            }
+        } else {
+            scan_keys([&](uint64_t key) { lb = key > lb ? key : lb; });
+        }
+        tmax_s[tid] = lb;
         if (tid == 0) {
             bound_s = 0;
             n_buf = 0;
         }
         block_sync();
-        int above = 0;  // keys are unique, so exactly one nonzero thread maximum has rank P - 1
-        for (int j = 0; j < kThreads; ++j) above += tmax_s[j] > tmax ? 1 : 0;
-        if (tmax != 0 && above == P - 1) bound_s = tmax;
+        // The P-th largest bound (ties allowed): P threads each own a key at or above it.
+        int above = 0, atleast = 0;
+        for (int j = 0; j < kThreads; ++j) {
+            const uint64_t o = tmax_s[j];
+            above += o > lb ? 1 : 0;
+            atleast += o >= lb ? 1 : 0;
+        }
+        if (lb != 0 && above < P && atleast >= P) bound_s = lb;
         block_sync();
         const uint64_t bound = bound_s;
         if (bound != 0) {
-            scan_keys([&](uint64_t key) {
-                if (key >= bound) {
-                    const int pos = atomicAdd(&n_buf, 1);
-                    if (pos < kPoolBuf) buf[pos] = key;
-                }
-            });
+            // Pass 2: the keys at or above the bound, i.e. raw >= rb; x >= xf is necessary for
+            // that (raw is non-decreasing in x, and xf is the smallest x whose raw reaches rb).
+            const float rb = key_raw(bound);
+            for (int k = 0; k < K; ++k) {
+                if (s_kind[k] != 1) continue;
+                const int64_t row = (static_cast<int64_t>(b) * p.T + t) * K + k;
+                const char* src = in + row * static_cast<int64_t>(V) * Elem<DT>::kBytes;
+                const RowSplit rs = RowSplit::of<Elem<DT>::kBytes>(src, V);
+                const float lse = LOGITS ? q.row_lse[row] : 0.0f;
+                const float base = s_raw[k];
+                const bool eos_masked = mask_eos && s_len[k] + 1 < m.min_length;
+                const uint32_t first = static_cast<uint32_t>(k) * static_cast<uint32_t>(V);
+                auto raw_of = [&](float x) { return __fadd_rn(base, LOGITS ? __fsub_rn(x, lse) : x); };
+                const float est = LOGITS ? __fadd_rn(__fsub_rn(rb, base), lse) : __fsub_rn(rb, base);
+                const float xf = smallest_x_reaching(est, rb, raw_of);
+                scan_row_above<DT>(src, rs, xf, [&](float x, int v) {
+                    if (p.banned && p.banned[v]) return;
+                    if (eos_masked && v == m.eos) return;
+                    const float lp = LOGITS ? __fsub_rn(x, lse) : x;
+                    if (!(lp < f_inf()) || lp == f_ninf()) return;
+                    const uint64_t key = make_key(__fadd_rn(base, lp), first + static_cast<uint32_t>(v));
+                    if (key >= bound) {
+                        const int pos = atomicAdd(&n_buf, 1);
+                        if (pos < kPoolBuf) buf[pos] = key;
+                    }
+                });
+            }
             block_sync();
             const int nb = n_buf;
             if (nb <= kPoolBuf) {
