@@ -1426,6 +1426,154 @@ __device__ __forceinline__ uint64_t lane_pair_sums(const Pack2& q, const char* r
     return acc;
 }
 
+// One entry of a row in shared memory, widened to float.
+template <int DT>
+__device__ __forceinline__ float lds_elem(uint32_t a) {
+    if constexpr (Elem<DT>::kBytes == 4) {
+        float x;
+        asm("ld.shared.f32 %0, [%1];" : "=f"(x) : "r"(a));
+        return x;
+    } else {
+        uint16_t h;
+        asm("ld.shared.u16 %0, [%1];" : "=h"(h) : "r"(a));
+        return Elem<DT>::to_f32(h);
+    }
+}
+
+// Logsumexp lane j of a staged row on one thread (all eight warps take part, one lane
+// each): exp(x - max) over v = j, j + 256, ... in increasing v, the entries of two
+// consecutive blocks evaluated as one packed pair and added to the lane sum in order.
+// MASKED: entries with x - max below -87 contribute +0.
+// The row is staged at shared address `row`. A function of its own: the chained kernel
+// holds much state across a row, and inlined into it the packed exp's operand pairs were
+// re-materialised on every entry (measured: about 28 K more FMA-pipe instructions per
+// 32000-entry row); called, the loop gets the whole register budget and the caller's
+// state is saved once per row.
+template <int DT, bool MASKED, int UR = 2>
+__device__ __noinline__ float lane_sum_staged(uint32_t row, int V, float mx, int j, uint64_t one2, uint64_t nzero2) {
+    constexpr uint32_t EB = Elem<DT>::kBytes;
+    constexpr uint32_t kStride = kLanes * EB;  // bytes between consecutive entries of a lane
+    const Pack2 q{one2, nzero2};
+    const int nfull = V / kLanes;
+    const int nb = nfull + (j < V - nfull * kLanes ? 1 : 0);
+    const uint64_t mx2 = f2_splat(mx);
+    auto ex2 = [&](float a, float b, float& ea, float& eb) {
+        const uint64_t d = f2_sub(q, f2_pack(a, b), mx2);
+        exp_nonpositive_fast2(q, d, ea, eb);
+        if constexpr (MASKED) {
+            float da, db;
+            f2_unpack(d, da, db);
+            uint32_t ka, kb;
+            asm("set.ge.u32.f32 %0, %1, %2;" : "=r"(ka) : "f"(da), "f"(cephes::kMin));
+            asm("set.ge.u32.f32 %0, %1, %2;" : "=r"(kb) : "f"(db), "f"(cephes::kMin));
+            ea = __uint_as_float(__float_as_uint(ea) & ka);
+            eb = __uint_as_float(__float_as_uint(eb) & kb);
+        }
+    };
+    uint32_t a = row + static_cast<uint32_t>(j) * EB;
+    float acc = 0.0f;
+    int i = 0;
+    for (; i + 2 * UR <= nb; i += 2 * UR, a += 2 * UR * kStride) {
+        float ea[UR], eb[UR];
+#pragma unroll
+        for (int u = 0; u < UR; ++u)
+            ex2(lds_elem<DT>(a + 2 * u * kStride), lds_elem<DT>(a + (2 * u + 1) * kStride), ea[u], eb[u]);
+#pragma unroll
+        for (int u = 0; u < UR; ++u) {
+            acc = __fadd_rn(acc, ea[u]);
+            acc = __fadd_rn(acc, eb[u]);
+        }
+    }
+    for (; i + 2 <= nb; i += 2, a += 2 * kStride) {
+        float ea, eb;
+        ex2(lds_elem<DT>(a), lds_elem<DT>(a + kStride), ea, eb);
+        acc = __fadd_rn(acc, ea);
+        acc = __fadd_rn(acc, eb);
+    }
+    if (i < nb) acc = __fadd_rn(acc, exp_nonpositive_masked(__fsub_rn(lds_elem<DT>(a), mx)));
+    return acc;
+}
+
+// Where the chained decode's from-logits record goes and which entries it may hold.
+struct RecordOut {
+    uint64_t* out;    // the row's LIST record keys
+    int list;         // LIST
+    bool mask_eos;    // EOS tokens excluded (the parent is shorter than min_length - 1)
+    bool exclusions;  // banned tokens excluded
+};
+
+constexpr int kCandCap = kWarps * 32;  // record candidates collected in RowShared::wkeys
+
+// The record candidates of a staged row: every eligible entry at or above the filter
+// bound xb, as keys in sh.wkeys[0, min(count, kCandCap)) with their number in sh.count.
+// Only a thread whose own maximum (pass 1's chunk assignment: chunk c on thread c mod 256,
+// ragged end i on thread i) reaches xb can own such an entry. Each warp takes its own
+// such threads one at a time and looks at a thread's chunks with all 32 lanes at once
+// (a lane per chunk), so no warp diverges into a long per-thread loop before pass 2.
+template <int DT>
+__device__ __forceinline__ void collect_candidates(const DecodeParams& p, RowShared& sh, const char* row,
+                                                   const RowSplit& rs, float xb, bool mine, const Meta& m,
+                                                   const RecordOut& ro) {
+    using E = Elem<DT>;
+    constexpr int PER = 16 / E::kBytes;
+    const int lane = threadIdx.x & 31;
+    const int wbase = threadIdx.x & ~31;
+    auto eligible = [&](float x, int v) {
+        return x >= xb && !(ro.exclusions && p.banned[v]) && !(ro.mask_eos && is_eos(p, m, v));
+    };
+    const char* body = row + static_cast<size_t>(rs.head) * E::kBytes;
+    unsigned owners = __ballot_sync(0xffffffffu, mine);
+    while (owners) {
+        const int q = wbase + __ffs(owners) - 1;  // the owning thread
+        owners &= owners - 1;
+        for (int i0 = 0; q + i0 * kThreads < rs.nvec; i0 += 32) {
+            const int c = q + (i0 + lane) * kThreads;
+            float x[PER];
+            unsigned mask = 0;
+            if (c < rs.nvec) {
+                unpack16<DT>(*reinterpret_cast<const uint4*>(body + static_cast<size_t>(c) * 16), x);
+                const int v0 = rs.head + c * PER;
+#pragma unroll
+                for (int jj = 0; jj < PER; ++jj) mask |= eligible(x[jj], v0 + jj) ? 1u << jj : 0u;
+            }
+            if (mask) {
+                int slot = atomicAdd(&sh.count, __popc(mask));
+                const int v0 = rs.head + c * PER;
+#pragma unroll
+                for (int jj = 0; jj < PER; ++jj) {
+                    if ((mask >> jj) & 1u) {
+                        if (slot < kCandCap) sh.wkeys[slot] = make_key(x[jj], static_cast<uint32_t>(v0 + jj));
+                        ++slot;
+                    }
+                }
+            }
+        }
+        if (lane == 0 && q < rs.n_ends()) {
+            const int v = rs.end_entry(q);
+            const float x = load_elem<DT>(row, v);
+            if (eligible(x, v)) {
+                const int slot = atomicAdd(&sh.count, 1);
+                if (slot < kCandCap) sh.wkeys[slot] = make_key(x, static_cast<uint32_t>(v));
+            }
+        }
+    }
+}
+
+// The record from the collected candidates by one warp: each key's rank is the number of
+// larger keys (keys are unique); ranks below LIST are written. The list count goes to
+// sh.nlist[4] (the first list warp's slot; the other list warps' slots are zero), as the
+// list warps' record scan would leave it.
+__device__ __forceinline__ void record_from_candidates(RowShared& sh, int n, const RecordOut& ro) {
+    const int lane = threadIdx.x & 31;
+    for (int i = lane; i < n; i += 32) {
+        const uint64_t key = sh.wkeys[i];
+        int rank = 0;
+        for (int k2 = 0; k2 < n; ++k2) rank += sh.wkeys[k2] > key ? 1 : 0;
+        if (rank < ro.list) ro.out[rank] = key;
+    }
+    if (lane < kWarps / 2) sh.nlist[kWarps / 2 + lane] = lane == 0 ? (n < ro.list ? n : ro.list) : 0;
+}
+
 // Row preparation, independent of the previous step's selection: stage the row in
 // shared memory (optional); pass 1: maximum, minimum, NaN/+inf flag and the per-thread
 // maxima behind the filter bound; from logits, pass 2: logsumexp on warps 0-3 (two
@@ -1433,10 +1581,16 @@ __device__ __forceinline__ uint64_t lane_pair_sums(const Pack2& q, const char* r
 // side(src, rs, xthr), e.g. the chained decode's record scan. RCAP: capacity of the
 // bound (R <= RCAP <= 32). want_bound: the candidates are not subject to exclusions
 // the per-thread maxima cannot see (banned tokens, constraints).
+//
+// ro (from logits, staged rows with a bound): the whole CTA runs pass 2 instead, one
+// logsumexp lane per thread, after the threads whose maximum reaches the bound have
+// collected the record candidates; warp 4 then ranks them into ro->out while warps 0-3
+// reduce the lanes, and side() runs only when the candidates overflow kCandCap or no
+// bound exists.
 template <int DT, bool LOGITS, int RCAP, class Side>
 __device__ __forceinline__ void prepare_row(const DecodeParams& p, RowShared& sh, char* srow, const char* grow,
                                             uint32_t& phase, bool use_smem, bool want_bound, int R, const Meta& m,
-                                            Prep& o, Side&& side) {
+                                            Prep& o, Side&& side, const RecordOut* ro = nullptr) {
     using E = Elem<DT>;
     constexpr int EB = E::kBytes;
     const int tid = threadIdx.x;
@@ -1480,6 +1634,7 @@ __device__ __forceinline__ void prepare_row(const DecodeParams& p, RowShared& sh
         const float sorted = warp_sort_desc(me);
         if (lane < R && lane < RCAP) sh.wtop[warp * RCAP + lane] = sorted;
     }
+    if (tid == 0) sh.count = 0;  // record candidates (from logits, all-warps pass 2)
     {
         const float wmx = warp_max_f32(bad ? f_ninf() : mxn);
         const float wmn = -warp_max_f32(-mn);
@@ -1516,6 +1671,51 @@ __device__ __forceinline__ void prepare_row(const DecodeParams& p, RowShared& sh
         if (make_bound && warp >= 4) bound_rank<RCAP>(sh, R, tid - kThreads / 2);
         block_sync();
         if (make_bound) o.xthr = sh.xbound;
+        return;
+    }
+    if (ro != nullptr && use_smem && make_bound && mx != f_ninf() && R <= kWarps * RCAP) {
+        // The filter bound: the smallest over the warps of each warp's ceil(R / 8)-th largest
+        // thread maximum, so at least R thread maxima (each an eligible entry) reach it. It
+        // is a lower bound on the row's R-th best eligible entry, looser than the R-th
+        // largest thread maximum but free of the rank search.
+        const int per_warp = (R + kWarps - 1) / kWarps;
+        float xb = sh.wtop[per_warp - 1];
+#pragma unroll
+        for (int w = 1; w < kWarps; ++w) xb = fminf(xb, sh.wtop[w * RCAP + per_warp - 1]);
+        const bool bounded = xb != f_ninf();
+        collect_candidates<DT>(p, sh, srow + soff, rs, xb, bounded && mxn >= xb, m, *ro);
+        const bool fast = __fsub_rn(mn, mx) >= cephes::kMin;  // every x - max >= -87
+        const uint32_t srow_a = smem_u32(srow + soff);
+        sh.lanes[tid] = fast ? lane_sum_staged<DT, false>(srow_a, V, mx, tid, p.one2, p.nzero2)
+                             : lane_sum_staged<DT, true>(srow_a, V, mx, tid, p.one2, p.nzero2);
+        block_sync();
+        if (warp < 4) {
+            // Pairwise tree lanes[i] += lanes[i + s], s = 128 ... 1 (src/kernels.hpp:197-202).
+#pragma unroll
+            for (int st = kLanes / 2; st >= 32; st >>= 1) {
+                if (tid < st) sh.lanes[tid] = __fadd_rn(sh.lanes[tid], sh.lanes[tid + st]);
+                half_sync(2);
+            }
+            if (warp == 0) {
+                float x = sh.lanes[tid];
+#pragma unroll
+                for (int st = 16; st >= 1; st >>= 1) {
+                    const float y = __shfl_down_sync(0xffffffffu, x, st);
+                    if (tid < st) x = __fadd_rn(x, y);
+                }
+                if (tid == 0) sh.row_lse = logsumexp_from(mx, x);
+            }
+        } else {
+            const int n = sh.count;
+            if (bounded && n <= kCandCap) {
+                if (warp == 4) record_from_candidates(sh, n, *ro);
+            } else {
+                side(src, rs, xb);
+            }
+        }
+        block_sync();
+        o.lse = sh.row_lse;
+        o.xthr = xb;
         return;
     }
     if (warp >= 4) {
@@ -2467,6 +2667,7 @@ __global__ void __launch_bounds__(kThreads, 3) decode_chain_kernel(const __grid_
             // without a bound.
             // With banned tokens the bound is ranked lower (LIST + LIST / 2 thread maxima), so
             // that a few banned entries among them still leave LIST eligible ones above it.
+            const RecordOut ro{p.rkeys + rowi * LIST, LIST, mask_eos, exclusions};
             prepare_row<DT, LOGITS, LIST>(p, sh, srow, grow, phase, p.staged != 0, true,
                                           exclusions ? LIST + LIST / 2 : LIST, m, o,
                                           [&](const char* src, const RowSplit& rs, float xthr) {
@@ -2478,7 +2679,8 @@ __global__ void __launch_bounds__(kThreads, 3) decode_chain_kernel(const __grid_
                                               if (lane == 0) sh.nlist[warp] = __popc(nz);
                                               half_sync(1);
                                               rank_merge<LIST>(sh.wkeys, kWarps / 2, lw, wt.wl, p.rkeys + rowi * LIST);
-                                          });
+                                          },
+                                          LOGITS ? &ro : nullptr);
             if (o.aborted) break;
             constexpr int kLists = LOGITS ? kWarps / 2 : kWarps;
             if constexpr (!LOGITS) {

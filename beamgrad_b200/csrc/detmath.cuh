@@ -209,15 +209,24 @@ __device__ __forceinline__ uint64_t f2_add(const Pack2& q, uint64_t a, uint64_t 
 // round(a - b) = round(a + (-b)); negation flips the sign bits exactly.
 __device__ __forceinline__ uint64_t f2_sub(const Pack2& q, uint64_t a, uint64_t b) { return f2_fma(q.one, a, b ^ kF2Sign); }
 
-// exp_nonpositive_fast on both halves of d (each in [-87, 0]), step for step:
-// the floor is the scalar round-toward-minus-infinity add, the rest packed.
+// fma(a, b, c) on both halves rounded toward minus infinity.
+__device__ __forceinline__ uint64_t f2_fma_rm(uint64_t a, uint64_t b, uint64_t c) {
+    uint64_t r;
+    asm("fma.rm.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+    return r;
+}
+
+// exp_nonpositive_fast on both halves of d (each in [-87, 0]), step for step, every
+// step packed: the floor's add rounded toward minus infinity is fma.rm(1, y, M), which
+// rounds y + M once in that direction exactly as the scalar add.rm does.
 __device__ __forceinline__ void exp_nonpositive_fast2(const Pack2& q, uint64_t d, float& e_lo, float& e_hi) {
     using namespace cephes;
     constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23
-    float y_lo, y_hi;
-    f2_unpack(f2_add(q, f2_mul(q, d, f2_splat(kLog2e)), f2_splat(0.5f)), y_lo, y_hi);
-    const float z_lo = __fadd_rd(y_lo, kMagic), z_hi = __fadd_rd(y_hi, kMagic);
-    const uint64_t k = f2_sub(q, f2_pack(z_lo, z_hi), f2_splat(kMagic));
+    const uint64_t y = f2_add(q, f2_mul(q, d, f2_splat(kLog2e)), f2_splat(0.5f));
+    const uint64_t z2 = f2_fma_rm(q.one, y, f2_splat(kMagic));
+    float z_lo, z_hi;
+    f2_unpack(z2, z_lo, z_hi);
+    const uint64_t k = f2_sub(q, z2, f2_splat(kMagic));
     // d - round(k ln2hi) is d - k ln2hi rounded once, a single fma: k ln2hi is exact
     // (k an integer in [-126, 0], ln2hi = 355/512 needs 9 significant bits).
     const uint64_t r1 = f2_fma(k, f2_splat(-kLn2Hi), d);
