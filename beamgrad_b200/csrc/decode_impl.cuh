@@ -1674,14 +1674,22 @@ __device__ __forceinline__ void prepare_row(const DecodeParams& p, RowShared& sh
         return;
     }
     if (ro != nullptr && use_smem && make_bound && mx != f_ninf() && R <= kWarps * RCAP) {
-        // The filter bound: the smallest over the warps of each warp's ceil(R / 8)-th largest
-        // thread maximum, so at least R thread maxima (each an eligible entry) reach it. It
-        // is a lower bound on the row's R-th best eligible entry, looser than the R-th
-        // largest thread maximum but free of the rank search.
-        const int per_warp = (R + kWarps - 1) / kWarps;
-        float xb = sh.wtop[per_warp - 1];
+        // The filter bound, computed by every warp on its own (no barrier): with R <= 32 and
+        // at least 4 sorted maxima per warp, the R-th largest of the union of the warps'
+        // top-4 thread maxima (32 values, one per lane); otherwise the smallest over the
+        // warps of each warp's ceil(R / 8)-th largest. Either way at least R thread maxima
+        // (each an eligible entry) reach it, so it bounds the row's R-th best eligible entry
+        // from below; the first equals the R-th largest thread maximum unless a warp holds
+        // more than four of the top R.
+        float xb;
+        if (R <= 32 && RCAP >= 4 && R >= 4) {
+            xb = warp_rth_largest(sh.wtop[(lane >> 2) * RCAP + (lane & 3)], R);
+        } else {
+            const int per_warp = (R + kWarps - 1) / kWarps;
+            xb = sh.wtop[per_warp - 1];
 #pragma unroll
-        for (int w = 1; w < kWarps; ++w) xb = fminf(xb, sh.wtop[w * RCAP + per_warp - 1]);
+            for (int w = 1; w < kWarps; ++w) xb = fminf(xb, sh.wtop[w * RCAP + per_warp - 1]);
+        }
         const bool bounded = xb != f_ninf();
         collect_candidates<DT>(p, sh, srow + soff, rs, xb, bounded && mxn >= xb, m, *ro);
         const bool fast = __fsub_rn(mn, mx) >= cephes::kMin;  // every x - max >= -87
