@@ -1440,44 +1440,43 @@ __device__ __forceinline__ float lds_elem(uint32_t a) {
     }
 }
 
-// Logsumexp lane j of a staged row on one thread (all eight warps take part, one lane
-// each): exp(x - max) over v = j, j + 256, ... in increasing v, the entries of two
-// consecutive blocks evaluated as one packed pair and added to the lane sum in order.
-// MASKED: entries with x - max below -87 contribute +0.
-// The row is staged at shared address `row`. A function of its own: the chained kernel
-// holds much state across a row, and inlined into it the packed exp's operand pairs were
-// re-materialised on every entry (measured: about 28 K more FMA-pipe instructions per
-// 32000-entry row); called, the loop gets the whole register budget and the caller's
-// state is saved once per row.
-template <int DT, bool MASKED, int UR = 2>
-__device__ __noinline__ float lane_sum_staged(uint32_t row, int V, float mx, int j, uint64_t one2, uint64_t nzero2) {
-    constexpr uint32_t EB = Elem<DT>::kBytes;
-    constexpr uint32_t kStride = kLanes * EB;  // bytes between consecutive entries of a lane
-    const Pack2 q{one2, nzero2};
+// One entry of a row in global memory (read-only for the kernel), widened to float.
+template <int DT>
+__device__ __forceinline__ float ldg_elem(const char* a) {
+    if constexpr (Elem<DT>::kBytes == 4) return __ldg(reinterpret_cast<const float*>(a));
+    else return Elem<DT>::to_f32(__ldg(reinterpret_cast<const unsigned short*>(a)));
+}
+
+// Logsumexp lane j of a row on one thread (all eight warps take part, one lane each):
+// exp(x - max) over v = j, j + 256, ... in increasing v, the entries of two consecutive
+// blocks evaluated as one packed pair and added to the lane sum in order. a: lane j's first
+// entry (a shared address or a global pointer), ld(a): one entry. MASKED: entries with
+// x - max below -87 contribute +0.
+template <int DT, bool MASKED, int UR, class Addr, class Load>
+__device__ __forceinline__ float lane_sum_loop(Addr a, int V, float mx, int j, const Pack2& q, Load&& ld) {
+    constexpr uint32_t kStride = kLanes * Elem<DT>::kBytes;  // bytes between consecutive entries of a lane
     const int nfull = V / kLanes;
     const int nb = nfull + (j < V - nfull * kLanes ? 1 : 0);
     const uint64_t mx2 = f2_splat(mx);
-    auto ex2 = [&](float a, float b, float& ea, float& eb) {
-        const uint64_t d = f2_sub(q, f2_pack(a, b), mx2);
-        exp_nonpositive_fast2(q, d, ea, eb);
+    auto ex2 = [&](float x0, float x1, float& e0, float& e1) {
+        const uint64_t d = f2_sub(q, f2_pack(x0, x1), mx2);
+        exp_nonpositive_fast2(q, d, e0, e1);
         if constexpr (MASKED) {
-            float da, db;
-            f2_unpack(d, da, db);
-            uint32_t ka, kb;
-            asm("set.ge.u32.f32 %0, %1, %2;" : "=r"(ka) : "f"(da), "f"(cephes::kMin));
-            asm("set.ge.u32.f32 %0, %1, %2;" : "=r"(kb) : "f"(db), "f"(cephes::kMin));
-            ea = __uint_as_float(__float_as_uint(ea) & ka);
-            eb = __uint_as_float(__float_as_uint(eb) & kb);
+            float d0, d1;
+            f2_unpack(d, d0, d1);
+            uint32_t k0, k1;
+            asm("set.ge.u32.f32 %0, %1, %2;" : "=r"(k0) : "f"(d0), "f"(cephes::kMin));
+            asm("set.ge.u32.f32 %0, %1, %2;" : "=r"(k1) : "f"(d1), "f"(cephes::kMin));
+            e0 = __uint_as_float(__float_as_uint(e0) & k0);
+            e1 = __uint_as_float(__float_as_uint(e1) & k1);
         }
     };
-    uint32_t a = row + static_cast<uint32_t>(j) * EB;
     float acc = 0.0f;
     int i = 0;
     for (; i + 2 * UR <= nb; i += 2 * UR, a += 2 * UR * kStride) {
         float ea[UR], eb[UR];
 #pragma unroll
-        for (int u = 0; u < UR; ++u)
-            ex2(lds_elem<DT>(a + 2 * u * kStride), lds_elem<DT>(a + (2 * u + 1) * kStride), ea[u], eb[u]);
+        for (int u = 0; u < UR; ++u) ex2(ld(a + 2 * u * kStride), ld(a + (2 * u + 1) * kStride), ea[u], eb[u]);
 #pragma unroll
         for (int u = 0; u < UR; ++u) {
             acc = __fadd_rn(acc, ea[u]);
@@ -1486,12 +1485,30 @@ __device__ __noinline__ float lane_sum_staged(uint32_t row, int V, float mx, int
     }
     for (; i + 2 <= nb; i += 2, a += 2 * kStride) {
         float ea, eb;
-        ex2(lds_elem<DT>(a), lds_elem<DT>(a + kStride), ea, eb);
+        ex2(ld(a), ld(a + kStride), ea, eb);
         acc = __fadd_rn(acc, ea);
         acc = __fadd_rn(acc, eb);
     }
-    if (i < nb) acc = __fadd_rn(acc, exp_nonpositive_masked(__fsub_rn(lds_elem<DT>(a), mx)));
+    if (i < nb) acc = __fadd_rn(acc, exp_nonpositive_masked(__fsub_rn(ld(a), mx)));
     return acc;
+}
+
+// lane_sum_loop over a row staged at shared address `row`, and over a row in global
+// memory. Functions of their own: the chained kernel holds much state across a row, and
+// inlined into it the packed exp's operand pairs were re-materialised on every entry
+// (measured: about 28 K more FMA-pipe instructions per 32000-entry row); called, the loop
+// gets the whole register budget and the caller's state is saved once per row.
+template <int DT, bool MASKED, int UR = 2>
+__device__ __noinline__ float lane_sum_staged(uint32_t row, int V, float mx, int j, uint64_t one2, uint64_t nzero2) {
+    const Pack2 q{one2, nzero2};
+    return lane_sum_loop<DT, MASKED, UR>(row + static_cast<uint32_t>(j) * Elem<DT>::kBytes, V, mx, j, q,
+                                         [](uint32_t a) { return lds_elem<DT>(a); });
+}
+template <int DT, bool MASKED, int UR = 2>
+__device__ __noinline__ float lane_sum_global(const char* row, int V, float mx, int j, uint64_t one2, uint64_t nzero2) {
+    const Pack2 q{one2, nzero2};
+    return lane_sum_loop<DT, MASKED, UR>(row + static_cast<size_t>(j) * Elem<DT>::kBytes, V, mx, j, q,
+                                         [](const char* a) { return ldg_elem<DT>(a); });
 }
 
 // Where the chained decode's from-logits record goes and which entries it may hold.
@@ -1582,7 +1599,7 @@ __device__ __forceinline__ void record_from_candidates(RowShared& sh, int n, con
 // bound (R <= RCAP <= 32). want_bound: the candidates are not subject to exclusions
 // the per-thread maxima cannot see (banned tokens, constraints).
 //
-// ro (from logits, staged rows with a bound): the whole CTA runs pass 2 instead, one
+// ro (from logits, rows with a bound, staged or not): the whole CTA runs pass 2 instead, one
 // logsumexp lane per thread, after the threads whose maximum reaches the bound have
 // collected the record candidates; warp 4 then ranks them into ro->out while warps 0-3
 // reduce the lanes, and side() runs only when the candidates overflow kCandCap or no
@@ -1673,7 +1690,7 @@ __device__ __forceinline__ void prepare_row(const DecodeParams& p, RowShared& sh
         if (make_bound) o.xthr = sh.xbound;
         return;
     }
-    if (ro != nullptr && use_smem && make_bound && mx != f_ninf() && R <= kWarps * RCAP) {
+    if (ro != nullptr && make_bound && mx != f_ninf() && R <= kWarps * RCAP) {
         // The filter bound, computed by every warp on its own (no barrier): with R <= 32 and
         // at least 4 sorted maxima per warp, the R-th largest of the union of the warps'
         // top-4 thread maxima (32 values, one per lane); otherwise the smallest over the
@@ -1691,11 +1708,18 @@ __device__ __forceinline__ void prepare_row(const DecodeParams& p, RowShared& sh
             for (int w = 1; w < kWarps; ++w) xb = fminf(xb, sh.wtop[w * RCAP + per_warp - 1]);
         }
         const bool bounded = xb != f_ninf();
-        collect_candidates<DT>(p, sh, srow + soff, rs, xb, bounded && mxn >= xb, m, *ro);
+        collect_candidates<DT>(p, sh, src, rs, xb, bounded && mxn >= xb, m, *ro);
         const bool fast = __fsub_rn(mn, mx) >= cephes::kMin;  // every x - max >= -87
-        const uint32_t srow_a = smem_u32(srow + soff);
-        sh.lanes[tid] = fast ? lane_sum_staged<DT, false>(srow_a, V, mx, tid, p.one2, p.nzero2)
-                             : lane_sum_staged<DT, true>(srow_a, V, mx, tid, p.one2, p.nzero2);
+        if (use_smem) {
+            const uint32_t srow_a = smem_u32(srow + soff);
+            sh.lanes[tid] = fast ? lane_sum_staged<DT, false>(srow_a, V, mx, tid, p.one2, p.nzero2)
+                                 : lane_sum_staged<DT, true>(srow_a, V, mx, tid, p.one2, p.nzero2);
+        } else {
+            // A row too large to stage: pass 2 reads it again from global memory, where
+            // pass 1 has just brought it into L2.
+            sh.lanes[tid] = fast ? lane_sum_global<DT, false>(src, V, mx, tid, p.one2, p.nzero2)
+                                 : lane_sum_global<DT, true>(src, V, mx, tid, p.one2, p.nzero2);
+        }
         block_sync();
         if (warp < 4) {
             // Pairwise tree lanes[i] += lanes[i + s], s = 128 ... 1 (src/kernels.hpp:197-202).
