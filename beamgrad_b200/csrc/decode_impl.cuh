@@ -1721,23 +1721,21 @@ __device__ __forceinline__ void prepare_row(const DecodeParams& p, RowShared& sh
                                  : lane_sum_global<DT, true>(src, V, mx, tid, p.one2, p.nzero2);
         }
         block_sync();
-        if (warp < 4) {
-            // Pairwise tree lanes[i] += lanes[i + s], s = 128 ... 1 (src/kernels.hpp:197-202).
+        if (warp == 0) {
+            // Pairwise tree lanes[i] += lanes[i + s], s = 128 ... 1 (src/kernels.hpp:197-202),
+            // by one warp: lane i forms the s = 128, 64, 32 levels of index i from lanes
+            // i, i + 32, ..., i + 224 in the tree's own order, then shuffles for s = 16 ... 1.
+            const float* l = sh.lanes;
+            const float a0 = __fadd_rn(l[tid], l[tid + 128]), a1 = __fadd_rn(l[tid + 32], l[tid + 160]);
+            const float a2 = __fadd_rn(l[tid + 64], l[tid + 192]), a3 = __fadd_rn(l[tid + 96], l[tid + 224]);
+            float x = __fadd_rn(__fadd_rn(a0, a2), __fadd_rn(a1, a3));
 #pragma unroll
-            for (int st = kLanes / 2; st >= 32; st >>= 1) {
-                if (tid < st) sh.lanes[tid] = __fadd_rn(sh.lanes[tid], sh.lanes[tid + st]);
-                half_sync(2);
+            for (int st = 16; st >= 1; st >>= 1) {
+                const float y = __shfl_down_sync(0xffffffffu, x, st);
+                if (tid < st) x = __fadd_rn(x, y);
             }
-            if (warp == 0) {
-                float x = sh.lanes[tid];
-#pragma unroll
-                for (int st = 16; st >= 1; st >>= 1) {
-                    const float y = __shfl_down_sync(0xffffffffu, x, st);
-                    if (tid < st) x = __fadd_rn(x, y);
-                }
-                if (tid == 0) sh.row_lse = logsumexp_from(mx, x);
-            }
-        } else {
+            if (tid == 0) sh.row_lse = logsumexp_from(mx, x);
+        } else if (warp >= 4) {
             const int n = sh.count;
             if (bounded && n <= kCandCap) {
                 if (warp == 4) record_from_candidates(sh, n, *ro);
@@ -2591,10 +2589,12 @@ __device__ __forceinline__ uint32_t arrive_acq_rel(uint32_t* counter) {
     return old;
 }
 
+// synced: the caller has just passed a barrier of the whole group after every write of its
+// row but the calling thread's own, so the first barrier here is skipped.
 template <int NT, class Select>
 __device__ __forceinline__ void chain_arrive_with(const DecodeParams& p, SelScratch& ss, int t, int b, int ltid,
-                                                  int bar, Select&& select) {
-    group_sync<NT>(bar);
+                                                  int bar, Select&& select, bool synced = false) {
+    if (!synced) group_sync<NT>(bar);
     if (ltid == 0) {
         const uint32_t target = static_cast<uint32_t>(p.K) + (t > 0 ? 1u : 0u);
         ss.next = arrive_acq_rel(p.count + static_cast<int64_t>(b) * p.T + t) == target - 1u ? t : -1;
@@ -2617,9 +2617,9 @@ __device__ __forceinline__ void chain_arrive_with(const DecodeParams& p, SelScra
 
 template <int DT, bool LOGITS, int KMAX, int LIST, int NT>
 __device__ __forceinline__ void chain_arrive(const DecodeParams& p, SelScratch& ss, int t, int b, const Meta& m,
-                                             int ltid, int bar) {
+                                             int ltid, int bar, bool synced = false) {
     chain_arrive_with<NT>(p, ss, t, b, ltid, bar,
-                          [&](int ct) { chain_select<DT, LOGITS, KMAX, LIST, NT>(p, ss, ct, b, m, ltid, bar); });
+                          [&](int ct) { chain_select<DT, LOGITS, KMAX, LIST, NT>(p, ss, ct, b, m, ltid, bar); }, synced);
 }
 
 template <int DT, bool LOGITS, int KMAX>
@@ -2769,7 +2769,10 @@ __global__ void __launch_bounds__(kThreads, 3) decode_chain_kernel(const __grid_
         }
 
         // Arrive: the K rows of (t, b), prepared or not, and for t > 0 the selection of t - 1.
-        chain_arrive<DT, LOGITS, KMAX, LIST, kThreads>(p, sh.sel, t, b, m, tid, 0);
+        // From logits every thread has passed a CTA barrier since its last write of this row
+        // (the end of prepare_row, or the ticket's), except thread 0's own record header above;
+        // log-probability rows merge their record after their last barrier.
+        chain_arrive<DT, LOGITS, KMAX, LIST, kThreads>(p, sh.sel, t, b, m, tid, 0, LOGITS);
     }
 }
 
