@@ -1847,6 +1847,13 @@ __device__ void select_fast_core(const DecodeParams& p, int t, int b, const Meta
     const int beam = m.beam;
 
     int filled = 0;
+    // Length penalties, computed before the top-k rounds so that their latency overlaps
+    // them: the reciprocal for a candidate extending a beam of length t (every scanned
+    // candidate of a chained decode step), and this slot's carried score.
+    const float inv_next = __fdiv_rn(1.0f, gnmt_penalty(t + 1, p.alpha));
+    const int l_carry = s_len > 1 ? s_len : 1;
+    const bool carry = active && m.eos >= 0 && lane < beam && s_end != 0 && f_finite(s_raw);
+    const float sc = carry ? __fdiv_rn(s_raw, gnmt_penalty(l_carry, p.alpha)) : 0.0f;
     // This lane's candidate (scanned: lanes [0, ns); carried: lanes [ns, ns + nc)).
     uint64_t my_key = 0;
     float c_score = 0.0f, c_raw = 0.0f;
@@ -1866,7 +1873,6 @@ __device__ void select_fast_core(const DecodeParams& p, int t, int b, const Meta
             if (lane == ns) my_key = w;
         }
         // Carried-forward candidates: finished, live beams (EOS handling on).
-        const bool carry = m.eos >= 0 && lane < beam && s_end != 0 && f_finite(s_raw);
         const unsigned cm = __ballot_sync(0xffffffffu, carry);
         const int nc = __popc(cm);
         // Scanned candidate of lane i < ns.
@@ -1879,15 +1885,14 @@ __device__ void select_fast_core(const DecodeParams& p, int t, int b, const Meta
                 c_token = static_cast<int>(index - static_cast<uint32_t>(par) * V);
                 c_len = plen + 1;
                 c_raw = key_raw(my_key);
-                c_score = __fmul_rn(c_raw, __fdiv_rn(1.0f, gnmt_penalty(c_len, p.alpha)));
+                c_score = __fmul_rn(c_raw, c_len == t + 1 ? inv_next : __fdiv_rn(1.0f, gnmt_penalty(c_len, p.alpha)));
                 c_from = 1;
             }
         }
         // Carried candidate j (the j-th carrying slot in slot order) moves to lane ns + j.
         {
             const int j = __popc(cm & ((1u << lane) - 1u));
-            const int l = s_len > 1 ? s_len : 1;
-            const float sc = carry ? __fdiv_rn(s_raw, gnmt_penalty(l, p.alpha)) : 0.0f;
+            const int l = l_carry;
             const int tok = (s_last >= 0 && s_last < p.V && is_eos(p, m, s_last)) ? s_last : m.eos;
             // Source lane of carried candidate (lane - ns): the (lane - ns)-th set bit of cm.
             int srcl = 0;
@@ -1911,10 +1916,16 @@ __device__ void select_fast_core(const DecodeParams& p, int t, int b, const Meta
                 c_from = 0;
             }
         }
-        // Positions by counting under the full order (src/common.hpp:269-276).
+        // Positions by counting under the full order (src/common.hpp:269-276). Without
+        // carried candidates, and with every scanned candidate of one length (one penalty, so
+        // the score never decreases as raw grows), the extraction order by key (raw, then
+        // parent and token) already is that order.
         const int total = ns + nc;
+        const int len0 = __shfl_sync(0xffffffffu, c_len, 0);
+        const bool one_len = __all_sync(0xffffffffu, lane >= ns || c_len == len0);
         pos = 0;
-        for (int o = 0; o < total; ++o) {
+        if (nc == 0 && one_len) pos = lane;
+        else for (int o = 0; o < total; ++o) {
             const float os = __shfl_sync(0xffffffffu, c_score, o);
             const float orr = __shfl_sync(0xffffffffu, c_raw, o);
             const int op = __shfl_sync(0xffffffffu, c_parent, o);
